@@ -1,0 +1,217 @@
+// Operator-level C ABI (include/uf_b200.h): the B200 replacements of the
+// reference's CUDA extension functions uf_conv / uf_conv_generic /
+// uf_conv_baseline / uf_add / uf_mul / uf_lut / uf_bytes / uf_wsilu4
+// (include/uf/cuda_ops.hpp:10-23).  Argument checks follow the reference's
+// TORCH_CHECKs in src/cuda/conv.cu:65-83 and src/cuda/elementwise.cu:49-98.
+#include "uf_b200.h"
+
+#include "capi_util.h"
+#include "conv_tc.h"
+#include "kernels.h"
+
+#include <climits>
+#include <cstdint>
+#include <string>
+
+using namespace ufb;
+
+namespace {
+
+bool check_conv(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
+                int bias_bits, int sh, int sw, int ph, int pw, int groups, int16_t* out, int& oh, int& ow) {
+    if (!x || !weight || !out) return fail(UFB_EINVAL, "convolution tensors must be non-null");
+    if (sh <= 0 || sw <= 0 || ph < 0 || pw < 0 || groups <= 0) return fail(UFB_EINVAL, "invalid convolution geometry");
+    if (ci <= 0 || co <= 0 || kh <= 0 || kw <= 0 || n <= 0 || h <= 0 || w <= 0)
+        return fail(UFB_EINVAL, "empty convolution");
+    if (ci % groups || co % groups) return fail(UFB_EINVAL, "invalid groups");
+    if (bias_bits != 16 && bias_bits != 32 && bias_bits != 0) return fail(UFB_EINVAL, "bias_bits must be 16 or 32");
+    const long long padded_h = static_cast<long long>(h) + 2ll * ph, padded_w = static_cast<long long>(w) + 2ll * pw;
+    if (padded_h < kh || padded_w < kw) return fail(UFB_EINVAL, "kernel exceeds input");
+    if (static_cast<long long>(ci / groups) * kh * kw >= (INT64_MAX / 1073741824LL) - 1)
+        return fail(UFB_ERANGE, "dot product overflow");
+    const long long ohl = (padded_h - kh) / sh + 1, owl = (padded_w - kw) / sw + 1;
+    const long long planes = static_cast<long long>(n) * co;
+    if (planes > INT32_MAX || ohl > INT32_MAX / planes || owl > INT32_MAX / (planes * ohl) ||
+        static_cast<long long>(n) * ci * h * w > INT32_MAX)
+        return fail(UFB_ERANGE, "convolution output exceeds indexing bounds");
+    oh = static_cast<int>(ohl);
+    ow = static_cast<int>(owl);
+    return true;
+}
+
+int conv_direct_path(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
+                     const void* bias, int bias_bits, int sh, int sw, int ph, int pw, int groups, int oh, int ow,
+                     int16_t* out, cudaStream_t s) {
+    return cuda_ok(conv_direct(out, x, weight, bias_bits ? bias : nullptr, bias_bits == 32, n, ci, co, h, w, oh, ow,
+                               kh, kw, sh, sw, ph, pw, groups, s),
+                   "direct convolution")
+               ? UFB_OK
+               : last_code();
+}
+
+int conv_tc_path(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
+                 const void* bias, int bias_bits, int ph, int pw, int oh, int ow, int16_t* out, cudaStream_t s) {
+    int device = 0;
+    if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return last_code();
+    const int cip = round_up(ci, 16), cop = round_up(co, 16);
+    TcWeights tw;
+    tw.co = co;
+    tw.ci = ci;
+    tw.kh = kh;
+    tw.kw = kw;
+    tw.cpad = round_up(ci, 128);
+    tw.kpad = kh * kw * tw.cpad;
+    StreamBuffer xs(static_cast<size_t>(n) * h * w * 2 * cip, s);
+    StreamBuffer wp(static_cast<size_t>(2) * co * tw.kpad, s);
+    StreamBuffer os(static_cast<size_t>(n) * oh * ow * 2 * cop, s);
+    if (!xs.ok() || !wp.ok() || !os.ok()) return err(UFB_ECUDA, "cudaMallocAsync failed for convolution scratch");
+    tw.planes = wp.get<uint8_t>();
+    std::string msg;
+    if (!tc_weight_map(tw, 128, &tw.map128, msg) || !tc_weight_map(tw, 64, &tw.map64, msg))
+        return err(UFB_ECUDA, msg);
+    const Act in = make_act(xs.get<uint8_t>(), n, h, w, ci, cip);
+    const Act ov = make_act(os.get<uint8_t>(), n, oh, ow, co, cop);
+    if (!cuda_ok(prep_weights(weight, co, ci, kh, kw, tw.cpad, tw.kpad, tw.planes, s), "weight preparation"))
+        return last_code();
+    if (!cuda_ok(nchw_to_split(x, n, ci, h, w, 1, in, s), "input layout")) return last_code();
+    Epilogue epi{};
+    epi.bias = bias_bits ? bias : nullptr;
+    epi.bias32 = bias_bits == 32;
+    if (conv_tc_run(tw, in, ov, epi, ph, pw, s, device_status(device), msg) != 0) return err(UFB_ECUDA, msg);
+    if (!cuda_ok(split_to_nchw(ov, 1, out, s), "output layout")) return last_code();
+    return UFB_OK;
+}
+
+int conv_dispatch(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
+                  const void* bias, int bias_bits, int sh, int sw, int ph, int pw, int groups, int16_t* out,
+                  void* stream, bool allow_tc, bool allow_direct) {
+    clear_error();
+    if (!bias) bias_bits = 0;
+    int oh = 0, ow = 0;
+    if (!check_conv(x, n, ci, h, w, weight, co, kh, kw, bias_bits, sh, sw, ph, pw, groups, out, oh, ow))
+        return last_code();
+    auto s = static_cast<cudaStream_t>(stream);
+    const bool tc_ok = allow_tc && groups == 1 && sh == 1 && sw == 1 && static_cast<long long>(ci) * kh * kw <= 32768;
+    if (tc_ok) return conv_tc_path(x, n, ci, h, w, weight, co, kh, kw, bias, bias_bits, ph, pw, oh, ow, out, s);
+    if (!allow_direct && !allow_tc) return err(UFB_EINVAL, "no convolution path");
+    return conv_direct_path(x, n, ci, h, w, weight, co, kh, kw, bias, bias_bits, sh, sw, ph, pw, groups, oh, ow, out,
+                            s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int ufb_version(void) { return 100; }
+
+const char* ufb_last_error(void) { return last_message(); }
+
+int ufb_device_status(int device) {
+    clear_error();
+    int* st = device_status(device);
+    if (!st) return last_code();
+    int prev = 0;
+    if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice") || !cuda_ok(cudaDeviceSynchronize(), "synchronize") ||
+        !cuda_ok(cudaMemcpy(&prev, st, sizeof(int), cudaMemcpyDeviceToHost), "status read") ||
+        !cuda_ok(cudaMemset(st, 0, sizeof(int)), "status clear"))
+        return last_code();
+    return prev;
+}
+
+int ufb_conv2d(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
+               const void* bias, int bias_bits, int sh, int sw, int ph, int pw, int groups, int16_t* out,
+               void* stream) {
+    return conv_dispatch(x, n, ci, h, w, weight, co, kh, kw, bias, bias_bits, sh, sw, ph, pw, groups, out, stream,
+                         true, true);
+}
+
+int ufb_conv2d_generic(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
+                       const void* bias, int bias_bits, int sh, int sw, int ph, int pw, int groups, int16_t* out,
+                       void* stream) {
+    return conv_dispatch(x, n, ci, h, w, weight, co, kh, kw, bias, bias_bits, sh, sw, ph, pw, groups, out, stream,
+                         false, true);
+}
+
+int ufb_conv2d_baseline(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh,
+                        int kw, const void* bias, int bias_bits, int sh, int sw, int ph, int pw, int groups,
+                        int16_t* out, void* stream) {
+    return conv_dispatch(x, n, ci, h, w, weight, co, kh, kw, bias, bias_bits, sh, sw, ph, pw, groups, out, stream,
+                         true, true);
+}
+
+int ufb_add(int count, const int16_t* const* values, int64_t numel, int16_t* out, void* stream) {
+    clear_error();
+    if (count < 2 || count > 4) return err(UFB_EINVAL, "add supports 2 to 4 tensors");
+    if (!values || !out || numel <= 0 || numel > INT32_MAX) return err(UFB_EINVAL, "unsupported tensor size");
+    for (int i = 0; i < count; ++i)
+        if (!values[i]) return err(UFB_EINVAL, "add operand is null");
+    return cuda_ok(ew_add(out, values[0], values[1], count > 2 ? values[2] : nullptr, count > 3 ? values[3] : nullptr,
+                          numel, static_cast<cudaStream_t>(stream)),
+                   "add")
+               ? UFB_OK
+               : last_code();
+}
+
+int ufb_mul(const int16_t* x, const int64_t* xs, const int16_t* scale, const int64_t* ss, int16_t* out,
+            void* stream) {
+    clear_error();
+    if (!x || !xs || !scale || !ss || !out) return err(UFB_EINVAL, "multiply requires matching CUDA 4D tensors");
+    long long xl[4], sl[4];
+    long long numel = 1, snumel = 1;
+    for (int d = 0; d < 4; ++d) {
+        xl[d] = xs[d];
+        sl[d] = ss[d];
+        if (sl[d] != 1 && sl[d] != xl[d]) return err(UFB_EINVAL, "invalid broadcast");
+        numel *= xl[d];
+        snumel *= sl[d];
+    }
+    if (numel <= 0 || numel > INT32_MAX || snumel <= 0) return err(UFB_EINVAL, "unsupported tensor size");
+    return cuda_ok(ew_mul(out, x, scale, xl, sl, static_cast<cudaStream_t>(stream)), "multiply") ? UFB_OK
+                                                                                                : last_code();
+}
+
+int ufb_lut(const int16_t* x, int64_t numel, const void* table, int table_bits, void* out, void* stream) {
+    clear_error();
+    if (!x || !table || !out || numel <= 0 || numel > INT32_MAX) return err(UFB_EINVAL, "unsupported tensor size");
+    auto s = static_cast<cudaStream_t>(stream);
+    if (table_bits == 16)
+        return cuda_ok(ew_lut16(static_cast<int16_t*>(out), x, static_cast<const int16_t*>(table), numel, s), "lut")
+                   ? UFB_OK
+                   : last_code();
+    if (table_bits == 8)
+        return cuda_ok(ew_lut8(static_cast<uint8_t*>(out), x, static_cast<const uint8_t*>(table), numel, s), "lut")
+                   ? UFB_OK
+                   : last_code();
+    return err(UFB_EINVAL, "invalid table dtype");
+}
+
+int ufb_bytes(const uint8_t* x, int64_t numel, int16_t* out, void* stream) {
+    clear_error();
+    if (!x || !out || numel <= 0 || numel > INT32_MAX) return err(UFB_EINVAL, "CUDA bytes required");
+    return cuda_ok(ew_bytes(out, x, numel, static_cast<cudaStream_t>(stream)), "bytes") ? UFB_OK : last_code();
+}
+
+int ufb_wsilu4(const int16_t* x, int n, int c4, int h, int w, const int16_t* table, int16_t* out, void* stream) {
+    clear_error();
+    if (!x || !table || !out || n <= 0 || c4 <= 0 || h <= 0 || w <= 0 || c4 % 4)
+        return err(UFB_EINVAL, "invalid WSiLU4 inputs");
+    if (static_cast<long long>(n) * c4 * h * w > INT32_MAX) return err(UFB_EINVAL, "unsupported tensor size");
+    return cuda_ok(ew_wsilu4(out, x, table, n, c4, static_cast<long long>(h) * w, static_cast<cudaStream_t>(stream)),
+                   "wsilu4")
+               ? UFB_OK
+               : last_code();
+}
+
+int ufb_warp(const int16_t* feature, const int16_t* flow, int n, int c, int h, int w, int16_t* out, void* stream) {
+    clear_error();
+    if (!feature || !flow || !out || n <= 0 || c <= 0 || h <= 0 || w <= 0)
+        return err(UFB_EINVAL, "invalid warp dimensions");
+    if (static_cast<long long>(n) * c * h * w > INT32_MAX || static_cast<long long>(w) * 512 > INT32_MAX / 2 ||
+        static_cast<long long>(h) * 512 > INT32_MAX / 2)
+        return err(UFB_ERANGE, "warp tensor exceeds indexing bounds");
+    return cuda_ok(warp_fixed(out, feature, flow, n, c, h, w, static_cast<cudaStream_t>(stream)), "warp")
+               ? UFB_OK
+               : last_code();
+}
+
+}  // extern "C"

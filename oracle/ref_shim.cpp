@@ -1,0 +1,372 @@
+// TEST INFRASTRUCTURE ONLY -- never linked into the product library.
+//
+// C-ABI shim around the reference's own CPU INT16 path, so tests and the
+// bench's CPU arm can run the UNMODIFIED reference sources
+//   src/int16_ops.cpp, src/layers.cpp, src/integer_model.cpp, src/entropy.cpp
+// (compiled in place from the reference checkout by oracle/Makefile) on the
+// same seeded inputs the CUDA engine receives.  Only two symbols the reference
+// declares but whose defining files drag in unrelated subsystems are supplied
+// here: uf::ProcessInterrupt::check() (include/uf/process.hpp:68-79; a no-op,
+// nothing here installs signal handlers) and uf::PreparedModel::tensor()
+// (include/uf/prepared.hpp:19-20; a plain map lookup).
+//
+// Every entry point returns 0 on success and -1 on a thrown exception, whose
+// message is kept in a thread-local string (ufref_last_error()).
+#include "uf/entropy.hpp"
+#include "uf/int16_ops.hpp"
+#include "uf/integer_model.hpp"
+#include "uf/layers.hpp"
+#include "uf/prepared.hpp"
+#include "uf/process.hpp"
+
+#include <ATen/Parallel.h>
+#include <torch/torch.h>
+
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace uf {
+void ProcessInterrupt::check() {}
+const torch::Tensor& PreparedModel::tensor(const std::string& name) const {
+    const auto it = tensors.find(name);
+    if (it == tensors.end()) throw std::runtime_error("Missing prepared UF tensor: " + name);
+    return it->second;
+}
+}  // namespace uf
+
+namespace {
+
+thread_local std::string g_error;
+
+template <class F>
+int guarded(F&& fn) {
+    try {
+        fn();
+        return 0;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+    } catch (...) {
+        g_error = "unknown exception";
+    }
+    return -1;
+}
+
+// dtype codes shared with oracle/__init__.py
+torch::ScalarType dtype_of(int code) {
+    switch (code) {
+        case 0: return torch::kInt16;
+        case 1: return torch::kUInt8;
+        case 2: return torch::kInt32;
+        case 3: return torch::kInt8;
+        case 4: return torch::kInt64;
+    }
+    throw std::invalid_argument("bad dtype code");
+}
+
+torch::Tensor wrap(const void* data, std::vector<int64_t> shape, torch::ScalarType type) {
+    return torch::from_blob(const_cast<void*>(data), shape, torch::TensorOptions().dtype(type)).clone();
+}
+
+void emit(const torch::Tensor& value, void* out, int64_t capacity_bytes, int64_t* shape4) {
+    const auto t = value.contiguous();
+    const auto bytes = static_cast<int64_t>(t.numel() * t.element_size());
+    if (bytes > capacity_bytes) throw std::length_error("output buffer too small");
+    if (bytes) std::memcpy(out, t.data_ptr(), bytes);
+    if (shape4) {
+        for (int d = 0; d < 4; ++d) shape4[d] = d < t.dim() ? t.size(d) : 1;
+    }
+}
+
+struct RefModel {
+    uf::PreparedModel prepared;
+    std::unique_ptr<uf::IntegerModel> model;
+    std::unique_ptr<uf::Layers> layers;
+    std::vector<uint8_t> payload;
+    std::vector<torch::Tensor> frames;
+};
+
+}  // namespace
+
+extern "C" {
+
+const char* ufref_last_error() { return g_error.c_str(); }
+
+int ufref_set_threads(int threads) {
+    return guarded([&] { torch::set_num_threads(threads); });
+}
+
+int ufref_get_threads() { return at::get_num_threads(); }
+
+// uf::int16::conv2d on CPU == conv2d_reference (src/int16_ops.cpp:132-171).
+// bias_dtype: 0 = int16, 2 = int32 (the reference widens either to int64).
+int ufref_conv2d(const int16_t* x, const int64_t* xs, const int16_t* w, const int64_t* ws,
+                 const void* bias, int bias_dtype, int64_t sh, int64_t sw, int64_t ph,
+                 int64_t pw, int64_t groups, int16_t* out, int64_t capacity, int64_t* os) {
+    return guarded([&] {
+        const auto input = wrap(x, {xs[0], xs[1], xs[2], xs[3]}, torch::kInt16);
+        const auto weight = wrap(w, {ws[0], ws[1], ws[2], ws[3]}, torch::kInt16);
+        torch::Tensor b;
+        if (bias) b = wrap(bias, {ws[0]}, dtype_of(bias_dtype));
+        emit(uf::int16::conv2d(input, weight, b, sh, sw, ph, pw, groups), out, capacity * 2, os);
+    });
+}
+
+int ufref_add(int count, const int16_t* const* values, int64_t numel, int16_t* out) {
+    return guarded([&] {
+        std::vector<torch::Tensor> operands;
+        for (int i = 0; i < count; ++i) operands.push_back(wrap(values[i], {numel}, torch::kInt16));
+        emit(uf::int16::add(operands), out, numel * 2, nullptr);
+    });
+}
+
+int ufref_multiply(const int16_t* x, const int64_t* xs, const int16_t* s, const int64_t* ss,
+                   int16_t* out) {
+    return guarded([&] {
+        const auto value = wrap(x, {xs[0], xs[1], xs[2], xs[3]}, torch::kInt16);
+        const auto scale = wrap(s, {ss[0], ss[1], ss[2], ss[3]}, torch::kInt16);
+        emit(uf::int16::multiply(value, scale), out, value.numel() * 2, nullptr);
+    });
+}
+
+int ufref_lookup(const int16_t* x, int64_t numel, const void* table, int table_dtype, void* out) {
+    return guarded([&] {
+        const auto value = wrap(x, {numel}, torch::kInt16);
+        const auto lut = wrap(table, {65536}, dtype_of(table_dtype));
+        const auto result = uf::int16::lookup(value, lut);
+        emit(result, out, numel * result.element_size(), nullptr);
+    });
+}
+
+int ufref_wsilu4(const int16_t* x, const int64_t* xs, const int16_t* table, int16_t* out) {
+    return guarded([&] {
+        const auto value = wrap(x, {xs[0], xs[1], xs[2], xs[3]}, torch::kInt16);
+        const auto lut = wrap(table, {65536}, torch::kInt16);
+        emit(uf::int16::wsilu4(value, lut), out, value.numel() / 4 * 2, nullptr);
+    });
+}
+
+int ufref_from_bytes(const uint8_t* x, int64_t numel, int16_t* out) {
+    return guarded([&] {
+        emit(uf::int16::from_bytes(wrap(x, {numel}, torch::kUInt8)), out, numel * 2, nullptr);
+    });
+}
+
+int ufref_divide_round(const int64_t* x, int64_t numel, int64_t denominator, int64_t* out) {
+    return guarded([&] {
+        emit(uf::int16::divide_round(wrap(x, {numel}, torch::kInt64), denominator), out,
+             numel * 8, nullptr);
+    });
+}
+
+int ufref_symbols(const int16_t* x, int64_t numel, int8_t* out) {
+    return guarded([&] { emit(uf::int16::symbols(wrap(x, {numel}, torch::kInt16)), out, numel, nullptr); });
+}
+
+int ufref_reciprocal(const int16_t* x, int64_t numel, int16_t* out) {
+    return guarded([&] { emit(uf::int16::reciprocal(wrap(x, {numel}, torch::kInt16)), out, numel * 2, nullptr); });
+}
+
+int ufref_pixel_shuffle(const int16_t* x, const int64_t* xs, int64_t factor, int unshuffle,
+                        int16_t* out, int64_t* os) {
+    return guarded([&] {
+        const auto value = wrap(x, {xs[0], xs[1], xs[2], xs[3]}, torch::kInt16);
+        const auto result = unshuffle ? uf::pixel_unshuffle(value, factor) : uf::pixel_shuffle(value, factor);
+        emit(result, out, value.numel() * 2, os);
+    });
+}
+
+// ---- model (uf::IntegerModel / uf::Layers, src/integer_model.cpp, src/layers.cpp) ----
+
+void* ufref_model_new(const char* variant, int count, const char* const* names, const int* dtypes,
+                      const int* ndims, const int64_t* shapes, const void* const* data) {
+    auto handle = std::make_unique<RefModel>();
+    const int rc = guarded([&] {
+        auto& p = handle->prepared;
+        p.format = "dcvc-uf-prepared-v1";
+        p.arithmetic = uf::int16::arithmetic_id;
+        p.variant = variant;
+        const int64_t* cursor = shapes;
+        for (int i = 0; i < count; ++i) {
+            std::vector<int64_t> shape(cursor, cursor + ndims[i]);
+            cursor += ndims[i];
+            p.tensors[names[i]] = wrap(data[i], shape, dtype_of(dtypes[i]));
+        }
+        handle->model = std::make_unique<uf::IntegerModel>(p, torch::kCPU, true);
+        handle->layers = std::make_unique<uf::Layers>(p, torch::kCPU);
+    });
+    return rc == 0 ? handle.release() : nullptr;
+}
+
+void ufref_model_free(void* h) { delete static_cast<RefModel*>(h); }
+
+int ufref_model_set_skip(void* h, double threshold) {
+    return guarded([&] { static_cast<RefModel*>(h)->model->set_skip_threshold(threshold); });
+}
+
+int ufref_model_clear_dpb(void* h) {
+    return guarded([&] { static_cast<RefModel*>(h)->model->clear_dpb(); });
+}
+
+int ufref_model_add_ref(void* h, const int16_t* frame, const int64_t* fs) {
+    return guarded([&] {
+        static_cast<RefModel*>(h)->model->add_ref_feature_from_frame(
+            wrap(frame, {fs[0], fs[1], fs[2], fs[3]}, torch::kInt16));
+    });
+}
+
+// IntegerModel::compress (src/integer_model.cpp:312-334).  The payload and the
+// reconstructed frames are kept in the handle; fetch them with the getters.
+int ufref_model_compress(void* h, const int16_t* frames, const int64_t* fs, int qp, int reset) {
+    return guarded([&] {
+        auto* m = static_cast<RefModel*>(h);
+        auto result = m->model->compress(wrap(frames, {fs[0], fs[1], fs[2], fs[3]}, torch::kInt16),
+                                         qp, reset != 0);
+        m->payload = std::move(result.payload);
+        m->frames = std::move(result.frames);
+    });
+}
+
+// IntegerModel::decompress (src/integer_model.cpp:336-359).
+int ufref_model_decompress(void* h, const uint8_t* payload, int64_t length, uint32_t width,
+                           uint32_t height, int qp, int reset) {
+    return guarded([&] {
+        auto* m = static_cast<RefModel*>(h);
+        std::vector<uint8_t> bytes(payload, payload + length);
+        m->frames = m->model->decompress(bytes, width, height, qp, 1, reset != 0);
+    });
+}
+
+int64_t ufref_model_payload(void* h, uint8_t* out, int64_t capacity) {
+    auto* m = static_cast<RefModel*>(h);
+    const auto n = static_cast<int64_t>(m->payload.size());
+    if (out && capacity >= n && n) std::memcpy(out, m->payload.data(), n);
+    return n;
+}
+
+int ufref_model_frame_count(void* h) { return static_cast<int>(static_cast<RefModel*>(h)->frames.size()); }
+
+int ufref_model_frame(void* h, int index, int16_t* out, int64_t capacity, int64_t* shape4) {
+    return guarded([&] {
+        auto* m = static_cast<RefModel*>(h);
+        emit(m->frames.at(index), out, capacity * 2, shape4);
+    });
+}
+
+// which: 0 = reference, 1 = memory, 2 = context.  Returns 1 when the state is
+// undefined (Python None), 0 after copying, -1 on error.
+int ufref_model_state(void* h, int which, int16_t* out, int64_t capacity, int64_t* shape4) {
+    int undefined = 0;
+    const int rc = guarded([&] {
+        auto* m = static_cast<RefModel*>(h);
+        const auto& t = which == 0 ? m->model->reference() : which == 1 ? m->model->memory() : m->model->context();
+        if (!t.defined()) { undefined = 1; return; }
+        emit(t, out, capacity * 2, shape4);
+    });
+    return rc ? rc : undefined;
+}
+
+// uf::Layers::run (src/layers.cpp:132-184) for per-module parity: args are
+// int16 NCHW tensors; the result is copied to out.
+int ufref_layers_run(void* h, const char* module, int count, const int16_t* const* args,
+                     const int64_t* shapes, int16_t* out, int64_t capacity, int64_t* shape4) {
+    return guarded([&] {
+        auto* m = static_cast<RefModel*>(h);
+        std::vector<torch::Tensor> values;
+        for (int i = 0; i < count; ++i) {
+            const int64_t* s = shapes + 4 * i;
+            values.push_back(wrap(args[i], {s[0], s[1], s[2], s[3]}, torch::kInt16));
+        }
+        emit(m->layers->run(module, values), out, capacity * 2, shape4);
+    });
+}
+
+// uf::Layers::parameter (src/layers.cpp:63-72), i.e. table[qp:qp+1,:,None,None].
+int ufref_layers_parameter(void* h, const char* name, int64_t qp, int16_t* out, int64_t capacity,
+                           int64_t* shape4) {
+    return guarded([&] {
+        auto* m = static_cast<RefModel*>(h);
+        emit(m->layers->parameter(name, qp), out, capacity * 2, shape4);
+    });
+}
+
+int ufref_layers_reconstruct(void* h, const int16_t* feature, const int64_t* fs, int for_reset,
+                             int index, int16_t* out, int64_t capacity, int64_t* shape4) {
+    return guarded([&] {
+        auto* m = static_cast<RefModel*>(h);
+        const auto frames = m->layers->reconstruct(wrap(feature, {fs[0], fs[1], fs[2], fs[3]}, torch::kInt16),
+                                                   for_reset != 0);
+        emit(frames.at(index), out, capacity * 2, shape4);
+    });
+}
+
+// ---- rANS (src/entropy.cpp) ----
+
+struct RefRans {
+    uf::EntropyEncoder encoder;
+    uf::EntropyDecoder decoder;
+    std::vector<uint8_t> out;
+};
+
+void* ufref_rans_new(const int32_t* z_cdf, int64_t z_rows, int64_t z_width, const int32_t* z_len,
+                     const int32_t* y_cdf, int64_t y_rows, int64_t y_width, const int32_t* y_len) {
+    auto r = std::make_unique<RefRans>();
+    const int rc = guarded([&] {
+        std::vector<int32_t> zc(z_cdf, z_cdf + z_rows * z_width), zl(z_len, z_len + z_rows);
+        std::vector<int32_t> yc(y_cdf, y_cdf + y_rows * y_width), yl(y_len, y_len + y_rows);
+        r->encoder.set_cdf(0, zc, zl);
+        r->encoder.set_cdf(1, yc, yl);
+        r->decoder.set_cdf(0, zc, zl);
+        r->decoder.set_cdf(1, yc, yl);
+    });
+    return rc == 0 ? r.release() : nullptr;
+}
+
+void ufref_rans_free(void* h) { delete static_cast<RefRans*>(h); }
+
+int ufref_rans_reset(void* h) { return guarded([&] { static_cast<RefRans*>(h)->encoder.reset(); }); }
+
+int ufref_rans_encode_y(void* h, const int16_t* packed, int64_t n) {
+    return guarded([&] { static_cast<RefRans*>(h)->encoder.encode_y(std::vector<int16_t>(packed, packed + n)); });
+}
+
+int ufref_rans_encode_z(void* h, const int8_t* symbols, int64_t n, int offset, int channels) {
+    return guarded([&] {
+        static_cast<RefRans*>(h)->encoder.encode_z(std::vector<int8_t>(symbols, symbols + n), offset, channels);
+    });
+}
+
+int64_t ufref_rans_flush(void* h, uint8_t* out, int64_t capacity) {
+    auto* r = static_cast<RefRans*>(h);
+    int64_t n = -1;
+    guarded([&] {
+        r->out = r->encoder.flush();
+        n = static_cast<int64_t>(r->out.size());
+    });
+    if (n >= 0 && out && capacity >= n && n) std::memcpy(out, r->out.data(), n);
+    return n;
+}
+
+int ufref_rans_set_stream(void* h, const uint8_t* data, int64_t n) {
+    return guarded([&] { static_cast<RefRans*>(h)->decoder.set_stream(std::vector<uint8_t>(data, data + n)); });
+}
+
+int ufref_rans_decode_z(void* h, int64_t count, int offset, int channels, int8_t* out) {
+    return guarded([&] {
+        const auto v = static_cast<RefRans*>(h)->decoder.decode_z(count, offset, channels);
+        if (!v.empty()) std::memcpy(out, v.data(), v.size());
+    });
+}
+
+int ufref_rans_decode_y(void* h, const uint8_t* indexes, int64_t n, int8_t* out) {
+    return guarded([&] {
+        const auto v = static_cast<RefRans*>(h)->decoder.decode_y(std::vector<uint8_t>(indexes, indexes + n));
+        if (!v.empty()) std::memcpy(out, v.data(), v.size());
+    });
+}
+
+}  // extern "C"

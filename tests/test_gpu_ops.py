@@ -1,0 +1,166 @@
+"""GPU parity of the operator-level C ABI against the CPU oracle (bit-exact).
+
+Mirrors the reference's CUDA checks in tests/model_free.cpp:580-621
+(elementwise parity, four convolution geometries, int64-accumulator extremes
+through all three convolution variants) and widens them to the HT-L layer
+shapes, K/N tails and the config-1 convolution.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "model_free.npz")
+
+
+def T(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def N(t):
+    return t.cpu().numpy()
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return np.load(GOLDEN)
+
+
+def _status_clean(ufb):
+    assert ufb.device_status(0) == 0
+
+
+@pytest.mark.parametrize("variant", ["auto", "generic", "baseline"])
+@pytest.mark.parametrize("i", range(8))
+def test_conv_golden(ufb, dev, gold, i, variant):
+    ci, co, k, stride, pad, groups = [int(g) for g in gold[f"conv{i}_geom"]]
+    x, w, b = gold[f"conv{i}_x"], gold[f"conv{i}_w"], gold[f"conv{i}_b"]
+    got = ufb.conv2d(T(x, dev), T(w, dev), T(b, dev), stride, stride, pad, pad, groups, variant=variant)
+    assert np.array_equal(N(got), gold[f"conv{i}_out"])
+    _status_clean(ufb)
+
+
+def test_elementwise_golden(ufb, dev, gold):
+    v, o = T(gold["ew_values"], dev), T(gold["ew_other"], dev)
+    lut = T(gold["ew_lut"], dev)
+    assert np.array_equal(N(ufb.add([v, o])), gold["ew_add"])
+    assert np.array_equal(N(ufb.multiply(v, T(gold["ew_scale"], dev))), gold["ew_mul"])
+    assert np.array_equal(N(ufb.lookup(v, lut)), gold["ew_lookup"])
+    assert np.array_equal(N(ufb.wsilu4(v, lut)), gold["ew_wsilu4"])
+    assert np.array_equal(N(ufb.from_bytes(T(gold["bytes_in"], dev))), gold["bytes_out"])
+
+
+def test_elementwise_random(ufb, ora, dev):
+    rng = np.random.default_rng(3)
+    shape = (2, 16, 9, 13)
+    a, b, c, d = (rng.integers(-32768, 32768, shape).astype(np.int16) for _ in range(4))
+    for k in (2, 3, 4):
+        ops = [a, b, c, d][:k]
+        assert np.array_equal(N(ufb.add([T(x, dev) for x in ops])), ora.add(*ops))
+    for sshape in [(1, 16, 1, 1), shape, (1, 1, 9, 13), (2, 1, 1, 1)]:
+        s = rng.integers(-32768, 32768, sshape).astype(np.int16)
+        assert np.array_equal(N(ufb.multiply(T(a, dev), T(s, dev))), ora.multiply(a, s))
+    t16 = rng.integers(-32768, 32768, 65536).astype(np.int16)
+    t8 = rng.integers(0, 256, 65536).astype(np.uint8)
+    assert np.array_equal(N(ufb.lookup(T(a, dev), T(t16, dev))), ora.lookup(a, t16))
+    assert np.array_equal(N(ufb.lookup(T(a, dev), T(t8, dev))), ora.lookup(a, t8))
+    assert np.array_equal(N(ufb.wsilu4(T(a, dev), T(t16, dev))), ora.wsilu4(a, t16))
+
+
+@pytest.mark.parametrize("ci,co,hw", [(16, 16, (7, 9)), (64, 64, (16, 16)), (128, 128, (11, 13)),
+                                      (192, 512, (8, 10)), (512, 512, (9, 17)), (512, 2048, (4, 8)),
+                                      (1024, 512, (6, 7)), (768, 256, (5, 8)), (256, 192, (12, 12)),
+                                      (2048, 512, (3, 5)), (100, 40, (5, 5))])
+def test_conv1x1_shapes(ufb, ora, dev, ci, co, hw):
+    rng = np.random.default_rng(ci * 7 + co)
+    x = rng.integers(-32768, 32768, (2, ci) + hw).astype(np.int16)
+    w = rng.integers(-32768, 32768, (co, ci, 1, 1)).astype(np.int16)
+    b = rng.integers(-32768, 32768, (co,)).astype(np.int16)
+    got = ufb.conv2d(T(x, dev), T(w, dev), T(b, dev))
+    assert np.array_equal(N(got), ora.conv2d(x, w, b))
+    _status_clean(ufb)
+
+
+@pytest.mark.parametrize("ci,co,hw", [(64, 64, (9, 20)), (256, 128, (10, 12)), (32, 80, (5, 33)),
+                                      (256, 2048, (4, 6)), (8, 6, (7, 8))])
+def test_conv3x3_shapes(ufb, ora, dev, ci, co, hw):
+    rng = np.random.default_rng(ci + co)
+    x = rng.integers(-32768, 32768, (1, ci) + hw).astype(np.int16)
+    w = rng.integers(-32768, 32768, (co, ci, 3, 3)).astype(np.int16)
+    b = rng.integers(-32768, 32768, (co,)).astype(np.int16)
+    got = ufb.conv2d(T(x, dev), T(w, dev), T(b, dev), 1, 1, 1, 1)
+    assert np.array_equal(N(got), ora.conv2d(x, w, b, 1, 1))
+    _status_clean(ufb)
+
+
+def test_conv_config1_int32_bias(ufb, ora, dev):
+    rng = np.random.default_rng(0)
+    x = rng.integers(-4096, 4097, (1, 64, 88, 160)).astype(np.int16)
+    w = rng.integers(-256, 257, (64, 64, 3, 3)).astype(np.int16)
+    b = rng.integers(-(1 << 16), (1 << 16) + 1, (64,)).astype(np.int32)
+    got = ufb.conv2d(T(x, dev), T(w, dev), T(b, dev), 1, 1, 1, 1)
+    assert np.array_equal(N(got), ora.conv2d(x, w, b, 1, 1))
+
+
+@pytest.mark.parametrize("kernel", [1, 3])
+@pytest.mark.parametrize("sign", [-1, 1])
+@pytest.mark.parametrize("ci", [32, 2048])
+def test_accumulator_extremes(ufb, ora, dev, kernel, sign, ci):
+    x = np.full((1, ci, 5, 5), 32767, np.int16)
+    w = np.full((32, ci, kernel, kernel), 32767 if sign == 1 else -32768, np.int16)
+    # mix in the low-byte extremes too: alternate 32767 and -32768 / -1 / 255
+    w.reshape(-1)[::3] = -1
+    x.reshape(-1)[::5] = -32768
+    b = np.zeros(32, np.int16)
+    for variant in ("auto", "generic", "baseline"):
+        got = ufb.conv2d(T(x, dev), T(w, dev), T(b, dev), 1, 1, kernel // 2, kernel // 2, variant=variant)
+        assert np.array_equal(N(got), ora.conv2d(x, w, b, 1, kernel // 2))
+
+
+def test_unsigned_low_byte_bound(ufb, ora, dev):
+    # low bytes 255 everywhere (value = 255 + 256 * hi) stress the u8 x u8 accumulator
+    ci = 3584  # K = 3584 * 9 = 32256 <= 32768, the exactness bound
+    x = np.full((1, ci, 3, 3), 255, np.int16)
+    w = np.full((16, ci, 3, 3), 255, np.int16)
+    got = ufb.conv2d(T(x, dev), T(w, dev), None, 1, 1, 1, 1)
+    assert np.array_equal(N(got), ora.conv2d(x, w, None, 1, 1))
+
+
+def test_large_reduction_uses_direct_path(ufb, ora, dev):
+    rng = np.random.default_rng(5)
+    x = rng.integers(-32768, 32768, (1, 4000, 3, 3)).astype(np.int16)  # 36000 > 32768
+    w = rng.integers(-32768, 32768, (4, 4000, 3, 3)).astype(np.int16)
+    got = ufb.conv2d(T(x, dev), T(w, dev), None, 1, 1, 1, 1)
+    assert np.array_equal(N(got), ora.conv2d(x, w, None, 1, 1))
+
+
+def test_depthwise_and_stride2(ufb, ora, dev):
+    rng = np.random.default_rng(9)
+    x = rng.integers(-32768, 32768, (1, 64, 10, 12)).astype(np.int16)
+    wd = rng.integers(-32768, 32768, (64, 1, 3, 3)).astype(np.int16)
+    b = rng.integers(-32768, 32768, (64,)).astype(np.int16)
+    assert np.array_equal(N(ufb.conv2d(T(x, dev), T(wd, dev), T(b, dev), 1, 1, 1, 1, 64)),
+                          ora.conv2d(x, wd, b, 1, 1, 64))
+    w2 = rng.integers(-32768, 32768, (32, 64, 3, 3)).astype(np.int16)
+    assert np.array_equal(N(ufb.conv2d(T(x, dev), T(w2, dev), None, 2, 2, 1, 1)), ora.conv2d(x, w2, None, 2, 1))
+
+
+def test_warp_matches_oracle(ufb, ora, dev):
+    rng = np.random.default_rng(1)
+    f = rng.integers(-4096, 4097, (1, 8, 44, 80)).astype(np.int16)
+    flow = np.round(512 * (rng.normal(0, 4, (1, 2, 44, 80)) + np.array([3.25, -1.5])[None, :, None, None]))
+    flow = np.clip(flow, -32768, 32767).astype(np.int16)
+    assert np.array_equal(N(ufb.warp(T(f, dev), T(flow, dev))), ora.warp(f, flow))
+
+
+def test_errors_are_raised_not_computed(ufb, dev):
+    x = torch.zeros((1, 8, 4, 4), dtype=torch.int16, device=dev)
+    with pytest.raises(ufb.UfbError):
+        ufb.conv2d(x, torch.zeros((8, 3, 1, 1), dtype=torch.int16, device=dev))
+    with pytest.raises(ufb.UfbError):
+        ufb.add([x])
+    with pytest.raises(ufb.UfbError):
+        ufb.multiply(x, torch.zeros((1, 3, 1, 1), dtype=torch.int16, device=dev))

@@ -1,0 +1,107 @@
+"""CPU: the oracle restatement is pinned to the reference's own known-answer
+cases (golden fixtures made from the reference's compiled CPU path) and, when
+oracle/_ref is built, to the reference on seeded random cases."""
+import os
+
+import numpy as np
+import pytest
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "model_free.npz")
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return np.load(GOLDEN)
+
+
+def test_bytes_all_values(ora, gold):
+    assert np.array_equal(ora.from_bytes(gold["bytes_in"]), gold["bytes_out"])
+
+
+def test_rna_ties(ora, gold):
+    got = np.array([ora.divide_round(int(v), 512) for v in gold["ties_in"]], np.int64)
+    assert np.array_equal(got, gold["ties_out"])
+    assert list(got) == [-2, -2, -1, -1, -1, 0, 0, 1, 1, 1, 2, 2]
+
+
+def test_elementwise_golden(ora, gold):
+    v, o = gold["ew_values"], gold["ew_other"]
+    assert np.array_equal(ora.add(v, o), gold["ew_add"])
+    assert np.array_equal(ora.multiply(v, gold["ew_scale"]), gold["ew_mul"])
+    assert np.array_equal(ora.lookup(v, gold["ew_lut"]), gold["ew_lookup"])
+    assert np.array_equal(ora.wsilu4(v, gold["ew_lut"]), gold["ew_wsilu4"])
+
+
+@pytest.mark.parametrize("i", range(8))
+def test_conv_golden(ora, gold, i):
+    ci, co, k, stride, pad, groups = [int(g) for g in gold[f"conv{i}_geom"]]
+    got = ora.conv2d(gold[f"conv{i}_x"], gold[f"conv{i}_w"], gold[f"conv{i}_b"], stride, pad, groups)
+    assert np.array_equal(got, gold[f"conv{i}_out"])
+
+
+def test_conv_extremes_saturate(gold):
+    # all-32767 inputs with +-full-scale weights saturate both ways (int64 accumulator)
+    outs = [gold[f"conv{i}_out"] for i in range(4, 8)]
+    assert (outs[0] == -32768).all() and (outs[1] == 32767).all()
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_conv_random_vs_reference(ora, ref, seed):
+    rng = np.random.default_rng(100 + seed)
+    ci, co = int(rng.integers(1, 40)), int(rng.integers(1, 40))
+    k = int(rng.choice([1, 3]))
+    stride = int(rng.choice([1, 2]))
+    groups = 1 if seed % 2 == 0 else int(np.gcd(ci, co))
+    h, w = int(rng.integers(k, 20)), int(rng.integers(k, 20))
+    x = rng.integers(-32768, 32768, (2, ci, h, w)).astype(np.int16)
+    wt = rng.integers(-32768, 32768, (co, ci // groups, k, k)).astype(np.int16)
+    b = rng.integers(-32768, 32768, (co,)).astype(np.int16)
+    assert np.array_equal(ora.conv2d(x, wt, b, stride, k // 2, groups), ref.conv2d(x, wt, b, stride, k // 2, groups))
+
+
+def test_conv_int32_bias_vs_reference(ora, ref):
+    rng = np.random.default_rng(0)
+    x = rng.integers(-4096, 4097, (1, 16, 12, 20)).astype(np.int16)
+    w = rng.integers(-256, 257, (16, 16, 3, 3)).astype(np.int16)
+    b = rng.integers(-(1 << 16), (1 << 16) + 1, (16,)).astype(np.int32)
+    assert np.array_equal(ora.conv2d(x, w, b, 1, 1), ref.conv2d(x, w, b, 1, 1))
+
+
+def test_elementwise_random_vs_reference(ora, ref):
+    rng = np.random.default_rng(7)
+    a = rng.integers(-32768, 32768, (2, 8, 5, 6)).astype(np.int16)
+    b = rng.integers(-32768, 32768, (2, 8, 5, 6)).astype(np.int16)
+    c = rng.integers(-32768, 32768, (2, 8, 5, 6)).astype(np.int16)
+    assert np.array_equal(ora.add(a, b, c), ref.add(a, b, c))
+    for shape in [(1, 8, 1, 1), (2, 8, 5, 6), (1, 1, 5, 6)]:
+        s = rng.integers(-32768, 32768, shape).astype(np.int16)
+        assert np.array_equal(ora.multiply(a, s), ref.multiply(a, s))
+    t8 = rng.integers(0, 256, 65536).astype(np.uint8)
+    assert np.array_equal(ora.lookup(a, t8), ref.lookup(a, t8))
+    assert np.array_equal(ora.symbols(a), ref.symbols(a))
+    assert np.array_equal(ora.reciprocal(a), ref.reciprocal(a))
+    for f in (2, 8):
+        x = rng.integers(-32768, 32768, (1, 3 * f * f, 4, 5)).astype(np.int16)
+        assert np.array_equal(ora.pixel_shuffle(x, f), ref.pixel_shuffle(x, f))
+        y = rng.integers(-32768, 32768, (1, 3, 4 * f, 5 * f)).astype(np.int16)
+        assert np.array_equal(ora.pixel_unshuffle(y, f), ref.pixel_shuffle(y, f, unshuffle=True))
+
+
+def test_warp_identity_and_shift(ora):
+    rng = np.random.default_rng(1)
+    f = rng.integers(-4096, 4097, (1, 4, 9, 11)).astype(np.int16)
+    zero = np.zeros((1, 2, 9, 11), np.int16)
+    assert np.array_equal(ora.warp(f, zero), f)
+    one = zero.copy()
+    one[:, 0] = 512  # +1 px in x: out[x] = f[min(x+1, W-1)]
+    want = np.concatenate([f[..., 1:], f[..., -1:]], axis=-1)
+    assert np.array_equal(ora.warp(f, one), want)
+
+
+def test_warp_close_to_float_semantics(ora):
+    rng = np.random.default_rng(2)
+    f = rng.integers(-4096, 4097, (1, 3, 16, 20)).astype(np.int16)
+    flow = np.round(512 * (rng.normal(0, 4, (1, 2, 16, 20)) + np.array([3.25, -1.5])[None, :, None, None]))
+    flow = flow.astype(np.int16)
+    diff = np.abs(ora.warp(f, flow).astype(np.float64) - ora.warp_float(f, flow))
+    assert diff.max() <= 1.0
