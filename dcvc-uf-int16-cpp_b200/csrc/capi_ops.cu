@@ -214,4 +214,78 @@ int ufb_warp(const int16_t* feature, const int16_t* flow, int n, int c, int h, i
                : last_code();
 }
 
+int ufb_to_split(const int16_t* x, int n, int c, int h, int w, int factor, uint8_t* out, int pitch, void* stream) {
+    clear_error();
+    if (!x || !out || n <= 0 || c <= 0 || h <= 0 || w <= 0 || factor <= 0 || h % factor || w % factor)
+        return err(UFB_EINVAL, "invalid split conversion geometry");
+    if (pitch % 16 || pitch < c * factor * factor || reinterpret_cast<uintptr_t>(out) % 16)
+        return err(UFB_EINVAL, "split pitch must be a multiple of 16 covering every channel");
+    const Act a = make_act(out, n, h / factor, w / factor, c * factor * factor, pitch);
+    return cuda_ok(nchw_to_split(x, n, c, h, w, factor, a, static_cast<cudaStream_t>(stream)), "to split")
+               ? UFB_OK
+               : last_code();
+}
+
+int ufb_from_split(const uint8_t* x, int n, int c, int h, int w, int pitch, int factor, int16_t* out,
+                   void* stream) {
+    clear_error();
+    if (!x || !out || n <= 0 || c <= 0 || h <= 0 || w <= 0 || factor <= 0 || c % (factor * factor))
+        return err(UFB_EINVAL, "invalid split conversion geometry");
+    if (pitch % 16 || pitch < c || reinterpret_cast<uintptr_t>(x) % 16)
+        return err(UFB_EINVAL, "split pitch must be a multiple of 16 covering every channel");
+    const Act a = make_act(const_cast<uint8_t*>(x), n, h, w, c, pitch);
+    return cuda_ok(split_to_nchw(a, factor, out, static_cast<cudaStream_t>(stream)), "from split") ? UFB_OK
+                                                                                                   : last_code();
+}
+
+int64_t ufb_weight_bytes(int co, int ci, int kh, int kw) {
+    if (co <= 0 || ci <= 0 || kh <= 0 || kw <= 0) return 0;
+    return static_cast<int64_t>(2) * co * kh * kw * round_up(ci, 128);
+}
+
+int ufb_prepare_weights(const int16_t* weight, int co, int ci, int kh, int kw, uint8_t* planes, void* stream) {
+    clear_error();
+    if (!weight || !planes || co <= 0 || ci <= 0 || kh <= 0 || kw <= 0) return err(UFB_EINVAL, "invalid weights");
+    const int cpad = round_up(ci, 128);
+    return cuda_ok(prep_weights(weight, co, ci, kh, kw, cpad, kh * kw * cpad, planes,
+                                static_cast<cudaStream_t>(stream)),
+                   "weight preparation")
+               ? UFB_OK
+               : last_code();
+}
+
+int ufb_conv2d_split(const uint8_t* x, int n, int ci, int h, int w, int x_pitch, const uint8_t* planes, int co,
+                     int kh, int kw, const void* bias, int bias_bits, int pad_h, int pad_w, uint8_t* out,
+                     int out_pitch, void* stream) {
+    clear_error();
+    if (!bias) bias_bits = 0;
+    int oh = 0, ow = 0;
+    // geometry checks of the NCHW entry point (x only needs to be non-null)
+    if (!check_conv(reinterpret_cast<const int16_t*>(x), n, ci, h, w, reinterpret_cast<const int16_t*>(planes), co,
+                    kh, kw, bias_bits, 1, 1, pad_h, pad_w, 1, reinterpret_cast<int16_t*>(out), oh, ow))
+        return last_code();
+    if (static_cast<long long>(ci) * kh * kw > 32768) return err(UFB_ERANGE, "reduction exceeds 32768");
+    int device = 0;
+    if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return last_code();
+    TcWeights tw;
+    tw.co = co;
+    tw.ci = ci;
+    tw.kh = kh;
+    tw.kw = kw;
+    tw.cpad = round_up(ci, 128);
+    tw.kpad = kh * kw * tw.cpad;
+    tw.planes = const_cast<uint8_t*>(planes);
+    std::string msg;
+    if (!tc_weight_map(tw, 128, &tw.map128, msg) || !tc_weight_map(tw, 64, &tw.map64, msg))
+        return err(UFB_ECUDA, msg);
+    const Act in = make_act(const_cast<uint8_t*>(x), n, h, w, ci, x_pitch);
+    const Act ov = make_act(out, n, oh, ow, co, out_pitch);
+    Epilogue epi{};
+    epi.bias = bias_bits ? bias : nullptr;
+    epi.bias32 = bias_bits == 32;
+    if (conv_tc_run(tw, in, ov, epi, pad_h, pad_w, static_cast<cudaStream_t>(stream), device_status(device), msg))
+        return err(UFB_EINVAL, msg);
+    return UFB_OK;
+}
+
 }  // extern "C"

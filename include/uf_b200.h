@@ -102,6 +102,43 @@ int ufb_wsilu4(const int16_t* x, int n, int c4, int h, int w, const int16_t* tab
 int ufb_warp(const int16_t* feature, const int16_t* flow, int n, int c, int h, int w, int16_t* out,
              void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Split-layout operators.  The engine keeps activations in HBM as "split
+ * NHWC": per pixel, a row of 2 * pitch bytes holding the low bytes (u8) of its
+ * channels followed by their high bytes (s8); value = lo + 256 * hi.  pitch
+ * and any channel offset are multiples of 16.  Callers that keep activations
+ * resident in this layout avoid the NCHW conversions of ufb_conv2d.
+ * ------------------------------------------------------------------------- */
+
+/* NCHW int16 -> split (pixel_unshuffle(factor) fused; factor 1 = layout only).
+ * out holds n x (h/f) x (w/f) pixels of c*f*f channels with row pitch `pitch`. */
+int ufb_to_split(const int16_t* x, int n, int c, int h, int w, int factor, uint8_t* out, int pitch, void* stream);
+
+/* split -> NCHW int16 (pixel_shuffle(factor) fused).  x holds n x h x w pixels
+ * of c channels; out is [n, c/(f*f), h*f, w*f]. */
+int ufb_from_split(const uint8_t* x, int n, int c, int h, int w, int pitch, int factor, int16_t* out,
+                   void* stream);
+
+/* Bytes of the prepared weight planes for a [co, ci, kh, kw] convolution. */
+int64_t ufb_weight_bytes(int co, int ci, int kh, int kw);
+
+/* Prepare int16 [co, ci, kh, kw] weights (device) into tensor-core planes
+ * (device, ufb_weight_bytes() bytes). */
+int ufb_prepare_weights(const int16_t* weight, int co, int ci, int kh, int kw, uint8_t* planes, void* stream);
+
+/* uf_conv on split activations with prepared weights: stride 1, zero padding
+ * (pad_h, pad_w), groups 1, ci*kh*kw <= 32768.  Uses no scratch memory. */
+int ufb_conv2d_split(const uint8_t* x, int n, int ci, int h, int w, int x_pitch, const uint8_t* planes, int co,
+                     int kh, int kw, const void* bias, int bias_bits, int pad_h, int pad_w, uint8_t* out,
+                     int out_pitch, void* stream);
+
+/* Measurement utility (no reference counterpart): launches `ctas` CTAs that
+ * each issue `iters` x 4 dense tcgen05 kind::i8 M=128 N=256 K=32 MMAs from
+ * resident shared-memory tiles; *int8_ops receives the operation count
+ * (2 per multiply-add).  The caller times the launch on `stream` to obtain
+ * the int8 tensor-pipe peak used as the convolution roofline. */
+int ufb_probe_i8_peak(int iters, int ctas, void* stream, int64_t* int8_ops);
+
 #ifdef __cplusplus
 }
 #endif
