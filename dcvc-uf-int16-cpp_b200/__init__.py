@@ -168,3 +168,198 @@ def warp(feature, flow):
     out = torch.empty_like(feature)
     _check(library().ufb_warp(feature.data_ptr(), flow.data_ptr(), n, c, h, w, out.data_ptr(), _stream(feature)))
     return out
+
+
+# ---------------------------------------------------------------- engine ----
+# Host-array wrappers of the model / codec / rANS entry points.  The engine owns
+# its device memory and CUDA stream; these calls take and return numpy arrays.
+
+import numpy as _np
+
+_DTYPE_CODES = {_np.dtype(_np.int16): 0, _np.dtype(_np.uint8): 1, _np.dtype(_np.int32): 2,
+                _np.dtype(_np.int8): 3, _np.dtype(_np.int64): 4}
+
+
+def _engine_lib():
+    L = library()
+    if getattr(L, "_engine_ready", False):
+        return L
+    vp, ci, i64, sz = C.c_void_p, C.c_int, C.c_int64, C.c_size_t
+    L.ufb_rans_create.restype = vp
+    L.ufb_rans_create.argtypes = [vp, ci, ci, vp, vp, ci, ci, vp]
+    L.ufb_rans_destroy.argtypes = [vp]
+    L.ufb_rans_encode.restype = i64
+    L.ufb_rans_encode.argtypes = [vp, ci, C.POINTER(vp), C.POINTER(sz), vp, sz, ci, ci, vp, sz]
+    L.ufb_rans_decode.argtypes = [vp, vp, sz, sz, ci, ci, vp, ci, C.POINTER(vp), C.POINTER(sz), C.POINTER(vp)]
+    L.ufb_model_create.restype = vp
+    L.ufb_model_create.argtypes = [ci, C.c_char_p, ci, C.POINTER(C.c_char_p), C.POINTER(ci), C.POINTER(ci),
+                                   C.POINTER(i64), C.POINTER(vp)]
+    L.ufb_model_destroy.argtypes = [vp]
+    L.ufb_model_run.argtypes = [vp, C.c_char_p, ci, C.POINTER(vp), C.POINTER(i64), C.c_char_p, ci, vp, i64,
+                                C.POINTER(i64)]
+    L.ufb_codec_create.restype = vp
+    L.ufb_codec_create.argtypes = [vp, ci]
+    L.ufb_codec_destroy.argtypes = [vp]
+    L.ufb_codec_set_skip_threshold.argtypes = [vp, C.c_double]
+    L.ufb_codec_clear_dpb.argtypes = [vp]
+    L.ufb_codec_add_ref_frames.argtypes = [vp, vp, ci, ci]
+    L.ufb_codec_decompress.argtypes = [vp, C.POINTER(vp), C.POINTER(sz), C.c_uint32, C.c_uint32, ci, ci, ci, vp, vp]
+    L.ufb_codec_compress.argtypes = [vp, vp, ci, ci, ci, ci, ci, vp, sz, C.POINTER(sz), vp]
+    L.ufb_codec_state.argtypes = [vp, ci, vp, i64, C.POINTER(i64)]
+    L.ufb_codec_host_seconds.restype = C.c_double
+    L.ufb_codec_host_seconds.argtypes = [vp]
+    L._engine_ready = True
+    return L
+
+
+def _c(a, dtype):
+    return _np.ascontiguousarray(a, dtype=dtype)
+
+
+class Rans:
+    """uf::EntropyEncoder / EntropyDecoder wire format (host)."""
+
+    def __init__(self, tables: dict):
+        L = self.L = _engine_lib()
+        self._t = [_c(tables[k], _np.int32) for k in ("tables.z_cdf", "tables.z_lengths", "tables.y_cdf",
+                                                       "tables.y_lengths")]
+        zc, zl, yc, yl = self._t
+        self.h = L.ufb_rans_create(zc.ctypes.data, zc.shape[0], zc.shape[1], zl.ctypes.data, yc.ctypes.data,
+                                   yc.shape[0], yc.shape[1], yl.ctypes.data)
+        if not self.h:
+            raise UfbError(-1, L.ufb_last_error().decode())
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.L.ufb_rans_destroy(self.h)
+            self.h = None
+
+    def encode(self, y_parts, z, z_offset, z_channels) -> bytes:
+        parts = [_c(p, _np.int16) for p in y_parts]
+        z = _c(z, _np.int8)
+        pp = (C.c_void_p * max(len(parts), 1))(*[p.ctypes.data for p in parts])
+        pl = (C.c_size_t * max(len(parts), 1))(*[p.size for p in parts])
+        n = self.L.ufb_rans_encode(self.h, len(parts), pp, pl, z.ctypes.data, z.size, z_offset, z_channels, None, 0)
+        if n < 0:
+            raise UfbError(int(n), self.L.ufb_last_error().decode())
+        out = _np.empty(n, _np.uint8)
+        self.L.ufb_rans_encode(self.h, len(parts), pp, pl, z.ctypes.data, z.size, z_offset, z_channels,
+                               out.ctypes.data, n)
+        return out.tobytes()
+
+    def decode(self, payload: bytes, z_count, z_offset, z_channels, index_parts):
+        data = _np.frombuffer(payload, _np.uint8).copy()
+        z = _np.empty(z_count, _np.int8)
+        idx = [_c(i, _np.uint8) for i in index_parts]
+        ys = [_np.empty(i.size, _np.int8) for i in idx]
+        ip = (C.c_void_p * max(len(idx), 1))(*[i.ctypes.data for i in idx])
+        il = (C.c_size_t * max(len(idx), 1))(*[i.size for i in idx])
+        yp = (C.c_void_p * max(len(ys), 1))(*[y.ctypes.data for y in ys])
+        _check(self.L.ufb_rans_decode(self.h, data.ctypes.data, data.size, z_count, z_offset, z_channels,
+                                      z.ctypes.data, len(idx), ip, il, yp))
+        return z, ys
+
+
+class Model:
+    """A prepared model resident on one GPU (uf::Layers + tables)."""
+
+    def __init__(self, variant: str, tensors: dict, device: int = 0):
+        L = self.L = _engine_lib()
+        names = sorted(tensors)
+        arrays = [_np.ascontiguousarray(tensors[n]) for n in names]
+        c_names = (C.c_char_p * len(names))(*[n.encode() for n in names])
+        dtypes = (C.c_int * len(names))(*[_DTYPE_CODES[a.dtype] for a in arrays])
+        ndims = (C.c_int * len(names))(*[a.ndim for a in arrays])
+        flat = [int(s) for a in arrays for s in a.shape]
+        shapes = (C.c_int64 * max(len(flat), 1))(*flat)
+        data = (C.c_void_p * len(names))(*[a.ctypes.data for a in arrays])
+        self.variant = variant
+        self.h = L.ufb_model_create(device, variant.encode(), len(names), c_names, dtypes, ndims, shapes, data)
+        if not self.h:
+            raise UfbError(-1, L.ufb_last_error().decode())
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.L.ufb_model_destroy(self.h)
+            self.h = None
+
+    def run(self, module, *args, q_name=None, qp=0):
+        vs = [_c(a, _np.int16) for a in args]
+        arr = (C.c_void_p * len(vs))(*[v.ctypes.data for v in vs])
+        shapes = (C.c_int64 * (4 * len(vs)))(*[int(s) for v in vs for s in v.shape])
+        cap = 1 << 26
+        out = _np.empty(cap, _np.int16)
+        shape = (C.c_int64 * 4)()
+        _check(self.L.ufb_model_run(self.h, module.encode(), len(vs), arr, shapes,
+                                    q_name.encode() if q_name else None, qp, out.ctypes.data, cap, shape))
+        return out[: int(_np.prod(list(shape)))].reshape(tuple(shape)).copy()
+
+
+class Codec:
+    """uf::IntegerModel for `batch` streams decoded together on the model's GPU."""
+
+    def __init__(self, model: Model, batch: int = 1):
+        L = self.L = _engine_lib()
+        self.model, self.batch = model, batch
+        self.h = L.ufb_codec_create(model.h, batch)
+        if not self.h:
+            raise UfbError(-1, L.ufb_last_error().decode())
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.L.ufb_codec_destroy(self.h)
+            self.h = None
+
+    def set_skip_threshold(self, t):
+        _check(self.L.ufb_codec_set_skip_threshold(self.h, float(t)))
+
+    def clear_dpb(self):
+        _check(self.L.ufb_codec_clear_dpb(self.h))
+
+    def add_ref_frames(self, frames):
+        f = _c(frames, _np.int16)
+        _check(self.L.ufb_codec_add_ref_frames(self.h, f.ctypes.data, f.shape[-2], f.shape[-1]))
+
+    def decompress(self, payloads, width, height, qp, reset=False, frames=True, yuv=False):
+        bufs = [_np.frombuffer(p, _np.uint8).copy() if len(p) else _np.zeros(1, _np.uint8) for p in payloads]
+        ptrs = (C.c_void_p * self.batch)(*[b.ctypes.data for b in bufs])
+        lens = (C.c_size_t * self.batch)(*[len(p) for p in payloads])
+        F = 1 if self.model.variant == "image" else 8
+        hp, wp = (height + 15) // 16 * 16, (width + 15) // 16 * 16
+        fo = _np.empty((self.batch, F, 3, hp, wp), _np.int16) if frames else None
+        yo = _np.empty((self.batch, F, width * height * 3 // 2), _np.uint8) if yuv else None
+        rc = self.L.ufb_codec_decompress(self.h, ptrs, lens, width, height, qp, 1, int(reset),
+                                         fo.ctypes.data if frames else None, yo.ctypes.data if yuv else None)
+        if rc < 0:
+            _check(rc)
+        return fo, yo
+
+    def compress(self, frames_u8, qp, reset=False, frames=False):
+        x = _c(frames_u8, _np.uint8)
+        b, c, h, w = x.shape
+        cap = max(4096, c * h * w * 2)
+        out = _np.empty(self.batch * cap, _np.uint8)
+        lens = (C.c_size_t * self.batch)()
+        F = 1 if self.model.variant == "image" else 8
+        hp, wp = (h + 15) // 16 * 16, (w + 15) // 16 * 16
+        fo = _np.empty((self.batch, F, 3, hp, wp), _np.int16) if frames else None
+        rc = self.L.ufb_codec_compress(self.h, x.ctypes.data, c, h, w, qp, int(reset), out.ctypes.data, cap, lens,
+                                       fo.ctypes.data if frames else None)
+        if rc < 0:
+            _check(rc)
+        return [out[i * cap: i * cap + lens[i]].tobytes() for i in range(self.batch)], fo
+
+    def state(self, which):
+        idx = {"reference": 0, "memory": 1, "context": 2}[which]
+        cap = 1 << 26
+        out = _np.empty(cap, _np.int16)
+        shape = (C.c_int64 * 4)()
+        rc = self.L.ufb_codec_state(self.h, idx, out.ctypes.data, cap, shape)
+        if rc < 0:
+            _check(rc)
+        if rc == 1:
+            return None
+        return out[: int(_np.prod(list(shape)))].reshape(tuple(shape)).copy()
+
+    def host_seconds(self):
+        return self.L.ufb_codec_host_seconds(self.h)

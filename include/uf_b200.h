@@ -132,6 +132,99 @@ int ufb_conv2d_split(const uint8_t* x, int n, int ci, int h, int w, int x_pitch,
                      int kh, int kw, const void* bias, int bias_bits, int pad_h, int pad_w, uint8_t* out,
                      int out_pitch, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Host rANS coder (no GPU needed).  Same wire format as the reference's
+ * uf::EntropyEncoder / uf::EntropyDecoder (include/uf/entropy.hpp:12-46,
+ * src/entropy.cpp:63-247): Y parts encoded last-first then Z, flushed as the
+ * final state followed by the emitted bytes reversed; decode runs Z first,
+ * then the Y parts in order.  CDF tables are the prepared model's
+ * tables.{z,y}_cdf ([rows, width] int32) and tables.{z,y}_lengths.
+ * ------------------------------------------------------------------------- */
+typedef struct ufb_rans ufb_rans;
+
+ufb_rans* ufb_rans_create(const int32_t* z_cdf, int z_rows, int z_width, const int32_t* z_len, const int32_t* y_cdf,
+                          int y_rows, int y_width, const int32_t* y_len);
+void ufb_rans_destroy(ufb_rans* r);
+
+/* Encode Y parts (packed (symbol << 8) | cdf_index int16, EntropyEncoder::encode_y)
+ * and Z symbols (NHWC int8, row z_offset + i % z_channels, encode_z) into one
+ * stream (reset, parts last-first, Z, flush).  Returns the stream length (out
+ * may be NULL to query it) or a negative UFB_E* code. */
+int64_t ufb_rans_encode(ufb_rans* r, int nparts, const int16_t* const* parts, const size_t* part_lens,
+                        const int8_t* z, size_t zn, int z_offset, int z_channels, uint8_t* out, size_t capacity);
+
+/* Decode zn Z symbols, then each Y part's symbols from its CDF indexes
+ * (EntropyDecoder::set_stream / decode_z / decode_y).  Corrupt or truncated
+ * streams return UFB_ESTREAM with the reference's message. */
+int ufb_rans_decode(ufb_rans* r, const uint8_t* data, size_t n, size_t zn, int z_offset, int z_channels,
+                    int8_t* z_out, int nparts, const uint8_t* const* indexes, const size_t* index_lens,
+                    int8_t* const* y_out);
+
+/* ---------------------------------------------------------------------------
+ * Model and codec (the reference's uf::Layers / uf::IntegerModel,
+ * include/uf/layers.hpp:36-49 and include/uf/integer_model.hpp:19-73).
+ * ------------------------------------------------------------------------- */
+typedef struct ufb_model ufb_model;
+typedef struct ufb_codec ufb_codec;
+
+/* Upload a prepared model (uf::PreparedModel::tensors, include/uf/prepared.hpp:12-21)
+ * to `device`: `count` host tensors with names, dtype codes (0 int16, 1 uint8,
+ * 2 int32, 3 int8, 4 int64), ranks, concatenated shapes and host data.
+ * variant: "htl" or "image" (the layer topology is derived from tensor
+ * names as src/layers.cpp does).  The caller may free the host data on
+ * return.  NULL on failure (see ufb_last_error). */
+ufb_model* ufb_model_create(int device, const char* variant, int count, const char* const* names, const int* dtypes,
+                            const int* ndims, const int64_t* shapes, const void* const* data);
+void ufb_model_destroy(ufb_model* m);
+
+/* uf::Layers::run(module, args) (src/layers.cpp:132-184) on host NCHW int16
+ * tensors (shapes: 4 per argument).  A QP-table argument of the reference
+ * (Layers::parameter(q_name, qp)) is named by q_name / qp.  "enc" / "dec" of
+ * the image model include their pixel (un)shuffle(8) as in the reference.
+ * The result is written to out (capacity elements), its shape to out_shape. */
+int ufb_model_run(ufb_model* m, const char* module, int nargs, const int16_t* const* args, const int64_t* shapes,
+                  const char* q_name, int qp, int16_t* out, int64_t capacity, int64_t* out_shape);
+
+/* A codec holds the decoded-picture buffer (reference / memory / context) of
+ * `batch` independent streams that are decoded together; every stream of a
+ * batch shares the model, packet QP and reset flag, and has its own payload. */
+ufb_codec* ufb_codec_create(ufb_model* model, int batch);
+void ufb_codec_destroy(ufb_codec* c);
+
+/* IntegerModel::set_skip_threshold: trunc(t * 512 + 0.5) must lie in [0, 32767]. */
+int ufb_codec_set_skip_threshold(ufb_codec* c, double threshold);
+
+/* IntegerModel::clear_dpb. */
+int ufb_codec_clear_dpb(ufb_codec* c);
+
+/* IntegerModel::add_ref_feature_from_frame: frames host int16 [batch][3][h][w]. */
+int ufb_codec_add_ref_frames(ufb_codec* c, const int16_t* frames, int height, int width);
+
+/* IntegerModel::decompress for every stream (src/integer_model.cpp:336-359).
+ * frames_out: host int16 [batch][F][3][Hp][Wp] (Hp, Wp = height, width padded
+ * to 16) or NULL; yuv_out: host uint8 [batch][F][width*height*3/2] YUV420
+ * (IntegerCodec::raw_frame, src/integer_codec.cpp:294-323) or NULL.
+ * Returns F (8 for a video model, 1 for the image model) or a UFB_E* code. */
+int ufb_codec_decompress(ufb_codec* c, const uint8_t* const* payloads, const size_t* lengths, uint32_t width,
+                         uint32_t height, int qp, int entropy_parallel, int reset, int16_t* frames_out,
+                         uint8_t* yuv_out);
+
+/* IntegerModel::compress (src/integer_model.cpp:312-334) with the frame
+ * conversion of IntegerCodec::frame_tensor fused: frames host uint8 YUV444
+ * [batch][channels][height][width] (channels = 3 per frame).  Each stream's
+ * payload is written at payload_out + b * capacity, its length to lengths[b].
+ * frames_out (optional) receives the reconstruction as in decompress.
+ * Returns the number of reconstructed frames or a UFB_E* code. */
+int ufb_codec_compress(ufb_codec* c, const uint8_t* frames, int channels, int height, int width, int qp, int reset,
+                       uint8_t* payload_out, size_t capacity, size_t* lengths, int16_t* frames_out);
+
+/* DPB state views (IntegerModel::reference/memory/context): which 0, 1, 2.
+ * Writes NCHW int16 and its shape; returns 1 when the state is undefined. */
+int ufb_codec_state(ufb_codec* c, int which, int16_t* out, int64_t capacity, int64_t* shape4);
+
+/* Seconds the last decompress/compress spent in host entropy coding. */
+double ufb_codec_host_seconds(ufb_codec* c);
+
 /* Measurement utility (no reference counterpart): launches `ctas` CTAs that
  * each issue `iters` x 4 dense tcgen05 kind::i8 M=128 N=256 K=32 MMAs from
  * resident shared-memory tiles; *int8_ops receives the operation count

@@ -1,0 +1,208 @@
+"""GPU parity of the model engine against the reference's own CPU path.
+
+The reference's uf::Layers / uf::IntegerModel (oracle/_ref, compiled from its
+sources) and the engine run the same seeded prepared models on the same
+inputs; every module output, bitstream byte, reconstructed frame and DPB
+state must be identical.  Sizes are small so the CPU reference finishes in
+seconds (64x64 frames: latent 4x4, features 8x8).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+W, H = 64, 64
+
+
+@pytest.fixture(scope="module")
+def models(ufb, ref, syn, dev):
+    img_t, vid_t = syn.prepared("image", 1), syn.prepared("htl", 2)
+    return {
+        "image": (ufb.Model("image", img_t), ref.model("image", img_t)),
+        "htl": (ufb.Model("htl", vid_t), ref.model("htl", vid_t)),
+    }
+
+
+def rnd(rng, shape, lo=-3000, hi=3000):
+    return rng.integers(lo, hi, shape).astype(np.int16)
+
+
+@pytest.mark.parametrize("module,shapes,q", [
+    ("feature_adaptor_i", [(1, 192, 8, 8)], None),
+    ("feature_adaptor_m", [(1, 512, 8, 8), (1, 512, 8, 8)], None),
+    ("feature_extractor", [(1, 512, 8, 10)], None),
+    ("hyper_decoder", [(1, 128, 2, 3)], None),
+    ("temporal_prior_encoder", [(1, 512, 8, 12)], "q_feature"),
+    ("y_prior_fusion", [(1, 256, 4, 6), (1, 512, 4, 6)], None),
+    ("y_spatial_prior_reduction", [(1, 768, 4, 5)], None),
+    ("y_spatial_prior_adaptor_2", [(1, 512, 4, 4)], None),
+    ("y_spatial_prior", [(1, 512, 3, 5)], None),
+    ("decoder", [(1, 256, 4, 4), (1, 512, 8, 8)], "q_decoder"),
+    ("recon_head.conv.3", [(1, 512, 8, 8)], None),
+    ("hyper_encoder", [(1, 256, 8, 8)], None),
+])
+def test_htl_module_parity(models, module, shapes, q):
+    mine, theirs = models["htl"]
+    rng = np.random.default_rng(abs(hash(module)) % 1000)
+    args = [rnd(rng, s) for s in shapes]
+    qp = 20
+    want = theirs.run(module, *(args + ([theirs.parameter(q, qp)] if q else [])))
+    got = mine.run(module, *args, q_name=q, qp=qp)
+    assert got.shape == want.shape
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("module,shapes,q", [
+    ("hyper_dec", [(1, 128, 2, 2)], None),
+    ("y_prior_fusion", [(1, 256, 4, 4)], None),
+    ("y_spatial_prior", [(1, 512, 4, 4)], None),
+    ("dec", [(1, 256, 4, 4)], "q_scale_dec"),
+    ("enc", [(1, 3, 64, 64)], "q_scale_enc"),
+])
+def test_image_module_parity(models, module, shapes, q):
+    mine, theirs = models["image"]
+    rng = np.random.default_rng(7)
+    args = [rnd(rng, s) for s in shapes]
+    qp = 36
+    want = theirs.run(module, *(args + ([theirs.parameter(q, qp)] if q else [])))
+    got = mine.run(module, *args, q_name=q, qp=qp)
+    assert got.shape == want.shape
+    assert np.array_equal(got, want)
+
+
+def _frames(syn, count, w=W, h=H, seed=3):
+    return syn.synthetic_video(w, h, count, seed)
+
+
+def _same_states(codec, refm):
+    for k in ("reference", "memory", "context"):
+        a, b = codec.state(k), refm.state(k)
+        assert (a is None) == (b is None), k
+        if a is not None:
+            assert np.array_equal(a, b), k
+
+
+@pytest.mark.parametrize("skip", [0.2, 0.0])
+def test_image_compress_decompress_parity(ufb, ora, ref, syn, models, skip):
+    mine, _ = models["image"]
+    img_t = syn.prepared("image", 1)
+    video = _frames(syn, 1)
+    chunk = syn.frames_to_chunk(video[:1])
+    r = ref.model("image", img_t)
+    r.set_skip_threshold(skip)
+    want_payload, want_frames = r.compress(ora.from_bytes(chunk), 0)
+    c = ufb.Codec(mine, 1)
+    c.set_skip_threshold(skip)
+    payloads, frames = c.compress(chunk, 0, frames=True)
+    assert payloads[0] == want_payload
+    assert np.array_equal(frames[0, 0], want_frames[0][0])
+    got, _ = c.decompress([want_payload], W, H, 0)
+    r2 = ref.model("image", img_t)
+    r2.set_skip_threshold(skip)
+    dec = r2.decompress(want_payload, W, H, 0)
+    assert np.array_equal(got[0, 0], dec[0][0])
+
+
+@pytest.mark.parametrize("reset", [True, False])
+def test_video_p_packet_parity(ufb, ora, ref, syn, models, reset):
+    mine, _ = models["htl"]
+    vid_t = syn.prepared("htl", 2)
+    video = _frames(syn, 17)
+    iframe = ora.from_bytes(syn.frames_to_chunk(video[:1]))
+    # the I frame reconstruction from the reference image path seeds both DPBs
+    ri = ref.model("image", syn.prepared("image", 1))
+    ri.set_skip_threshold(0.2)
+    _, rec = ri.compress(iframe, 0)
+    ref_frame = rec[0]
+    enc_ref = ref.model("htl", vid_t)
+    enc_ref.set_skip_threshold(0.2)
+    enc_ref.add_ref_feature_from_frame(ref_frame)
+    enc = ufb.Codec(mine, 1)
+    enc.set_skip_threshold(0.2)
+    enc.add_ref_frames(ref_frame)
+    for packet in range(2):
+        chunk = syn.frames_to_chunk(video[1 + 8 * packet: 9 + 8 * packet])
+        want_payload, _ = enc_ref.compress(ora.from_bytes(chunk), 20, reset)
+        got_payloads, _ = enc.compress(chunk, 20, reset)
+        assert got_payloads[0] == want_payload, f"packet {packet}"
+        _same_states(enc, enc_ref)
+    # decode the reference's stream with a fresh engine codec
+    dec_ref = ref.model("htl", vid_t)
+    dec_ref.set_skip_threshold(0.2)
+    dec_ref.add_ref_feature_from_frame(ref_frame)
+    dec = ufb.Codec(mine, 1)
+    dec.set_skip_threshold(0.2)
+    dec.add_ref_frames(ref_frame)
+    chunk = syn.frames_to_chunk(video[1:9])
+    enc_ref2 = ref.model("htl", vid_t)
+    enc_ref2.set_skip_threshold(0.2)
+    enc_ref2.add_ref_feature_from_frame(ref_frame)
+    payload, _ = enc_ref2.compress(ora.from_bytes(chunk), 20, reset)
+    want = dec_ref.decompress(payload, W, H, 20, reset)
+    got, yuv = dec.decompress([payload], W, H, 20, reset, frames=True, yuv=True)
+    assert len(want) == 8
+    for f in range(8):
+        assert np.array_equal(got[0, f], want[f][0]), f"frame {f}"
+        assert np.array_equal(yuv[0, f], ora.raw_frame(want[f][0], H, W)), f"yuv {f}"
+    _same_states(dec, dec_ref)
+
+
+def test_batched_streams_match_single(ufb, ora, ref, syn, models):
+    """Two independent streams decoded as one batch equal two single decodes."""
+    mine, _ = models["htl"]
+    vid_t = syn.prepared("htl", 2)
+    payloads, refs = [], []
+    for s in range(2):
+        video = _frames(syn, 9, seed=40 + s)
+        frame0 = ora.from_bytes(syn.frames_to_chunk(video[:1]))
+        e = ref.model("htl", vid_t)
+        e.set_skip_threshold(0.2)
+        e.add_ref_feature_from_frame(frame0)
+        p, _ = e.compress(ora.from_bytes(syn.frames_to_chunk(video[1:9])), 20, True)
+        payloads.append(p)
+        refs.append(frame0)
+    batch = ufb.Codec(mine, 2)
+    batch.set_skip_threshold(0.2)
+    batch.add_ref_frames(np.concatenate(refs, 0))
+    got, _ = batch.decompress(payloads, W, H, 20, True)
+    for s in range(2):
+        one = ufb.Codec(mine, 1)
+        one.set_skip_threshold(0.2)
+        one.add_ref_frames(refs[s])
+        single, _ = one.decompress([payloads[s]], W, H, 20, True)
+        assert np.array_equal(got[s], single[0])
+
+
+def test_odd_size_padding(ufb, ora, ref, syn, models):
+    """Width/height not multiples of 16: replicate padding and raw-frame crop."""
+    mine, _ = models["htl"]
+    vid_t = syn.prepared("htl", 2)
+    w, h = 72, 40
+    video = _frames(syn, 9, w=w, h=h, seed=9)
+    frame0 = ora.from_bytes(syn.frames_to_chunk(video[:1]))
+    frame0 = np.pad(frame0, ((0, 0), (0, 0), (0, 8), (0, 8)), mode="edge")  # reference frames are padded
+    e = ref.model("htl", vid_t)
+    e.set_skip_threshold(0.2)
+    e.add_ref_feature_from_frame(frame0)
+    want_payload, _ = e.compress(ora.from_bytes(syn.frames_to_chunk(video[1:9])), 30, False)
+    c = ufb.Codec(mine, 1)
+    c.set_skip_threshold(0.2)
+    c.add_ref_frames(frame0)
+    got_payloads, _ = c.compress(syn.frames_to_chunk(video[1:9]), 30, False)
+    assert got_payloads[0] == want_payload
+
+
+def test_truncated_payload_raises(ufb, syn, models):
+    mine, _ = models["htl"]
+    c = ufb.Codec(mine, 1)
+    c.add_ref_frames(np.zeros((1, 3, H, W), np.int16))
+    with pytest.raises(ufb.UfbError):
+        c.decompress([b"\x00\x00\x80\x00\x01"], W, H, 20, False)
+
+
+def test_p_frame_without_reference_raises(ufb, models):
+    mine, _ = models["htl"]
+    c = ufb.Codec(mine, 1)
+    with pytest.raises(ufb.UfbError) as e:
+        c.decompress([b"\x00\x00\x80\x00"], W, H, 20, False)
+    assert "no reference" in str(e.value)
