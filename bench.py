@@ -3,21 +3,28 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload W]
 
 Workloads
-  conv    BASELINE config 1 batched: 64 copies of the 1x64x88x160 int16 3x3
-          conv (weights U[-256,256], int32 bias U[-2^16,2^16], pad 1, seed 0);
-          one step = one launch over all copies.  Unit: int16 MAC/s.
+  decode  (default) BASELINE config 5: 64 independent seeded synthetic 1920x1088
+          sequences of 32 frames (config-4 scene generator, seeds 100..163), each
+          coded as 1 I packet (qp_i 0) + 4 P packets of 8 frames (qp_p 20,
+          reset_interval 8 -> every P packet resets, skip 0.2), sharded
+          64/N streams per GPU with no inter-GPU communication.  One step decodes
+          every sequence of the rank completely (I packet, then the 4 P packets),
+          host rANS included.  Unit: decoded frames/s (whole job).
+  conv    BASELINE config 1 batched: 64 copies of the 1x64x88x160 int16 3x3 conv.
 
-Timing follows the driver contract: W untimed warm-up steps, then K steps
-bracketed by a barrier and torch.cuda.synchronize(), device time from CUDA
-events on the launching stream, max over ranks.  Inputs are larger than L2
-(126 MB), so no flush is needed between steps.  `value` has inputs resident
-in HBM; `e2e` goes through the public C ABI with host buffers: each step
-copies its input from pinned host memory, runs ufb_conv2d (NCHW, as the
-reference's uf_conv) and copies the result back.
+Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
+torch.cuda.synchronize(), device time from CUDA events on the stream the
+engine launches on, max over ranks.  The decoder's working set per step is
+several GB (far above the 126 MB L2).  `value` leaves decoded frames in HBM;
+`e2e` decodes through the same public C ABI and also converts every frame to
+8-bit YUV420 (IntegerCodec::raw_frame) and copies it to pinned host memory.
+Payloads always start in host memory (the entropy decoder runs on the host,
+as in the reference).
 
---impl reference times the reference's own CPU INT16 path (oracle/_ref,
-compiled from the reference sources) on the same workload, as a bounded
-sample per step, using all host threads.
+--impl reference times the reference's own CPU INT16 decoder
+(IntegerModel::decompress from oracle/_ref, compiled from the reference
+sources) with all host threads on a bounded sample -- one P packet and one I
+packet at 128x128 -- and extrapolates to the workload by pixel count.
 """
 from __future__ import annotations
 
@@ -36,28 +43,31 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-CONV_BATCH = 64  # copies of the config-1 conv per step
+CONV_BATCH = 64
+SEQS, FRAMES, W1080, H1080 = 64, 32, 1920, 1088
+QP_I, QP_P, SKIP = 0, 20, 0.2
+SAMPLE = 128  # reference sample resolution (pixels per side)
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=10)
-    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--steps", type=int, default=2)
+    p.add_argument("--warmup", type=int, default=1)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--workload", default="conv", choices=["conv"])
+    p.add_argument("--workload", default="decode", choices=["decode", "conv"])
     return p.parse_args()
 
 
 class Clocks:
-    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+    """Samples nvidia-smi SM clocks and throttle reasons while the GPU is loaded."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpus):
-        self.gpus = gpus
+    def __init__(self, index):
+        self.index = index
         self.rows = []
         self._stop = threading.Event()
         self._t = None
@@ -65,11 +75,12 @@ class Clocks:
     def _run(self):
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
-                                     capture_output=True, text=True, timeout=5).stdout
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout
                 for line in out.strip().splitlines():
                     f = [x.strip() for x in line.split(",")]
-                    if len(f) >= 9 and int(f[0]) < self.gpus:
+                    if len(f) >= 9:
                         self.rows.append(f)
             except Exception:
                 pass
@@ -86,7 +97,7 @@ class Clocks:
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         sm = [float(r[1]) for r in self.rows]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower() == "active"})
@@ -94,11 +105,9 @@ class Clocks:
                 "samples": len(self.rows)}
 
 
-def dist_setup(n_gpus):
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return rank, world, local
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
 
 
 def barrier(world):
@@ -107,22 +116,14 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(value, world, device):
+def reduce_over_ranks(value, world, device, op):
     if world == 1:
         return value
     import torch
     import torch.distributed as dist
     t = torch.tensor([value], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
     return float(t.item())
-
-
-def conv_inputs(seed=0):
-    rng = np.random.default_rng(seed)
-    x = rng.integers(-4096, 4097, (CONV_BATCH, 64, 88, 160)).astype(np.int16)
-    w = rng.integers(-256, 257, (64, 64, 3, 3)).astype(np.int16)
-    b = rng.integers(-(1 << 16), (1 << 16) + 1, (64,)).astype(np.int32)
-    return x, w, b
 
 
 def load_traffic(key):
@@ -132,14 +133,225 @@ def load_traffic(key):
     return None
 
 
-# ------------------------------------------------------------------ ours ----
+def i8_peak_tops(L, stream):
+    """int8 tensor-pipe peak measured live with the dense kind::i8 probe."""
+    import torch
+    L.ufb_probe_i8_peak.argtypes = [C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_int64)]
+    sp = C.c_void_p(stream.cuda_stream)
+    ops = C.c_int64()
+    for _ in range(2):
+        L.ufb_probe_i8_peak(4000, 148, sp, C.byref(ops))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    L.ufb_probe_i8_peak(4000, 148, sp, C.byref(ops))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return ops.value / (e0.elapsed_time(e1) * 1e-3) / 1e12
+
+
+# --------------------------------------------------------------- decode ----
+
+def shard(rank, world):
+    per = SEQS // world
+    return list(range(rank * per, (rank + 1) * per))
+
+
+def encode_sequences(ufb, syn, mi, mv, seqs, batch, dev):
+    """Seeded synthetic sequences coded by this engine's encoder (untimed
+    setup).  Per group of streams: ids, I payloads, the I-frame reconstruction
+    of the encoder, 4 lists of P payloads and their reset flags."""
+    import torch
+    groups = []
+    for g0 in range(0, len(seqs), batch):
+        ids = seqs[g0:g0 + batch]
+        video = torch.stack([syn.synthetic_video_gpu(W1080, H1080, FRAMES, 100 + s, dev) for s in ids])
+        ci = ufb.Codec(mi, len(ids))
+        ci.set_skip_threshold(SKIP)
+        cv = ufb.Codec(mv, len(ids))
+        cv.set_skip_threshold(SKIP)
+        i_pay, i_rec = ci.compress(video[:, 0].cpu().numpy(), QP_I, frames=True)
+        cv.set_reference_from(ci)
+        p_pays, resets = [], []
+        count = 1
+        for k in range(4):
+            chunk = video[:, 1 + 8 * k: 9 + 8 * k]
+            if chunk.shape[1] < 8:  # pad by repeating the last frame (src/integer_codec.cpp:257-261)
+                chunk = torch.cat([chunk] + [chunk[:, -1:]] * (8 - chunk.shape[1]), 1)
+            reset = (count + 8) % 8 == 1  # reset_interval 8 (src/integer_codec.cpp:263-264)
+            pay, _ = cv.compress(chunk.reshape(len(ids), 24, H1080, W1080).cpu().numpy(), QP_P, reset)
+            p_pays.append(pay)
+            resets.append(reset)
+            count += 8
+        groups.append((ids, i_pay, i_rec if g0 == 0 else None, p_pays, resets))
+        del video
+    return groups
+
+
+def bench_decode_ours(args, rank, world, local):
+    import torch
+    import __graft_entry__ as entry
+    ufb = entry.load_package()
+    syn = entry.load_synthetic()
+    L = ufb.library()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    seqs = shard(rank, world)
+    batch = min(32, len(seqs))
+    mi = ufb.Model("image", syn.prepared("image", 1), device=local)
+    mv = ufb.Model("htl", syn.prepared("htl", 2), device=local)
+    groups = encode_sequences(ufb, syn, mi, mv, seqs, batch, dev)
+    peak = i8_peak_tops(L, stream)
+
+    decoders = []
+    for ids, *_ in groups:
+        di, dv = ufb.Codec(mi, len(ids)), ufb.Codec(mv, len(ids))
+        for c in (di, dv):
+            c.set_skip_threshold(SKIP)
+            c.set_stream(stream)
+        decoders.append((di, dv))
+
+    def step(yuv):
+        """Decode every sequence of this rank: I packet, then 4 P packets."""
+        frames = 0
+        for (ids, i_pay, _, p_pays, resets), (di, dv) in zip(groups, decoders):
+            di.decompress(i_pay, W1080, H1080, QP_I, frames=False, yuv=yuv)
+            dv.set_reference_from(di)
+            frames += len(ids)
+            for k in range(4):
+                dv.decompress(p_pays[k], W1080, H1080, QP_P, resets[k], frames=False, yuv=yuv)
+                frames += len(ids) * (8 if k < 3 else FRAMES - 1 - 24)
+        return frames
+
+    def timed(yuv, steps):
+        for pair in decoders:
+            for c in pair:
+                c.stats(reset=True)
+                c.profile(True)
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        frames = sum(step(yuv) for _ in range(steps))
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        st = {"launches": 0, "conv_launches": 0, "conv_int16_macs": 0.0, "conv_ms": 0.0}
+        for pair in decoders:
+            for c in pair:
+                s = c.stats()
+                c.profile(False)
+                for k in st:
+                    st[k] += s[k]
+        return frames, e0.elapsed_time(e1), st
+
+    with Clocks(local) as clk:
+        for _ in range(args.warmup):
+            step(False)
+        torch.cuda.synchronize()
+        frames, ms, st = timed(False, args.steps)
+    clocks = clk.summary()
+    ms_max = reduce_over_ranks(ms, world, dev, "max")
+    total_frames = reduce_over_ranks(frames, world, dev, "sum")
+
+    # integrity check: decoding reproduces the encoder-side reconstruction
+    _, i_pay, i_rec, _, _ = groups[0]
+    got_i, _ = decoders[0][0].decompress(i_pay, W1080, H1080, QP_I, frames=True)
+    if not np.array_equal(got_i, i_rec):
+        raise RuntimeError("I-packet decode differs from the encoder reconstruction")
+
+    e2e_frames, e2e_ms, _ = timed(True, 1)
+    e2e_ms = reduce_over_ranks(e2e_ms, world, dev, "max")
+    e2e_total = reduce_over_ranks(e2e_frames, world, dev, "sum")
+    h2d = sum(len(p) for g in groups for p in list(g[1]) + [x for pp in g[3] for x in pp])
+    d2h = len(seqs) * 33 * W1080 * H1080 * 3 // 2  # every decoded frame (incl. the padding frame) as YUV420
+
+    per_step_ms = ms / args.steps
+    achieved = 8 * st["conv_int16_macs"] / (st["conv_ms"] * 1e-3) / 1e12 if st["conv_ms"] else None
+    return {
+        "metric": "INT16 HT-L decoded frames/s (1920x1088, BASELINE config 5)",
+        "value": total_frames / (ms_max * 1e-3), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int16 (int8 tensor planes, s32 accumulators, int64 recombination)",
+        "data": "synthetic (seeded scene generator, seeded random-init HT-L + image models)",
+        "config": {"workload": "config 5: 64 seqs x 32 frames 1920x1088, I + 4 P packets each, qp_i 0 qp_p 20, "
+                               "reset 8, skip 0.2", "streams_per_gpu": len(seqs), "codec_batch": batch,
+                   "l2": "working set per step several GB, far above L2",
+                   "parallelism": f"stream sharding x{world}, no inter-GPU communication"},
+        "gpu_launches": int(st["launches"]),
+        "clocks": clocks,
+        "roofline": {"bound": "tensor", "kernel": "conv_i16_tc_kernel (all tensor-core convolution launches)",
+                     "achieved": achieved, "peak": peak, "unit": "TOPS(int8)",
+                     "frac": achieved / peak if achieved else None,
+                     "traffic": load_traffic("decode_conv_per_launch"),
+                     "peak_source": "measured live: dense tcgen05 kind::i8 probe (ufb_probe_i8_peak)",
+                     "algorithmic": "8 int8 ops per int16 MAC",
+                     "conv_share_of_step": (st["conv_ms"] / args.steps) / per_step_ms if ms else None,
+                     "conv_launches_per_step": st["conv_launches"] / args.steps,
+                     "conv_int16_macs_per_step": st["conv_int16_macs"] / args.steps},
+        "e2e": {"value": e2e_total / (e2e_ms * 1e-3), "unit": "frames/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+    }
+
+
+def ref_decode_sample(threads):
+    """Reference IntegerModel::decompress (oracle/_ref) on a 128x128 sample;
+    returns (seconds per P packet, seconds per I packet)."""
+    import oracle
+    import __graft_entry__ as entry
+    syn = entry.load_synthetic()
+    ref = oracle.ref_oracle()
+    ora = oracle.c_oracle()
+    ref.set_threads(threads)
+    img_t, vid_t = syn.prepared("image", 1), syn.prepared("htl", 2)
+    video = syn.synthetic_video(SAMPLE, SAMPLE, 9, 100)
+    ri = ref.model("image", img_t)
+    ri.set_skip_threshold(SKIP)
+    i_pay, rec = ri.compress(ora.from_bytes(syn.frames_to_chunk(video[:1])), QP_I)
+    rv = ref.model("htl", vid_t)
+    rv.set_skip_threshold(SKIP)
+    rv.add_ref_feature_from_frame(rec[0])
+    p_pay, _ = rv.compress(ora.from_bytes(syn.frames_to_chunk(video[1:9])), QP_P, True)
+    di = ref.model("image", img_t)
+    di.set_skip_threshold(SKIP)
+    t0 = time.perf_counter()
+    frames = di.decompress(i_pay, SAMPLE, SAMPLE, QP_I)
+    t_i = time.perf_counter() - t0
+    dv = ref.model("htl", vid_t)
+    dv.set_skip_threshold(SKIP)
+    dv.add_ref_feature_from_frame(frames[0])
+    t0 = time.perf_counter()
+    dv.decompress(p_pay, SAMPLE, SAMPLE, QP_P, True)
+    t_p = time.perf_counter() - t0
+    return t_p, t_i
+
+
+def ref_fps_1080(t_p, t_i):
+    """Extrapolate the 128x128 sample to a 1920x1088 32-frame sequence by pixel count."""
+    seq_seconds = (t_i + 4 * t_p) * (W1080 * H1080) / (SAMPLE * SAMPLE)
+    return FRAMES / seq_seconds
+
+
+def ref_decode_note(t_p, t_i):
+    return (f"reference IntegerModel::decompress at {SAMPLE}x{SAMPLE}: P packet {t_p:.2f} s, I packet {t_i:.2f} s, "
+            f"extrapolated by pixel count to 1920x1088 sequences of 1 I + 4 P packets")
+
+
+# ----------------------------------------------------------------- conv ----
+
+def conv_inputs(seed=0):
+    rng = np.random.default_rng(seed)
+    x = rng.integers(-4096, 4097, (CONV_BATCH, 64, 88, 160)).astype(np.int16)
+    w = rng.integers(-256, 257, (64, 64, 3, 3)).astype(np.int16)
+    b = rng.integers(-(1 << 16), (1 << 16) + 1, (64,)).astype(np.int32)
+    return x, w, b
+
 
 def bench_conv_ours(args, rank, world, local):
     import torch
     import __graft_entry__ as entry
     ufb = entry.load_package()
     L = ufb.library()
-    L.ufb_probe_i8_peak.argtypes = [C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_int64)]
     L.ufb_prepare_weights.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
     L.ufb_weight_bytes.restype = C.c_int64
     L.ufb_weight_bytes.argtypes = [C.c_int] * 4
@@ -155,9 +367,7 @@ def bench_conv_ours(args, rank, world, local):
     x, w, b = conv_inputs(seed=rank)
     n, ci, h, wd = x.shape
     co = w.shape[0]
-    xd = torch.from_numpy(x).to(dev)
-    wdv = torch.from_numpy(w).to(dev)
-    bd = torch.from_numpy(b).to(dev)
+    xd, wdv, bd = torch.from_numpy(x).to(dev), torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev)
     xs = torch.empty(n * h * wd * 2 * ci, dtype=torch.uint8, device=dev)
     os_ = torch.empty(n * h * wd * 2 * co, dtype=torch.uint8, device=dev)
     planes = torch.empty(L.ufb_weight_bytes(co, ci, 3, 3), dtype=torch.uint8, device=dev)
@@ -170,21 +380,10 @@ def bench_conv_ours(args, rank, world, local):
         if rc:
             raise RuntimeError(L.ufb_last_error().decode())
 
-    # int8 tensor-pipe peak, measured live with the dense kind::i8 probe
-    ops = C.c_int64()
-    for _ in range(2):
-        L.ufb_probe_i8_peak(4000, 148, sp, C.byref(ops))
+    peak = i8_peak_tops(L, stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    L.ufb_probe_i8_peak(4000, 148, sp, C.byref(ops))
-    e1.record(stream)
-    torch.cuda.synchronize()
-    peak_tops = ops.value / (e0.elapsed_time(e1) * 1e-3) / 1e12
-
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # the sampler runs through warm-up and timed steps (a step lasts under 1 ms,
-    # shorter than one nvidia-smi query), so its samples see the same load
-    with Clocks(max(world, 1)) as clk:
+    # the sampler runs through warm-up and timed steps (a step is shorter than one query)
+    with Clocks(local) as clk:
         for _ in range(max(args.warmup, 3)):
             step()
         t_end = time.time() + 0.5
@@ -199,13 +398,8 @@ def bench_conv_ours(args, rank, world, local):
         e1.record(stream)
         torch.cuda.synchronize()
     barrier(world)
-    clocks = clk.summary()
     ms = e0.elapsed_time(e1) / args.steps
-    ms_max = max_over_ranks(ms, world, dev)
-    if ufb.device_status(local) != 0:
-        raise RuntimeError("kernel pipeline timeout")
-
-    # end to end through the public NCHW C ABI with host buffers
+    ms_max = reduce_over_ranks(ms, world, dev, "max")
     xh = torch.from_numpy(x).pin_memory()
     oh_ = torch.empty((n, co, h, wd), dtype=torch.int16).pin_memory()
     out_d = torch.empty((n, co, h, wd), dtype=torch.int16, device=dev)
@@ -228,82 +422,87 @@ def bench_conv_ours(args, rank, world, local):
         e2e_step()
     e3.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e2.elapsed_time(e3) / args.steps, world, dev)
-    # parity spot check of the last e2e output against the CPU checker (one image)
+    e2e_ms = reduce_over_ranks(e2.elapsed_time(e3) / args.steps, world, dev, "max")
     import oracle
-    want = oracle.c_oracle().conv2d(x[:1], w, b, 1, 1)
-    if not np.array_equal(oh_[:1].numpy(), want):
+    if not np.array_equal(oh_[:1].numpy(), oracle.c_oracle().conv2d(x[:1], w, b, 1, 1)):
         raise RuntimeError("bench output differs from the CPU oracle")
-
     macs = n * co * h * wd * ci * 9
-    value = world * macs / (ms_max * 1e-3)
-    achieved_tops = 8 * macs / (ms * 1e-3) / 1e12
-    res = {
+    achieved = 8 * macs / (ms * 1e-3) / 1e12
+    return {
         "metric": "INT16 3x3 conv int16-MAC/s (BASELINE config 1 shape, 64 copies per step)",
-        "value": value, "unit": "MAC/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int16 (int8 planes, s32 accumulators, int64 recombination)", "data": "synthetic (seeded)",
-        "config": {"workload": "config-1 conv 64x[1x64x88x160] 3x3 64->64 int32 bias, pad 1",
-                   "batch": CONV_BATCH, "l2": "inputs larger than L2 (115 MB in + 115 MB out per step)",
-                   "parallelism": f"replicas x{world}"},
-        "gpu_launches": args.steps,
-        "clocks": clocks,
-        "roofline": {"bound": "tensor", "achieved": achieved_tops, "peak": peak_tops, "unit": "TOPS(int8)",
-                     "frac": achieved_tops / peak_tops, "traffic": load_traffic("conv_config1_b64"),
-                     "peak_source": "measured live: dense tcgen05 kind::i8 probe (ufb_probe_i8_peak)",
-                     "algorithmic": "8 int8 ops per int16 MAC"},
-        "e2e": {"value": world * macs / (e2e_ms * 1e-3), "unit": "MAC/s",
-                "h2d_bytes_per_step": int(x.nbytes), "d2h_bytes_per_step": int(n * co * h * wd * 2)},
+        "value": world * macs / (ms_max * 1e-3), "unit": "MAC/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int16 (int8 planes, s32 accumulators, int64 recombination)",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "config-1 conv 64x[1x64x88x160] 3x3 64->64 int32 bias, pad 1", "batch": CONV_BATCH,
+                   "l2": "inputs larger than L2", "parallelism": f"replicas x{world}"},
+        "gpu_launches": args.steps, "clocks": clk.summary(),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS(int8)",
+                     "frac": achieved / peak, "traffic": load_traffic("conv_config1_b64"),
+                     "peak_source": "measured live: dense tcgen05 kind::i8 probe (ufb_probe_i8_peak)"},
+        "e2e": {"value": world * macs / (e2e_ms * 1e-3), "unit": "MAC/s", "h2d_bytes_per_step": int(x.nbytes),
+                "d2h_bytes_per_step": int(n * co * h * wd * 2)},
     }
-    return res
 
 
-def cpu_baseline_conv(threads):
-    """Reference conv2d_reference (oracle/_ref) on a bounded sample: 8 of the 64 copies."""
+def ref_conv(threads):
     import oracle
     ref = oracle.ref_oracle()
     ref.set_threads(threads)
     x, w, b = conv_inputs(0)
     sample = 8
-    ref.conv2d(x[:1], w, b, 1, 1)
     t0 = time.perf_counter()
     ref.conv2d(x[:sample], w, b, 1, 1)
     dt = time.perf_counter() - t0
-    macs = sample * 64 * 88 * 160 * 64 * 9
-    return {"value": macs / dt, "unit": "MAC/s", "cores": threads, "kind": "reference",
-            "sample": f"{sample} of {CONV_BATCH} config-1 convs through the reference conv2d_reference "
-                      f"({dt:.2f} s)"}
+    return sample * 64 * 88 * 160 * 64 * 9 / dt, f"{sample} of {CONV_BATCH} config-1 convs ({dt:.2f} s)"
 
+
+# ----------------------------------------------------------------- main ----
 
 def main():
     args = parse()
-    rank, world, local = dist_setup(args.gpus)
+    rank, world, local = dist_env()
+    threads = os.cpu_count() or 1
     if args.impl == "reference":
         if rank != 0:
             return
-        threads = os.cpu_count() or 1
-        base = cpu_baseline_conv(threads)
-        steps = []
-        for _ in range(args.steps):
-            steps.append(cpu_baseline_conv(threads)["value"])
-        value = statistics.median(steps)
+        if args.workload == "conv":
+            runs = [ref_conv(threads) for _ in range(max(args.steps, 1))]
+            value, unit, note = statistics.median(r[0] for r in runs), "MAC/s", runs[-1][1]
+            metric = "INT16 3x3 conv int16-MAC/s (BASELINE config 1 shape, 64 copies per step)"
+            cfg = "config-1 conv 64x[1x64x88x160] 3x3 64->64 int32 bias, pad 1"
+        else:
+            samples = [ref_decode_sample(threads) for _ in range(max(args.steps, 1))]
+            t_p = statistics.median(s[0] for s in samples)
+            t_i = statistics.median(s[1] for s in samples)
+            value, unit, note = ref_fps_1080(t_p, t_i), "frames/s", ref_decode_note(t_p, t_i)
+            metric = "INT16 HT-L decoded frames/s (1920x1088, BASELINE config 5)"
+            cfg = "config 5: 64 seqs x 32 frames 1920x1088, I + 4 P packets each, qp_i 0 qp_p 20, reset 8, skip 0.2"
         print(json.dumps({
-            "impl": "reference", "metric": "INT16 3x3 conv int16-MAC/s (BASELINE config 1 shape, 64 copies per step)",
-            "value": value, "unit": "MAC/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "dtype": "int16", "data": "synthetic (seeded)",
-            "config": {"workload": "config-1 conv 64x[1x64x88x160] 3x3 64->64 int32 bias, pad 1"},
-            "cpu_baseline": dict(base, value=value),
-            "e2e": {"value": value, "unit": "MAC/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+            "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "int16",
+            "data": "synthetic (seeded)", "config": {"workload": cfg},
+            "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "reference", "sample": note},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         return
     if world > 1:
         import torch
         import torch.distributed as dist
         from datetime import timedelta
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
-    res = bench_conv_ours(args, rank, world, local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+    if args.workload == "conv":
+        res = bench_conv_ours(args, rank, world, local)
+        if rank == 0 and world == 1:
+            v, note = ref_conv(1)
+            res["cpu_baseline"] = {"value": v, "unit": "MAC/s", "cores": 1, "kind": "reference", "sample": note}
+    else:
+        res = bench_decode_ours(args, rank, world, local)
+        if rank == 0 and world == 1:
+            t_p, t_i = ref_decode_sample(threads)
+            res["cpu_baseline"] = {"value": ref_fps_1080(t_p, t_i), "unit": "frames/s", "cores": threads,
+                                   "kind": "reference", "sample": ref_decode_note(t_p, t_i)}
     if rank == 0:
-        res["cpu_baseline"] = cpu_baseline_conv(1)
         print(json.dumps(res))
     if world > 1:
         import torch.distributed as dist

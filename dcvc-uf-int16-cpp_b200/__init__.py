@@ -208,6 +208,11 @@ def _engine_lib():
     L.ufb_codec_state.argtypes = [vp, ci, vp, i64, C.POINTER(i64)]
     L.ufb_codec_host_seconds.restype = C.c_double
     L.ufb_codec_host_seconds.argtypes = [vp]
+    L.ufb_codec_set_reference_from.argtypes = [vp, vp]
+    L.ufb_codec_set_stream.argtypes = [vp, vp]
+    L.ufb_codec_profile.argtypes = [vp, ci]
+    L.ufb_codec_stats.argtypes = [vp, ci, C.POINTER(i64), C.POINTER(i64), C.POINTER(C.c_double),
+                                  C.POINTER(C.c_double)]
     L._engine_ready = True
     return L
 
@@ -363,3 +368,20 @@ class Codec:
 
     def host_seconds(self):
         return self.L.ufb_codec_host_seconds(self.h)
+
+    def set_reference_from(self, image_codec: "Codec"):
+        _check(self.L.ufb_codec_set_reference_from(self.h, image_codec.h))
+
+    def set_stream(self, stream):
+        """stream: a torch.cuda.Stream, a raw handle, or None for the codec's own."""
+        handle = getattr(stream, "cuda_stream", stream)
+        _check(self.L.ufb_codec_set_stream(self.h, C.c_void_p(handle) if handle else None))
+
+    def profile(self, enable=True):
+        _check(self.L.ufb_codec_profile(self.h, int(enable)))
+
+    def stats(self, reset=False):
+        a, b = C.c_int64(), C.c_int64()
+        m, t = C.c_double(), C.c_double()
+        _check(self.L.ufb_codec_stats(self.h, int(reset), C.byref(a), C.byref(b), C.byref(m), C.byref(t)))
+        return {"launches": a.value, "conv_launches": b.value, "conv_int16_macs": m.value, "conv_ms": t.value}

@@ -228,4 +228,45 @@ int ufb_codec_state(ufb_codec* c, int which, int16_t* out, int64_t capacity, int
 
 double ufb_codec_host_seconds(ufb_codec* c) { return c ? c->c->last_host_seconds() : 0.0; }
 
+int ufb_codec_set_reference_from(ufb_codec* video, ufb_codec* image) {
+    return guarded([&] {
+        if (!video || !image) throw std::invalid_argument("codec is null");
+        video->c->set_reference_from(*image->c);
+        return 0;
+    });
+}
+
+int ufb_codec_set_stream(ufb_codec* c, void* stream) {
+    return guarded([&] {
+        if (!c) throw std::invalid_argument("codec is null");
+        c->c->set_stream(static_cast<cudaStream_t>(stream));
+        return 0;
+    });
+}
+
+int ufb_codec_profile(ufb_codec* c, int enable) {
+    return guarded([&] {
+        if (!c) throw std::invalid_argument("codec is null");
+        c->c->stats().profile = enable != 0;
+        return 0;
+    });
+}
+
+int ufb_codec_stats(ufb_codec* c, int reset, int64_t* launches, int64_t* conv_launches, double* conv_int16_macs,
+                    double* conv_ms) {
+    return guarded([&] {
+        if (!c) throw std::invalid_argument("codec is null");
+        EngineStats& st = c->c->stats();
+        if (launches) *launches = st.launches;
+        if (conv_launches) *conv_launches = st.conv_launches;
+        if (conv_int16_macs) *conv_int16_macs = st.conv_int16_macs;
+        if (conv_ms) *conv_ms = st.conv_ms;
+        if (reset) {
+            st.launches = st.conv_launches = 0;
+            st.conv_int16_macs = st.conv_ms = 0;
+        }
+        return 0;
+    });
+}
+
 }  // extern "C"

@@ -89,6 +89,24 @@ void* Pinned::get(size_t bytes) {
     return p_;
 }
 
+EngineStats::~EngineStats() {
+    for (auto& e : pending) {
+        cudaEventDestroy(e.first);
+        cudaEventDestroy(e.second);
+    }
+    for (auto e : spare) cudaEventDestroy(e);
+}
+
+void EngineStats::collect() {
+    for (auto& e : pending) {
+        float ms = 0;
+        if (cudaEventElapsedTime(&ms, e.first, e.second) == cudaSuccess) conv_ms += ms;
+        spare.push_back(e.first);
+        spare.push_back(e.second);
+    }
+    pending.clear();
+}
+
 // ----------------------------------------------------------------- model ----
 
 Model::Model(int device, const std::string& variant, const std::vector<HostTensor>& tensors)
@@ -238,6 +256,7 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
         if (L->kh != 3 || L->kw != 3 || stride != 1 || f.lut || f.wsilu4 || f.shuffle2 || f.res1 || f.mulq)
             throw std::invalid_argument("unsupported depthwise configuration in " + name);
         ck(dwconv3x3(in.a, out.a, L->weights16, L->bias, s_), "depthwise conv");
+        count();
         return out;
     }
     if (stride == 1 && L->tc.planes) {
@@ -251,8 +270,29 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
         if (f.res2) e.res2 = f.res2->a;
         e.mulq = f.mulq;
         std::string err;
+        cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+        if (stats_ && stats_->profile) {
+            for (cudaEvent_t* ev : {&ev0, &ev1}) {
+                if (!stats_->spare.empty()) {
+                    *ev = stats_->spare.back();
+                    stats_->spare.pop_back();
+                } else {
+                    ck(cudaEventCreate(ev), "event");
+                }
+            }
+            ck(cudaEventRecord(ev0, s_), "event");
+        }
         if (conv_tc_run(L->tc, in.a, out.a, e, pad, pad, s_, status_, err) != 0)
             throw std::runtime_error(name + ": " + err);
+        if (ev0) {
+            ck(cudaEventRecord(ev1, s_), "event");
+            stats_->pending.emplace_back(ev0, ev1);
+        }
+        if (stats_) {
+            ++stats_->launches;
+            ++stats_->conv_launches;
+            stats_->conv_int16_macs += static_cast<double>(in.a.n) * oh * ow * L->co * L->ci * L->kh * L->kw;
+        }
         return out;
     }
     // Strided convolution: direct int64 kernel on NCHW copies (encode only).
@@ -266,6 +306,7 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
                    L->co, in.a.h, in.a.w, oh, ow, L->kh, L->kw, stride, stride, pad, pad, 1, s_),
        "strided conv");
     ck(nchw_to_split(static_cast<int16_t*>(xout), in.a.n, L->co, oh, ow, 1, out.a, s_), "strided conv layout");
+    count(3);
     pool_.put(xin, in_el * 2);
     pool_.put(xout, out_el * 2);
     return out;
@@ -329,6 +370,7 @@ Tensor Runner::cat(const std::vector<Tensor>& parts) {
         if (p.a.n != x.a.n || p.a.h != x.a.h || p.a.w != x.a.w) throw std::invalid_argument("cat shape mismatch");
         if (off % 16) throw std::invalid_argument("cat needs channel counts that are multiples of 16");
         ck(copy_channels(p.a, out.channels(off, p.a.c).a, s_), "cat");
+        count();
         off += p.a.c;
     }
     return out;
@@ -337,6 +379,7 @@ Tensor Runner::cat(const std::vector<Tensor>& parts) {
 Tensor Runner::multiply(const Tensor& x, const int16_t* q) {
     Tensor out = alloc(x.a.n, x.a.h, x.a.w, x.a.c);
     ck(mul_channels(x.a, q, out.a, s_), "multiply");
+    count();
     return out;
 }
 
@@ -344,6 +387,7 @@ Tensor Runner::unshuffle2(const Tensor& x, const int16_t* q) {
     if (x.a.h % 2 || x.a.w % 2) throw std::invalid_argument("pixel_unshuffle(2) needs even extents");
     Tensor out = alloc(x.a.n, x.a.h / 2, x.a.w / 2, x.a.c * 4);
     ck(mul_unshuffle2(x.a, q, out.a, s_), "pixel_unshuffle");
+    count();
     return out;
 }
 
@@ -414,19 +458,28 @@ std::vector<Tensor> Runner::reconstruct(const Tensor& feature, bool for_reset) {
 Codec::Codec(const Model& model, int batch) : m_(model), batch_(batch), pool_(model.device()) {
     if (batch <= 0) throw std::invalid_argument("batch must be positive");
     ck(cudaSetDevice(model.device()), "cudaSetDevice");
-    ck(cudaStreamCreateWithFlags(&s_, cudaStreamNonBlocking), "stream");
+    ck(cudaStreamCreateWithFlags(&own_, cudaStreamNonBlocking), "stream");
+    s_ = own_;
     ck(cudaMalloc(&status_, sizeof(int)), "status");
     ck(cudaMemset(status_, 0, sizeof(int)), "status");
     decoders_.resize(batch);
 }
 
 Codec::~Codec() {
+    if (s_) cudaStreamSynchronize(s_);
     reference_ = memory_ = context_ = Tensor();
-    if (s_) {
-        cudaStreamSynchronize(s_);
-        cudaStreamDestroy(s_);
+    last_frames_.clear();
+    if (own_) {
+        cudaStreamSynchronize(own_);
+        cudaStreamDestroy(own_);
     }
     if (status_) cudaFree(status_);
+}
+
+void Codec::set_stream(cudaStream_t s) {
+    // all pooled blocks are reused in stream order, so drain the old stream first
+    ck(cudaStreamSynchronize(s_), "codec stream");
+    s_ = s ? s : own_;
 }
 
 void Codec::set_skip_threshold(double threshold) {
@@ -442,6 +495,7 @@ void Codec::clear_dpb() { reference_ = memory_ = context_ = Tensor(); }
 
 void Codec::sync_and_check() {
     ck(cudaStreamSynchronize(s_), "codec stream");
+    stats_.collect();
     int st = 0;
     ck(cudaMemcpy(&st, status_, sizeof(int), cudaMemcpyDeviceToHost), "status read");
     if (st != 0) {
@@ -480,14 +534,23 @@ void Codec::add_ref_frames(const int16_t* frames, int h, int w) {
     // pixel_unshuffle(frame, 8) (src/integer_model.cpp:107-114).
     if (h % 8 || w % 8) throw std::invalid_argument("reference frame extents must be multiples of 8");
     clear_dpb();
-    Runner r(m_, pool_, s_, status_);
+    Runner r(m_, pool_, s_, status_, &stats_);
     const size_t bytes = static_cast<size_t>(batch_) * 3 * h * w * 2;
     void* d = pool_.get(bytes);
     ck(cudaMemcpyAsync(d, frames, bytes, cudaMemcpyHostToDevice, s_), "reference upload");
     reference_ = r.alloc(batch_, h / 8, w / 8, 192);
     ck(nchw_to_split(static_cast<int16_t*>(d), batch_, 3, h, w, 8, reference_.a, s_), "reference unshuffle");
+    stats_.launches += 1;
     sync_and_check();
     pool_.put(d, bytes);
+}
+
+void Codec::set_reference_from(const Codec& image) {
+    if (image.last_frames_.empty()) throw std::runtime_error("image codec has no reconstruction");
+    const Tensor& f = image.last_frames_.back();
+    if (f.a.n != batch_ || f.a.c != 192) throw std::invalid_argument("reference batch or channels differ");
+    clear_dpb();
+    reference_ = f;  // shared device storage; the image codec's next call allocates new tensors
 }
 
 void Codec::update_context(Runner& r) {
@@ -531,11 +594,14 @@ Tensor Codec::prior(Runner& r, const Tensor* y, const Tensor& params, int qp, bo
         yenc = r.alloc(n, h, w, C);
         if (image) {
             ck(mul_channels(y->a, qrow, yenc.a, r.stream()), "encode multiply");
+    stats_.launches += 1;
         } else {
             // q_enc = reciprocal(max(q_raw, 256)); encoded_y = multiply(y, q_enc)
             Tensor qenc = r.alloc(n, h, w, C);
             ck(reciprocal_q(qraw.a, qenc.a, r.stream()), "reciprocal");
+    stats_.launches += 1;
             ck(mul_elementwise(y->a, qenc.a, yenc.a, r.stream()), "encode multiply");
+    stats_.launches += 1;
         }
     }
     // cat(restored, reduction) lives in one buffer so the adaptors read it in place
@@ -544,6 +610,7 @@ Tensor Codec::prior(Runner& r, const Tensor* y, const Tensor& params, int qp, bo
     Tensor reduction_view = rr.channels(C, C);
     r.conv("y_spatial_prior_reduction", params, Fuse(), &reduction_view);
     ck(fill_zero(restored.a, r.stream()), "restored clear");
+    stats_.launches += 1;
 
     const long long cap = static_cast<long long>(C) * h * w;
     const int bps = prior_blocks_per_stream(C, h, w);
@@ -563,11 +630,13 @@ Tensor Codec::prior(Runner& r, const Tensor* y, const Tensor& params, int qp, bo
             means = next.channels(C, C);
         }
         ck(prior_scan(C, h, w, n, part, scales.a, skip_threshold_, d_counts, d_totals, r.stream()), "prior scan");
+    stats_.launches += 2;
         ck(cudaMemcpyAsync(h_totals, d_totals, sizeof(int) * n, cudaMemcpyDeviceToHost, r.stream()), "totals");
         if (!encode) {
             ck(prior_indexes(C, h, w, n, part, scales.a, skip_threshold_, d_counts, m_.scale_index(),
                              static_cast<uint8_t*>(d_buf), cap, r.stream()),
                "prior indexes");
+    stats_.launches += 1;
             sync_and_check();
             for (int b = 0; b < n; ++b)
                 if (h_totals[b])
@@ -588,12 +657,14 @@ Tensor Codec::prior(Runner& r, const Tensor* y, const Tensor& params, int qp, bo
             ck(prior_restore(C, h, w, n, part, scales.a, means.a, skip_threshold_, d_counts, d_sym, cap, restored.a,
                              r.stream()),
                "prior restore");
+    stats_.launches += 1;
             // the host buffers are reused by the next part: wait for the uploads
             ck(cudaStreamSynchronize(r.stream()), "symbols");
         } else {
             ck(prior_encode(C, h, w, n, part, scales.a, means.a, yenc.a, skip_threshold_, d_counts, m_.scale_index(),
                             static_cast<int16_t*>(d_buf), cap, restored.a, r.stream()),
                "prior encode");
+    stats_.launches += 1;
             sync_and_check();
             int16_t* hp = reinterpret_cast<int16_t*>(h_buf);
             for (int b = 0; b < n; ++b)
@@ -612,8 +683,10 @@ Tensor Codec::prior(Runner& r, const Tensor* y, const Tensor& params, int qp, bo
     if (image) {
         const ParamTable* q = m_.param("q_scale_y_dec");
         ck(mul_channels(restored.a, q->data + static_cast<size_t>(qp) * q->cols, yhat_t.a, r.stream()), "y_hat");
+    stats_.launches += 1;
     } else {
         ck(yhat(restored.a, qraw.a, yhat_t.a, r.stream()), "y_hat");
+    stats_.launches += 1;
     }
     return yhat_t;
 }
@@ -657,6 +730,7 @@ void Codec::emit_frames(const std::vector<Tensor>& frames, uint32_t width, uint3
                 one.base = frames[f].a.base + static_cast<long long>(b) * frames[f].a.img_px * 2 * frames[f].a.pitch;
                 one.n = 1;
                 ck(split_to_nchw(one, 8, d + (static_cast<size_t>(b) * F + f) * per_frame, s_), "frame shuffle");
+    stats_.launches += 1;
             }
         }
         ck(cudaMemcpyAsync(frames_out, d, bytes, cudaMemcpyDeviceToHost, s_), "frames download");
@@ -674,6 +748,7 @@ void Codec::emit_frames(const std::vector<Tensor>& frames, uint32_t width, uint3
                 ck(raw_frame(one, static_cast<int>(height), static_cast<int>(width),
                              d + (static_cast<size_t>(b) * F + f) * yuv_frame, static_cast<long long>(yuv_frame), s_),
                    "raw frame");
+    stats_.launches += 1;
             }
         }
         ck(cudaMemcpyAsync(yuv_out, d, bytes, cudaMemcpyDeviceToHost, s_), "yuv download");
@@ -687,7 +762,7 @@ int Codec::decompress(const uint8_t* const* payloads, const size_t* lengths, uin
                       bool reset, int16_t* frames_out, uint8_t* yuv_out) {
     if (qp < 0 || qp >= 64 || !width || !height) throw std::invalid_argument("Unsupported UF integer packet parameters");
     host_seconds_ = 0;
-    Runner r(m_, pool_, s_, status_);
+    Runner r(m_, pool_, s_, status_, &stats_);
     const bool image = m_.variant() == "image";
     if (!image) update_context(r);  // queued on the GPU while the host decodes z
     const int y_h = static_cast<int>((height + 15) / 16), y_w = static_cast<int>((width + 15) / 16);
@@ -703,10 +778,12 @@ int Codec::decompress(const uint8_t* const* payloads, const size_t* lengths, uin
     ck(cudaMemcpyAsync(dz, hz, zn * batch_, cudaMemcpyHostToDevice, s_), "z upload");
     Tensor z = r.alloc(batch_, z_h, z_w, zc);
     ck(symbols_to_split(dz, z.a, s_), "from_symbols");
+    stats_.launches += 1;
     const Tensor p = params(r, z, qp, y_h, y_w);
     const Tensor y_hat = prior(r, nullptr, p, qp, false, nullptr);
     pool_.put(dz, zn * batch_);
     const std::vector<Tensor> frames = reconstruct(r, y_hat, qp, reset, true);
+    last_frames_ = frames;
     emit_frames(frames, width, height, frames_out, yuv_out);
     sync_and_check();
     return static_cast<int>(frames.size());
@@ -717,7 +794,7 @@ int Codec::compress(const uint8_t* frames, int channels, int h, int w, int qp, b
                     std::vector<std::vector<uint8_t>>& payloads, int16_t* frames_out) {
     if (qp < 0 || qp >= 64) throw std::invalid_argument("UF QP must be between 0 and 63");
     host_seconds_ = 0;
-    Runner r(m_, pool_, s_, status_);
+    Runner r(m_, pool_, s_, status_, &stats_);
     const bool image = m_.variant() == "image";
     const int hp = (h + 15) / 16 * 16, wp = (w + 15) / 16 * 16;  // pad_right_bottom(x, 16)
     const size_t in_bytes = static_cast<size_t>(batch_) * channels * h * w;
@@ -728,6 +805,7 @@ int Codec::compress(const uint8_t* frames, int channels, int h, int w, int qp, b
         if (channels != 3) throw std::invalid_argument("image model takes one frame");
         Tensor x = r.alloc(batch_, hp / 8, wp / 8, 192);
         ck(bytes_to_split_padded(d_in, batch_, channels, h, w, hp, wp, 8, x.a, s_), "frame unshuffle");
+    stats_.launches += 1;
         const ParamTable* q = m_.param("q_scale_enc");
         y = r.run("enc", {x}, q->data + static_cast<size_t>(qp) * q->cols);
     } else {
@@ -736,8 +814,10 @@ int Codec::compress(const uint8_t* frames, int channels, int h, int w, int qp, b
         Tensor xin = r.alloc(batch_, hp / 8, wp / 8, channels * 64 + context_.a.c);
         Tensor xv = xin.channels(0, channels * 64);
         ck(bytes_to_split_padded(d_in, batch_, channels, h, w, hp, wp, 8, xv.a, s_), "frame unshuffle");
+    stats_.launches += 1;
         Tensor cv = xin.channels(channels * 64, context_.a.c);
         ck(copy_channels(context_.a, cv.a, s_), "context cat");
+    stats_.launches += 1;
         const ParamTable* q = m_.param("q_encoder");
         Tensor out = r.simple("encoder.conv1", xin);
         if (m_.has_child("encoder.conv2")) out = r.simple("encoder.conv2", out);
@@ -749,13 +829,16 @@ int Codec::compress(const uint8_t* frames, int channels, int h, int w, int qp, b
     const int yph = (y_h + 3) / 4 * 4, ypw = (y_w + 3) / 4 * 4;
     Tensor ypad = r.alloc(batch_, yph, ypw, y.a.c);
     ck(pad_replicate(y.a, ypad.a, s_), "pad_right_bottom");
+    stats_.launches += 1;
     const Tensor zf = r.run(image ? "hyper_enc" : "hyper_encoder", {ypad});
     const int z_h = zf.a.h, z_w = zf.a.w, zc = zf.a.c;
     const size_t zn = static_cast<size_t>(z_h) * z_w * zc;
     int8_t* dz = static_cast<int8_t*>(pool_.get(zn * batch_));
     ck(split_to_symbols(zf.a, dz, s_), "symbols");
+    stats_.launches += 1;
     Tensor z = r.alloc(batch_, z_h, z_w, zc);
     ck(symbols_to_split(dz, z.a, s_), "from_symbols");
+    stats_.launches += 1;
     int8_t* hz = static_cast<int8_t*>(pin_c_.get(zn * batch_));
     ck(cudaMemcpyAsync(hz, dz, zn * batch_, cudaMemcpyDeviceToHost, s_), "z download");
     std::vector<int8_t> zhost;
@@ -775,6 +858,7 @@ int Codec::compress(const uint8_t* frames, int channels, int h, int w, int qp, b
         payloads[b] = enc.flush();
     });
     const std::vector<Tensor> rec = reconstruct(r, y_hat, qp, reset, frames_out != nullptr || image);
+    last_frames_ = rec;
     if (frames_out) {
         emit_frames(rec, static_cast<uint32_t>(wp), static_cast<uint32_t>(hp), frames_out, nullptr);
     }

@@ -111,6 +111,20 @@ private:
     RansTables z_table_, y_table_;
 };
 
+// Launch accounting of one engine (all kernels) and, when profiling is on,
+// CUDA-event timing of the tensor-core convolution launches.
+struct EngineStats {
+    long long launches = 0;        // kernels launched
+    long long conv_launches = 0;   // tensor-core convolution launches
+    double conv_int16_macs = 0;    // algorithmic int16 MACs of those launches
+    double conv_ms = 0;            // summed event time of those launches (profiling on)
+    bool profile = false;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;
+    std::vector<cudaEvent_t> spare;
+    void collect();                // adds the elapsed time of completed launches
+    ~EngineStats();
+};
+
 // Epilogue options of one convolution call.
 struct Fuse {
     bool lut = false;
@@ -124,8 +138,11 @@ struct Fuse {
 // Executes module paths by parameter name, mirroring src/layers.cpp:74-216.
 class Runner {
 public:
-    Runner(const Model& m, DevicePool& pool, cudaStream_t s, int* status)
-        : m_(m), pool_(pool), s_(s), status_(status) {}
+    Runner(const Model& m, DevicePool& pool, cudaStream_t s, int* status, EngineStats* stats = nullptr)
+        : m_(m), pool_(pool), s_(s), status_(status), stats_(stats) {}
+    void count(int n = 1) {
+        if (stats_) stats_->launches += n;
+    }
     Tensor alloc(int n, int h, int w, int c);
     Tensor conv(const std::string& name, const Tensor& in, const Fuse& f = Fuse(), const Tensor* out = nullptr);
     Tensor depth(const std::string& name, const Tensor& in, bool shortcut, const Tensor* out = nullptr);
@@ -148,6 +165,7 @@ private:
     DevicePool& pool_;
     cudaStream_t s_;
     int* status_;
+    EngineStats* stats_;
 };
 
 // Host buffers pinned for transfers, grown on demand.
@@ -187,6 +205,13 @@ public:
     bool state(int which, int16_t* out, size_t capacity, int64_t* shape4);
     int frames_per_packet() const { return m_.variant() == "image" ? 1 : 8; }
     double last_host_seconds() const { return host_seconds_; }
+    // reference = another codec's last reconstruction (device to device): the
+    // image model's output is pixel_unshuffle(frame, 8) of the I frame, which
+    // is what add_ref_feature_from_frame stores (src/integer_model.cpp:107-114)
+    void set_reference_from(const Codec& image);
+    EngineStats& stats() { return stats_; }
+    // run on a caller-owned CUDA stream from now on (null: back to our own)
+    void set_stream(cudaStream_t s);
 
 private:
     void update_context(Runner& r);
@@ -204,12 +229,15 @@ private:
     int batch_;
     DevicePool pool_;
     cudaStream_t s_ = nullptr;
+    cudaStream_t own_ = nullptr;
     int* status_ = nullptr;
     int skip_threshold_ = 0;
     Tensor reference_, memory_, context_;
     std::vector<RansDecoder> decoders_;
     Pinned pin_a_, pin_b_, pin_c_;
     double host_seconds_ = 0;
+    std::vector<Tensor> last_frames_;  // last reconstruction (head outputs, 192 ch)
+    EngineStats stats_;
 };
 
 }  // namespace ufb

@@ -353,3 +353,40 @@ def frames_to_chunk(frames_u8: np.ndarray) -> np.ndarray:
     src/integer_codec.cpp:183-213 concatenates each frame's 3 planes)."""
     f, c, h, w = frames_u8.shape
     return np.ascontiguousarray(frames_u8.reshape(1, f * c, h, w))
+
+
+def synthetic_video_gpu(width: int, height: int, frames: int, seed: int, device="cuda"):
+    """The synthetic_video scene (same background, six moving textured
+    rectangles, N(0, 2^2) noise) generated with torch on a GPU for the
+    large benchmark workloads.  Rectangle parameters come from the same numpy
+    generator; the noise comes from a torch generator seeded with `seed`, so
+    the pixels differ from synthetic_video() but are equally reproducible.
+    Returns uint8 [frames, 3, height, width] on `device`."""
+    import torch
+    rng = np.random.default_rng(seed)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    yy, xx = torch.meshgrid(torch.arange(height, device=device, dtype=torch.float32),
+                            torch.arange(width, device=device, dtype=torch.float32), indexing="ij")
+    base = torch.stack([60 + 120 * xx / max(width - 1, 1) + 30 * yy / max(height - 1, 1),
+                        128 + 40 * torch.sin(xx / 37.0), 128 + 40 * torch.cos(yy / 29.0)])
+    rects = []
+    for _ in range(6):
+        rw, rh = int(rng.integers(width // 10 + 4, width // 4 + 8)), int(rng.integers(height // 10 + 4, height // 4 + 8))
+        x0, y0 = rng.uniform(0, width - rw), rng.uniform(0, height - rh)
+        speed, ang = rng.uniform(0, 4), rng.uniform(0, 2 * math.pi)
+        color = rng.uniform(20, 235, 3)
+        freq = rng.uniform(0.2, 0.8)
+        rects.append((rw, rh, x0, y0, speed * math.cos(ang), speed * math.sin(ang), color, freq))
+    out = torch.empty((frames, 3, height, width), dtype=torch.uint8, device=device)
+    for f in range(frames):
+        img = base.clone()
+        for rw, rh, x0, y0, vx, vy, color, freq in rects:
+            cx, cy = int(round(x0 + vx * f)) % width, int(round(y0 + vy * f)) % height
+            ys, xs = slice(cy, min(cy + rh, height)), slice(cx, min(cx + rw, width))
+            tex = 25 * torch.sin(freq * (xx[ys, xs] + yy[ys, xs]))
+            for c in range(3):
+                img[c, ys, xs] = float(color[c]) + (tex if c == 0 else 0.3 * tex)
+        img += torch.randn(img.shape, generator=gen, device=device) * 2.0
+        out[f] = img.round().clamp(0, 255).to(torch.uint8)
+    return out

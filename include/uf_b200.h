@@ -225,6 +225,25 @@ int ufb_codec_state(ufb_codec* c, int which, int16_t* out, int64_t capacity, int
 /* Seconds the last decompress/compress spent in host entropy coding. */
 double ufb_codec_host_seconds(ufb_codec* c);
 
+/* IntegerCodec's I-to-P hand-off (video->add_ref_feature_from_frame(frames.at(0)),
+ * src/integer_codec.cpp:453-456) without leaving the GPU: the video codec's
+ * DPB is cleared and its reference becomes the image codec's last
+ * reconstruction (same batch). */
+int ufb_codec_set_reference_from(ufb_codec* video, ufb_codec* image);
+
+/* Run the codec's work on a caller-owned CUDA stream (NULL: the codec's own
+ * stream, the default).  Like the reference's pooled per-codec stream
+ * (src/integer_codec.cpp:30-49), all of a codec's kernels use one stream. */
+int ufb_codec_set_stream(ufb_codec* c, void* stream);
+
+/* Measurement: with profiling on, every tensor-core convolution launch is
+ * bracketed by CUDA events on the codec's stream.  ufb_codec_stats reports the
+ * kernels launched, the convolution launches, their algorithmic int16 MACs and
+ * summed event time (ms) since the last reset (reset != 0 clears them). */
+int ufb_codec_profile(ufb_codec* c, int enable);
+int ufb_codec_stats(ufb_codec* c, int reset, int64_t* launches, int64_t* conv_launches, double* conv_int16_macs,
+                    double* conv_ms);
+
 /* Measurement utility (no reference counterpart): launches `ctas` CTAs that
  * each issue `iters` x 4 dense tcgen05 kind::i8 M=128 N=256 K=32 MMAs from
  * resident shared-memory tiles; *int8_ops receives the operation count
