@@ -1,0 +1,121 @@
+// ufb_conv2d_noalloc: the uf_conv replacement for callers that must not
+// allocate GPU memory while they process (see include/uf_b200.h).
+//
+// ufb_conv2d needs three scratch buffers per call -- the input in split NHWC,
+// the weights as tensor-core planes and the output in split NHWC -- and takes
+// them from cudaMallocAsync.  This variant carves them out of one fixed,
+// file-scope device array instead, sized kNoAllocScratchBytes.  The array is
+// part of the library image: every GPU that loads the library holds it until
+// the process exits.
+#include "uf_b200.h"
+
+#include "capi_util.h"
+#include "conv_tc.h"
+#include "kernels.h"
+
+#include <climits>
+#include <mutex>
+#include <string>
+#include <vector>
+
+using namespace ufb;
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(UFB_NOALLOC_SCRATCH_BYTES);
+
+// Shared by every call on a device; holds the last call's contents.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_mutex;
+std::vector<uint8_t*> g_device_ptr;  // per device ordinal, null until resolved
+
+// Host code may not use g_noalloc_scratch as an address (it names the host
+// shadow of the symbol).  Resolve the device address once per device, with
+// that device current.
+uint8_t* scratch_for_current_device() {
+    int device = 0;
+    if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return nullptr;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (static_cast<size_t>(device) >= g_device_ptr.size()) g_device_ptr.resize(device + 1, nullptr);
+    if (!g_device_ptr[device]) {
+        void* p = nullptr;
+        if (!cuda_ok(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(scratch)")) return nullptr;
+        g_device_ptr[device] = static_cast<uint8_t*>(p);
+    }
+    return g_device_ptr[device];
+}
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+}  // namespace
+
+extern "C" int ufb_conv2d_noalloc(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co,
+                                  int kh, int kw, const void* bias, int bias_bits, int sh, int sw, int ph, int pw,
+                                  int groups, int16_t* out, void* stream) {
+    clear_error();
+    if (!bias) bias_bits = 0;
+    if (!x || !weight || !out) return err(UFB_EINVAL, "convolution tensors must be non-null");
+    if (sh <= 0 || sw <= 0 || ph < 0 || pw < 0 || groups <= 0) return err(UFB_EINVAL, "invalid convolution geometry");
+    if (ci <= 0 || co <= 0 || kh <= 0 || kw <= 0 || n <= 0 || h <= 0 || w <= 0) return err(UFB_EINVAL, "empty convolution");
+    if (ci % groups || co % groups) return err(UFB_EINVAL, "invalid groups");
+    if (bias_bits != 0 && bias_bits != 16 && bias_bits != 32) return err(UFB_EINVAL, "bias_bits must be 16 or 32");
+    const long long padded_h = static_cast<long long>(h) + 2ll * ph, padded_w = static_cast<long long>(w) + 2ll * pw;
+    if (padded_h < kh || padded_w < kw) return err(UFB_EINVAL, "kernel exceeds input");
+    const long long ohl = (padded_h - kh) / sh + 1, owl = (padded_w - kw) / sw + 1;
+    const long long planes = static_cast<long long>(n) * co;
+    if (planes > INT32_MAX || ohl > INT32_MAX / planes || owl > INT32_MAX / (planes * ohl) ||
+        static_cast<long long>(n) * ci * h * w > INT32_MAX)
+        return err(UFB_ERANGE, "convolution output exceeds indexing bounds");
+    const int oh = static_cast<int>(ohl), ow = static_cast<int>(owl);
+    auto s = static_cast<cudaStream_t>(stream);
+    // first call on this device: resolve the scratch array's device address
+    uint8_t* base = scratch_for_current_device();
+    if (!base) return last_code();
+
+    const bool tensor_core = groups == 1 && sh == 1 && sw == 1 && static_cast<long long>(ci) * kh * kw <= 32768;
+    if (!tensor_core) {
+        // the direct int64 kernel reads NCHW in place and needs no scratch
+        return cuda_ok(conv_direct(out, x, weight, bias_bits ? bias : nullptr, bias_bits == 32, n, ci, co, h, w, oh,
+                                   ow, kh, kw, sh, sw, ph, pw, groups, s),
+                       "direct convolution")
+                   ? UFB_OK
+                   : last_code();
+    }
+    const int cip = round_up(ci, 16), cop = round_up(co, 16);
+    TcWeights tw;
+    tw.co = co;
+    tw.ci = ci;
+    tw.kh = kh;
+    tw.kw = kw;
+    tw.cpad = round_up(ci, 128);
+    tw.kpad = kh * kw * tw.cpad;
+    const size_t x_bytes = align256(static_cast<size_t>(n) * h * w * 2 * cip);
+    const size_t w_bytes = align256(static_cast<size_t>(2) * co * tw.kpad);
+    const size_t o_bytes = align256(static_cast<size_t>(n) * oh * ow * 2 * cop);
+    if (x_bytes + w_bytes + o_bytes > kNoAllocScratchBytes)
+        return err(UFB_ERANGE, "convolution needs " + std::to_string(x_bytes + w_bytes + o_bytes) +
+                                   " scratch bytes; ufb_conv2d_noalloc is limited to " +
+                                   std::to_string(kNoAllocScratchBytes) + " (UFB_NOALLOC_SCRATCH_BYTES)");
+    int device = 0;
+    if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return last_code();
+    // Nothing in the scratch must start at zero: the layout conversion and the
+    // weight preparation overwrite every byte the convolution reads (channels
+    // past ci are outside the TMA tensor extent and read as zero), and the
+    // epilogue writes every output byte that is converted back.
+    tw.planes = base + x_bytes;
+    std::string msg;
+    if (!tc_weight_map(tw, 128, &tw.map128, msg) || !tc_weight_map(tw, 64, &tw.map64, msg))
+        return err(UFB_ECUDA, msg);
+    const Act in = make_act(base, n, h, w, ci, cip);
+    const Act ov = make_act(base + x_bytes + w_bytes, n, oh, ow, co, cop);
+    if (!cuda_ok(prep_weights(weight, co, ci, kh, kw, tw.cpad, tw.kpad, tw.planes, s), "weight preparation"))
+        return last_code();
+    if (!cuda_ok(nchw_to_split(x, n, ci, h, w, 1, in, s), "input layout")) return last_code();
+    Epilogue epi{};
+    epi.bias = bias_bits ? bias : nullptr;
+    epi.bias32 = bias_bits == 32;
+    if (conv_tc_run(tw, in, ov, epi, ph, pw, s, device_status(device), msg) != 0) return err(UFB_ECUDA, msg);
+    if (!cuda_ok(split_to_nchw(ov, 1, out, s), "output layout")) return last_code();
+    return UFB_OK;
+}

@@ -244,6 +244,37 @@ int ufb_codec_profile(ufb_codec* c, int enable);
 int ufb_codec_stats(ufb_codec* c, int reset, int64_t* launches, int64_t* conv_launches, double* conv_int16_macs,
                     double* conv_ms);
 
+/* ---------------------------------------------------------------------------
+ * No-allocation convolution (no counterpart in the reference: its uf_conv
+ * always allocates its output and temporaries through the caller's allocator).
+ * ------------------------------------------------------------------------- */
+
+/* Fixed scratch capacity of ufb_conv2d_noalloc, per GPU, in bytes. */
+#define UFB_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
+
+/* ufb_conv2d without any device allocation, for callers that cannot allocate
+ * GPU memory while they process -- for example a host application that
+ * reserves all device memory up front and hands this library only input and
+ * output buffers, or a real-time frame loop where an allocation could stall
+ * or fail part-way through a stream.  Same arguments, checks and results as
+ * ufb_conv2d; the caller still owns x, weight, bias and out.
+ *
+ * Tensor-core geometries stage the input, the prepared weights and the output
+ * in one fixed device array of UFB_NOALLOC_SCRATCH_BYTES that the library
+ * holds on every GPU it is loaded on until the process exits; a call whose
+ * staging would exceed it fails with UFB_ERANGE and a message giving the
+ * needed size.  Other geometries (grouped, strided, K > 32768) use the direct
+ * kernel, which needs no scratch.
+ *
+ * The first call on a device resolves the array's device address with that
+ * device current; make that first call before any stream capture.  All calls
+ * on a device share the one array and it keeps the last call's contents, so
+ * calls that overlap on the GPU (different streams, or host threads) race:
+ * serialise them.  No part of the array needs to start at zero. */
+int ufb_conv2d_noalloc(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
+                       const void* bias, int bias_bits, int stride_h, int stride_w, int pad_h, int pad_w, int groups,
+                       int16_t* out, void* stream);
+
 /* Measurement utility (no reference counterpart): launches `ctas` CTAs that
  * each issue `iters` x 4 dense tcgen05 kind::i8 M=128 N=256 K=32 MMAs from
  * resident shared-memory tiles; *int8_ops receives the operation count
