@@ -56,6 +56,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=1)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="decode", choices=["decode", "conv"])
+    p.add_argument("--seqs", type=int, default=SEQS,
+                   help="sequences in the job (default: BASELINE config 5's 64); smaller values are for profiling")
     return p.parse_args()
 
 
@@ -151,8 +153,8 @@ def i8_peak_tops(L, stream):
 
 # --------------------------------------------------------------- decode ----
 
-def shard(rank, world):
-    per = SEQS // world
+def shard(rank, world, seqs):
+    per = max(seqs // world, 1)
     return list(range(rank * per, (rank + 1) * per))
 
 
@@ -196,7 +198,7 @@ def bench_decode_ours(args, rank, world, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream(dev)
-    seqs = shard(rank, world)
+    seqs = shard(rank, world, args.seqs)
     batch = min(32, len(seqs))
     mi = ufb.Model("image", syn.prepared("image", 1), device=local)
     mv = ufb.Model("htl", syn.prepared("htl", 2), device=local)
@@ -231,10 +233,12 @@ def bench_decode_ours(args, rank, world, local):
         barrier(world)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("timed_e2e" if yuv else "timed")  # ncu --nvtx-include "timed/"
         e0.record(stream)
         frames = sum(step(yuv) for _ in range(steps))
         e1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
         barrier(world)
         st = {"launches": 0, "conv_launches": 0, "conv_int16_macs": 0.0, "conv_ms": 0.0}
         for pair in decoders:
@@ -274,8 +278,8 @@ def bench_decode_ours(args, rank, world, local):
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int16 (int8 tensor planes, s32 accumulators, int64 recombination)",
         "data": "synthetic (seeded scene generator, seeded random-init HT-L + image models)",
-        "config": {"workload": "config 5: 64 seqs x 32 frames 1920x1088, I + 4 P packets each, qp_i 0 qp_p 20, "
-                               "reset 8, skip 0.2", "streams_per_gpu": len(seqs), "codec_batch": batch,
+        "config": {"workload": f"config 5: {len(seqs) * world} seqs x 32 frames 1920x1088, I + 4 P packets each, "
+                               "qp_i 0 qp_p 20, reset 8, skip 0.2", "streams_per_gpu": len(seqs), "codec_batch": batch,
                    "l2": "working set per step several GB, far above L2",
                    "parallelism": f"stream sharding x{world}, no inter-GPU communication"},
         "gpu_launches": int(st["launches"]),
