@@ -83,15 +83,8 @@ extern "C" int ufb_conv2d_noalloc(const int16_t* x, int n, int ci, int h, int w,
                    : last_code();
     }
     const int cip = round_up(ci, 16), cop = round_up(co, 16);
-    TcWeights tw;
-    tw.co = co;
-    tw.ci = ci;
-    tw.kh = kh;
-    tw.kw = kw;
-    tw.cpad = round_up(ci, 128);
-    tw.kpad = kh * kw * tw.cpad;
     const size_t x_bytes = align256(static_cast<size_t>(n) * h * w * 2 * cip);
-    const size_t w_bytes = align256(static_cast<size_t>(2) * co * tw.kpad);
+    const size_t w_bytes = align256(tc_weight_bytes(co, ci, kh, kw));
     const size_t o_bytes = align256(static_cast<size_t>(n) * oh * ow * 2 * cop);
     if (x_bytes + w_bytes + o_bytes > kNoAllocScratchBytes)
         return err(UFB_ERANGE, "convolution needs " + std::to_string(x_bytes + w_bytes + o_bytes) +
@@ -103,14 +96,12 @@ extern "C" int ufb_conv2d_noalloc(const int16_t* x, int n, int ci, int h, int w,
     // weight preparation overwrite every byte the convolution reads (channels
     // past ci are outside the TMA tensor extent and read as zero), and the
     // epilogue writes every output byte that is converted back.
-    tw.planes = base + x_bytes;
+    TcWeights tw;
     std::string msg;
-    if (!tc_weight_map(tw, 128, &tw.map128, msg) || !tc_weight_map(tw, 64, &tw.map64, msg))
-        return err(UFB_ECUDA, msg);
+    // unsigned byte split: valid for any weights, needs no host inspection
+    if (!tc_prepare(tw, weight, co, ci, kh, kw, false, base + x_bytes, s, msg)) return err(UFB_ECUDA, msg);
     const Act in = make_act(base, n, h, w, ci, cip);
     const Act ov = make_act(base + x_bytes + w_bytes, n, oh, ow, co, cop);
-    if (!cuda_ok(prep_weights(weight, co, ci, kh, kw, tw.cpad, tw.kpad, tw.planes, s), "weight preparation"))
-        return last_code();
     if (!cuda_ok(nchw_to_split(x, n, ci, h, w, 1, in, s), "input layout")) return last_code();
     Epilogue epi{};
     epi.bias = bias_bits ? bias : nullptr;

@@ -4,224 +4,288 @@
 // (src/cuda/int16_mma.cuh:40-109, dispatched from src/cuda/conv.cu:62-127) with
 // the same exact arithmetic (src/cuda/conv.cu:9-13):
 //     out = sat(rna(sum_k x_k * w_k / 8192) + bias)
-// Each int16 operand is split into an unsigned low byte and a signed high byte,
-// v = lo + 256 * hi.  Four tcgen05 kind::i8 products per K block
-//     LL = xlo*wlo (u8*u8),  X = xhi*wlo (s8*u8) + xlo*whi (u8*s8),  HH = xhi*whi (s8*s8)
-// accumulate exactly in three s32 TMEM accumulators (for K <= 32768:
-// |X| <= 65280 K < 2^31, LL <= 65025 K < 2^31) and the epilogue recombines
-// LL + 256 X + 65536 HH in int64.
 //
-// GEMM orientation: M = 128 output pixels (TMEM lanes), N = BN output
-// channels (TMEM columns), K = taps x input channels.  Activations are split
-// NHWC in HBM, so both operands are K-major and arrive by TMA as 128-byte
-// swizzled tiles: one u8 and one s8 tile per operand per K block of 128
-// channels.  3x3 taps are spatially shifted TMA boxes over a 5-D tensor map;
-// the zero fill of out-of-range coordinates is the convolution's zero padding.
+// Operands are split into bytes, x = xl + 256 xh (xl u8, xh s8) and
+// w = wl + 256 wh, and the products accumulate exactly in three s32 TMEM
+// accumulators LL = sum xl wl, X = sum (xh wl + xl wh), HH = sum xh wh, which
+// the epilogue recombines as LL + 256 X + 65536 HH.  Two weight splits:
+//   unsigned (any weights): wl u8, wh s8 -- four N=128 MMAs per K step;
+//   signed (w <= 32639):    wl s8, wh s8 -- the weight tile stacks its 128
+//     low rows over its 128 high rows, so one N=256 MMA A_lo x [wl; wh]
+//     yields [LL | xl wh] and one N=256 MMA A_hi x [wl; wh], written 128
+//     columns further on, adds xh wl onto X and yields HH: two MMAs per step.
+// For K <= 32768 every partial sum fits s32 (|X| <= 383 * 128 * K).
 //
-// Warp roles (320 threads): warp 0 issues TMA, warp 1 owns TMEM and issues
-// the MMAs, warps 2-9 run the epilogue (two warps per TMEM lane quarter, each
-// taking half of the accumulator columns).
+// GEMM orientation: M = 128 output pixels (TMEM lanes), N = 128 output
+// channels per tile, K = taps x input channels.  Activations are split NHWC in
+// HBM, so both operands are K-major and arrive by TMA as 128-byte swizzled
+// tiles; 3x3 taps are spatially shifted TMA boxes over a 5-D tensor map whose
+// zero fill is the convolution's zero padding.
+//
+// Persistent CTAs (one per SM) walk the output tiles.  Warp 0 issues TMA into a
+// 3-stage ring that runs ahead across tiles, warp 1 owns TMEM and issues the
+// MMAs, warps 2-9 run the epilogue in two phases: phase 1 reads the three
+// accumulators, rounds, adds the bias and saturates into registers, then
+// releases TMEM so the next tile's MMAs start; phase 2 applies the fused
+// elementwise steps (LUT, residual adds, QP multiply, WSiLU4, pixel shuffle)
+// and stores while those MMAs run.
 #include "umma.cuh"
 #include "uf_common.cuh"
 #include "conv_tc.h"
 
 #include <cuda_runtime.h>
-#include <cstdio>
 #include <mutex>
 #include <string>
+#include <vector>
 
 namespace ufb {
 
-constexpr int kBM = 128;   // output pixels per tile
-constexpr int kBK = 128;   // input channels (bytes per plane row) per K block
-constexpr int kThreads = 320;
+namespace {
+
+constexpr int kBM = 128;                                    // output pixels per tile
+constexpr int kBK = 128;                                    // input channels per K block
+constexpr int kBN = kTcTileN;                               // output channels per tile
+constexpr int kStages = 3;
+constexpr int kEpiWarps = 16;                               // four per TMEM lane quarter
+constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr uint32_t kABytes = kBM * kBK;                     // one activation plane tile
+constexpr uint32_t kBBytes = 2 * kBN * kBK;                 // stacked low / high weight rows
+constexpr uint32_t kStageBytes = 2 * kABytes + kBBytes;     // 64 KB
+constexpr uint32_t kTmemCols = 512;                         // LL [0,128) X [128,256) HH [256,384)
+constexpr size_t kRingBytes = size_t(kStages) * kStageBytes + 1024;
+constexpr int kCols = kBN / 4;                              // accumulator columns per epilogue warp
+
+// Fused elementwise step applied by the epilogue (compile-time, so each
+// instantiation is short straight-line code).
+enum EpiMode : int { kEpiPlain = 0, kEpiLut = 1, kEpiRes = 2, kEpiWsilu4 = 3, kEpiShuffle2 = 4 };
 
 struct ConvTcArgs {
     Act out;
     Epilogue epi;
-    int co, ci;
-    int taps_h, taps_w, pad_h, pad_w;
-    int cpad;              // channels per tap in the weight matrix (multiple of kBK)
-    int n, oh, ow;         // output geometry before any pixel shuffle
+    int co, ci, taps_h, taps_w, pad_h, pad_w, cpad;
+    int oh, ow;
     int tile_w, tile_h, tiles_x, tiles_y;
-    long long m_total;     // flat mode: output pixels
-    Act res1, res2;
+    long long m_total;  // flat mode: output pixels
+    int n_tiles, total_tiles;
+    int signed_split;
+    int wide;           // K >= 16384: int64 recombination
     int* status;
 };
 
-template <int BN>
-struct TcConfig {
-    static constexpr int kStages = BN == 128 ? 3 : 4;
-    static constexpr uint32_t kABytes = kBM * kBK;
-    static constexpr uint32_t kBBytes = BN * kBK;
-    static constexpr uint32_t kStageBytes = 2 * kABytes + 2 * kBBytes;
-    static constexpr uint32_t kTmemCols = 3 * BN <= 256 ? 256 : 512;
-    static constexpr size_t kSmem = size_t(kStages) * kStageBytes + 1024;
+struct TileCoord {
+    int img, y0, x0, co0;
+    long long p0;
 };
 
-__device__ __forceinline__ int16_t epilogue_value(int64_t sum, int co, const ConvTcArgs& a) {
-    int64_t v = rna_shift(sum, 13);
-    if (a.epi.bias) {
-        v += a.epi.bias32 ? static_cast<const int32_t*>(a.epi.bias)[co] : static_cast<const int16_t*>(a.epi.bias)[co];
+template <bool SPATIAL>
+__device__ __forceinline__ TileCoord tile_coord(const ConvTcArgs& a, int tile) {
+    TileCoord t{};
+    const int m = tile / a.n_tiles;
+    t.co0 = (tile - m * a.n_tiles) * kBN;
+    if (SPATIAL) {
+        int r = m;
+        const int tx = r % a.tiles_x;
+        r /= a.tiles_x;
+        const int ty = r % a.tiles_y;
+        t.img = r / a.tiles_y;
+        t.x0 = tx * a.tile_w;
+        t.y0 = ty * a.tile_h;
+    } else {
+        t.p0 = static_cast<long long>(m) * kBM;
     }
-    return sat16(v);
+    return t;
 }
 
-// Applies the epilogue to 16 accumulator columns of one pixel row and stores
-// them (split NHWC, 16-byte vector stores when the whole chunk is in range).
-__device__ __forceinline__ void store_chunk(const ConvTcArgs& args, const uint32_t (&ll)[16], const uint32_t (&xx)[16],
-                                            const uint32_t (&hh)[16], int cbase, int img, int oy, int ox,
-                                            long long px, bool spatial) {
-    const Epilogue& e = args.epi;
-    int16_t v[16];
+// rna(S / 8192) of S = L + 256 X + 65536 H without 64-bit arithmetic (valid
+// for K < 16384, where 8 |H| < 2^31): S = 8192 T + Rl with 0 <= Rl < 8192, and
+// round-half-away gives T + (Rl > 4096 || (Rl == 4096 && T >= 0)).
+__device__ __forceinline__ int32_t recombine32(int32_t L, int32_t X, int32_t H) {
+    const int32_t R = ((X & 31) << 8) + (L & 8191);
+    const int32_t T = H * 8 + (X >> 5) + (L >> 13) + (R >> 13);
+    const int32_t Rl = R & 8191;
+    return T + ((Rl > 4096) | ((Rl == 4096) & (T >= 0)));
+}
+
+__device__ __forceinline__ int64_t recombine64(int32_t L, int32_t X, int32_t H) {
+    return rna_shift(static_cast<int64_t>(L) + 256 * static_cast<int64_t>(X) + 65536 * static_cast<int64_t>(H), 13);
+}
+
+__device__ __forceinline__ int32_t clamp16(int32_t v) { return v < -32768 ? -32768 : (v > 32767 ? 32767 : v); }
+
+__device__ __forceinline__ uint32_t pack2(int32_t a, int32_t b) {
+    return (static_cast<uint32_t>(a) & 0xffffu) | (static_cast<uint32_t>(b) << 16);
+}
+
+__device__ __forceinline__ int32_t lo16(uint32_t p) { return static_cast<int16_t>(p & 0xffffu); }
+__device__ __forceinline__ int32_t hi16(uint32_t p) { return static_cast<int16_t>(p >> 16); }
+
+// 16 packed int16 values (8 words) -> 16 low bytes + 16 high bytes.
+__device__ __forceinline__ void split_bytes(const uint32_t (&p)[8], uint4& lo, uint4& hi) {
+    lo.x = __byte_perm(p[0], p[1], 0x6420);
+    lo.y = __byte_perm(p[2], p[3], 0x6420);
+    lo.z = __byte_perm(p[4], p[5], 0x6420);
+    lo.w = __byte_perm(p[6], p[7], 0x6420);
+    hi.x = __byte_perm(p[0], p[1], 0x7531);
+    hi.y = __byte_perm(p[2], p[3], 0x7531);
+    hi.z = __byte_perm(p[4], p[5], 0x7531);
+    hi.w = __byte_perm(p[6], p[7], 0x7531);
+}
+
+// 4 low bytes + 4 high bytes -> 2 packed words of int16 pairs.
+__device__ __forceinline__ void join_bytes(uint32_t lo, uint32_t hi, uint32_t& p0, uint32_t& p1) {
+    p0 = __byte_perm(lo, hi, 0x5140);
+    p1 = __byte_perm(lo, hi, 0x7362);
+}
+
+// Phase 2 of 16 conv outputs (packed pairs p) of one pixel, output channels
+// cbase .. cbase + 15, in the order of src/layers.cpp:91-104.
+template <int MODE>
+__device__ __forceinline__ void finish16(const ConvTcArgs& a, uint32_t (&p)[8], int cbase, int n_valid,
+                                         long long opx, long long rpx1, long long rpx2, const Act& out) {
+    const Epilogue& e = a.epi;
+    if (MODE == kEpiLut) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const int64_t sum = static_cast<int64_t>(static_cast<int32_t>(ll[j])) +
-                            256 * static_cast<int64_t>(static_cast<int32_t>(xx[j])) +
-                            65536 * static_cast<int64_t>(static_cast<int32_t>(hh[j]));
-        v[j] = cbase + j < args.co ? epilogue_value(sum, cbase + j, args) : int16_t(0);
+        for (int i = 0; i < 8; ++i)
+            p[i] = pack2(__ldg(&e.lut[lo16(p[i]) + 32768]), __ldg(&e.lut[hi16(p[i]) + 32768]));
     }
-    const bool full = cbase + 16 <= args.co;
-    if (e.wsilu4) {
-        // four output channels cbase / 4 .. cbase / 4 + 3
-        uint8_t lo[4], hi[4];
+    if (MODE == kEpiRes) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const Act& res = r == 0 ? e.res1 : e.res2;
+            if (r == 1 && !res.base) break;
+            const long long rp = r == 0 ? rpx1 : rpx2;
+            uint4 rl, rh;
+            if (n_valid >= 16) {
+                rl = *reinterpret_cast<const uint4*>(res.lo(rp) + cbase);
+                rh = *reinterpret_cast<const uint4*>(res.hi(rp) + cbase);
+            } else {
+                uint8_t bl[16], bh[16];
+                for (int j = 0; j < 16; ++j) {
+                    bl[j] = j < n_valid ? res.lo(rp)[cbase + j] : 0;
+                    bh[j] = j < n_valid ? res.hi(rp)[cbase + j] : 0;
+                }
+                rl = *reinterpret_cast<const uint4*>(bl);
+                rh = *reinterpret_cast<const uint4*>(bh);
+            }
+            const uint32_t lw[4] = {rl.x, rl.y, rl.z, rl.w}, hw[4] = {rh.x, rh.y, rh.z, rh.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                uint32_t q0, q1;
+                join_bytes(lw[k], hw[k], q0, q1);
+                p[2 * k] = pack2(clamp16(lo16(p[2 * k]) + lo16(q0)), clamp16(hi16(p[2 * k]) + hi16(q0)));
+                p[2 * k + 1] = pack2(clamp16(lo16(p[2 * k + 1]) + lo16(q1)), clamp16(hi16(p[2 * k + 1]) + hi16(q1)));
+            }
+        }
+    }
+    if (MODE == kEpiWsilu4) {
+        // out[c] = sat(sum_{k<4} lut[v[4c + k]]): four output channels cbase / 4 ..
+        int32_t r[4];
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-            int32_t s = 0;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) s += __ldg(&e.lut[static_cast<int32_t>(v[4 * g + t]) + 32768]);
-            const int16_t r = sat16i(s);
-            lo[g] = static_cast<uint8_t>(r & 0xff);
-            hi[g] = static_cast<uint8_t>((r >> 8) & 0xff);
+            const int32_t s = __ldg(&e.lut[lo16(p[2 * g]) + 32768]) + __ldg(&e.lut[hi16(p[2 * g]) + 32768]) +
+                              __ldg(&e.lut[lo16(p[2 * g + 1]) + 32768]) + __ldg(&e.lut[hi16(p[2 * g + 1]) + 32768]);
+            r[g] = clamp16(s);
         }
-        const long long opx = spatial ? args.out.pixel(img, oy, ox) : px;
-        const int oc = cbase >> 2;
-        uint8_t* dl = args.out.lo(opx) + oc;
-        uint8_t* dh = args.out.hi(opx) + oc;
-        if (full) {
-            *reinterpret_cast<uint32_t*>(dl) = *reinterpret_cast<const uint32_t*>(lo);
-            *reinterpret_cast<uint32_t*>(dh) = *reinterpret_cast<const uint32_t*>(hi);
+        const uint32_t w0 = pack2(r[0], r[1]), w1 = pack2(r[2], r[3]);
+        uint8_t* dl = out.lo(opx) + (cbase >> 2);
+        uint8_t* dh = out.hi(opx) + (cbase >> 2);
+        if (n_valid >= 16) {
+            *reinterpret_cast<uint32_t*>(dl) = __byte_perm(w0, w1, 0x6420);
+            *reinterpret_cast<uint32_t*>(dh) = __byte_perm(w0, w1, 0x7531);
         } else {
-            for (int g = 0; g < 4 && 4 * g + cbase < args.co; ++g) {
-                dl[g] = lo[g];
-                dh[g] = hi[g];
+            for (int g = 0; g < 4 && 4 * g < n_valid; ++g) {
+                dl[g] = static_cast<uint8_t>(r[g] & 0xff);
+                dh[g] = static_cast<uint8_t>((r[g] >> 8) & 0xff);
             }
         }
         return;
     }
-    if (e.shuffle2) {
-        // channel 4c + 2i + j of pixel (oy, ox) -> channel c of pixel (2oy + i, 2ox + j)
-        const int c0 = cbase >> 2;
-#pragma unroll
-        for (int ij = 0; ij < 4; ++ij) {
-            const long long opx = args.out.pixel(img, 2 * oy + (ij >> 1), 2 * ox + (ij & 1));
-            uint8_t* dl = args.out.lo(opx) + c0;
-            uint8_t* dh = args.out.hi(opx) + c0;
-            for (int g = 0; g < 4; ++g) {
-                if (cbase + 4 * g + ij >= args.co) break;
-                const int16_t r = v[4 * g + ij];
-                dl[g] = static_cast<uint8_t>(r & 0xff);
-                dh[g] = static_cast<uint8_t>((r >> 8) & 0xff);
-            }
-        }
-        return;
-    }
-    if (e.lut) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = __ldg(&e.lut[static_cast<int32_t>(v[j]) + 32768]);
-    }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        const Act& res = r == 0 ? args.res1 : args.res2;
-        if (!res.base) continue;
-        const long long rpx = spatial ? res.pixel(img, oy, ox) : px;
-        const uint8_t* rl = res.lo(rpx) + cbase;
-        const uint8_t* rh = res.hi(rpx) + cbase;
-        uint8_t bl[16], bh[16];
-        if (full) {
-            *reinterpret_cast<uint4*>(bl) = *reinterpret_cast<const uint4*>(rl);
-            *reinterpret_cast<uint4*>(bh) = *reinterpret_cast<const uint4*>(rh);
-        } else {
-            for (int j = 0; j < 16; ++j) {
-                bl[j] = cbase + j < args.co ? rl[j] : 0;
-                bh[j] = cbase + j < args.co ? rh[j] : 0;
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = sat16i(static_cast<int32_t>(v[j]) + join16(bl[j], bh[j]));
-    }
-    if (e.mulq) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int32_t q = cbase + j < args.co ? __ldg(&e.mulq[cbase + j]) : 0;
-            v[j] = sat16(rna_shift(static_cast<int64_t>(v[j]) * q, 9));
-        }
-    }
-    uint8_t ol[16], oh8[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        ol[j] = static_cast<uint8_t>(v[j] & 0xff);
-        oh8[j] = static_cast<uint8_t>((v[j] >> 8) & 0xff);
-    }
-    const long long opx = spatial ? args.out.pixel(img, oy, ox) : px;
-    uint8_t* dl = args.out.lo(opx) + cbase;
-    uint8_t* dh = args.out.hi(opx) + cbase;
-    if (full) {
-        *reinterpret_cast<uint4*>(dl) = *reinterpret_cast<const uint4*>(ol);
-        *reinterpret_cast<uint4*>(dh) = *reinterpret_cast<const uint4*>(oh8);
+    if (MODE == kEpiShuffle2) return;  // stored by the caller, which knows the four target pixels
+    uint4 lo, hi;
+    split_bytes(p, lo, hi);
+    uint8_t* dl = out.lo(opx) + cbase;
+    uint8_t* dh = out.hi(opx) + cbase;
+    if (n_valid >= 16) {
+        *reinterpret_cast<uint4*>(dl) = lo;
+        *reinterpret_cast<uint4*>(dh) = hi;
     } else {
-        for (int j = 0; j < 16 && cbase + j < args.co; ++j) {
-            dl[j] = ol[j];
-            dh[j] = oh8[j];
+        const uint8_t* bl = reinterpret_cast<const uint8_t*>(&lo);
+        const uint8_t* bh = reinterpret_cast<const uint8_t*>(&hi);
+        for (int j = 0; j < n_valid; ++j) {
+            dl[j] = bl[j];
+            dh[j] = bh[j];
         }
     }
 }
 
-template <int BN, bool SPATIAL>
+// pixel_shuffle(2) store: channel 4c + 2i + j of pixel (oy, ox) -> channel c
+// of pixel (2 oy + i, 2 ox + j).
+__device__ __forceinline__ void store_shuffle2(const Act& out, const uint32_t (&p)[8], int cbase, int n_valid,
+                                               int img, int oy, int ox) {
+    const int c0 = cbase >> 2;
+    int32_t v[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[2 * i] = lo16(p[i]);
+        v[2 * i + 1] = hi16(p[i]);
+    }
+#pragma unroll
+    for (int ij = 0; ij < 4; ++ij) {
+        const long long opx = out.pixel(img, 2 * oy + (ij >> 1), 2 * ox + (ij & 1));
+        uint8_t* dl = out.lo(opx) + c0;
+        uint8_t* dh = out.hi(opx) + c0;
+        if (n_valid >= 16) {
+            const uint32_t w0 = pack2(v[ij], v[4 + ij]), w1 = pack2(v[8 + ij], v[12 + ij]);
+            *reinterpret_cast<uint32_t*>(dl) = __byte_perm(w0, w1, 0x6420);
+            *reinterpret_cast<uint32_t*>(dh) = __byte_perm(w0, w1, 0x7531);
+        } else {
+            for (int g = 0; g < 4 && 4 * g + ij < n_valid; ++g) {
+                dl[g] = static_cast<uint8_t>(v[4 * g + ij] & 0xff);
+                dh[g] = static_cast<uint8_t>((v[4 * g + ij] >> 8) & 0xff);
+            }
+        }
+    }
+}
+
+template <bool SPATIAL, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    const ConvTcArgs args) {
-    using Cfg = TcConfig<BN>;
-    constexpr int S = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t full_bar[S];
-    __shared__ __align__(8) uint64_t empty_bar[S];
-    __shared__ __align__(8) uint64_t accum_bar;
+    int32_t* bias_s = reinterpret_cast<int32_t*>(smem + size_t(kStages) * kStageBytes);  // [n_tiles * 128]
+    __shared__ __align__(8) uint64_t full_bar[kStages];
+    __shared__ __align__(8) uint64_t empty_bar[kStages];
+    __shared__ __align__(8) uint64_t tmem_full;
+    __shared__ __align__(8) uint64_t tmem_empty;
     __shared__ uint32_t tmem_holder;
     __shared__ int consumed;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int co0 = blockIdx.y * BN;
-
-    int img = 0, y0 = 0, x0 = 0;
-    long long p0 = 0;
-    if (SPATIAL) {
-        int t = blockIdx.x;
-        const int tx = t % args.tiles_x;
-        t /= args.tiles_x;
-        const int ty = t % args.tiles_y;
-        img = t / args.tiles_y;
-        x0 = tx * args.tile_w;
-        y0 = ty * args.tile_h;
-    } else {
-        p0 = static_cast<long long>(blockIdx.x) * kBM;
-    }
     const int kb_per_tap = (args.ci + kBK - 1) / kBK;
     const int num_k = args.taps_h * args.taps_w * kb_per_tap;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
-        mbar_init(&accum_bar, 1);
+        mbar_init(&tmem_full, 1);
+        mbar_init(&tmem_empty, kEpiWarps);
         consumed = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(&tmem_holder, Cfg::kTmemCols);
+        tmem_alloc(&tmem_holder, kTmemCols);
         tmem_relinquish();
+    }
+    // the whole bias vector, zero padded to the tile grid, once per CTA
+    for (int i = threadIdx.x; i < args.n_tiles * kBN; i += kThreads) {
+        int32_t b = 0;
+        if (args.epi.bias && i < args.co)
+            b = args.epi.bias32 ? static_cast<const int32_t*>(args.epi.bias)[i]
+                                : static_cast<const int16_t*>(args.epi.bias)[i];
+        bias_s[i] = b;
     }
     tc_fence_before();
     __syncthreads();
@@ -233,92 +297,171 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         if (lane == 0) {
             prefetch_tmap(&mapA);
             prefetch_tmap(&mapB);
-            for (int k = 0; k < num_k; ++k) {
-                const int s = k % S;
-                const uint32_t round = k / S;
-                if (k >= S && !mbar_wait(&empty_bar[s], (round - 1) & 1, args.status, 1)) break;
-                const int tap = k / kb_per_tap, cb = k - tap * kb_per_tap;
-                const int ky = tap / args.taps_w, kx = tap - ky * args.taps_w;
-                uint8_t* st = smem + size_t(s) * Cfg::kStageBytes;
-                mbar_arrive_expect_tx(&full_bar[s], Cfg::kStageBytes);
-                const int c0 = cb * kBK;
-                if (SPATIAL) {
-                    const int ix = x0 + kx - args.pad_w, iy = y0 + ky - args.pad_h;
-                    tma_load_5d(st, &mapA, &full_bar[s], c0, 0, ix, iy, img);
-                    tma_load_5d(st + Cfg::kABytes, &mapA, &full_bar[s], c0, 1, ix, iy, img);
-                } else {
-                    tma_load_3d(st, &mapA, &full_bar[s], c0, 0, static_cast<int>(p0));
-                    tma_load_3d(st + Cfg::kABytes, &mapA, &full_bar[s], c0, 1, static_cast<int>(p0));
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x) {
+                const TileCoord tc = tile_coord<SPATIAL>(args, tile);
+                for (int k = 0; k < num_k; ++k, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t round = it / kStages;
+                    if (it >= kStages && !mbar_wait(&empty_bar[s], (round - 1) & 1, args.status, 1)) {
+                        ok = false;
+                        break;
+                    }
+                    const int tap = k / kb_per_tap, cb = k - tap * kb_per_tap;
+                    const int ky = tap / args.taps_w, kx = tap - ky * args.taps_w;
+                    uint8_t* st = smem + size_t(s) * kStageBytes;
+                    mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+                    const int c0 = cb * kBK;
+                    if (SPATIAL) {
+                        const int ix = tc.x0 + kx - args.pad_w, iy = tc.y0 + ky - args.pad_h;
+                        tma_load_5d(st, &mapA, &full_bar[s], c0, 0, ix, iy, tc.img);
+                        tma_load_5d(st + kABytes, &mapA, &full_bar[s], c0, 1, ix, iy, tc.img);
+                    } else {
+                        tma_load_3d(st, &mapA, &full_bar[s], c0, 0, static_cast<int>(tc.p0));
+                        tma_load_3d(st + kABytes, &mapA, &full_bar[s], c0, 1, static_cast<int>(tc.p0));
+                    }
+                    tma_load_2d(st + 2 * kABytes, &mapB, &full_bar[s], tap * args.cpad + c0, (tc.co0 / kBN) * 2 * kBN);
+                    issued = it + 1;
                 }
-                const int kw = tap * args.cpad + c0;
-                tma_load_3d(st + 2 * Cfg::kABytes, &mapB, &full_bar[s], kw, co0, 0);
-                tma_load_3d(st + 2 * Cfg::kABytes + Cfg::kBBytes, &mapB, &full_bar[s], kw, co0, 1);
-                issued = k + 1;
             }
         }
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t i_uu = i8_idesc(kBM, BN, false, false);
-            constexpr uint32_t i_su = i8_idesc(kBM, BN, true, false);
-            constexpr uint32_t i_us = i8_idesc(kBM, BN, false, true);
-            constexpr uint32_t i_ss = i8_idesc(kBM, BN, true, true);
-            const uint32_t d_ll = tmem, d_x = tmem + BN, d_hh = tmem + 2 * BN;
-            int k = 0;
-            for (; k < num_k; ++k) {
-                const int s = k % S;
-                const uint32_t round = k / S;
-                if (!mbar_wait(&full_bar[s], round & 1, args.status, 2)) break;
-                tc_fence_after();
-                const uint32_t base = smem_u32(smem + size_t(s) * Cfg::kStageBytes);
-#pragma unroll
-                for (int kk = 0; kk < kBK / 32; ++kk) {
-                    const uint64_t a_lo = sw128_desc(base + kk * 32);
-                    const uint64_t a_hi = sw128_desc(base + Cfg::kABytes + kk * 32);
-                    const uint64_t b_lo = sw128_desc(base + 2 * Cfg::kABytes + kk * 32);
-                    const uint64_t b_hi = sw128_desc(base + 2 * Cfg::kABytes + Cfg::kBBytes + kk * 32);
-                    const uint32_t acc = (k > 0 || kk > 0) ? 1u : 0u;
-                    mma_i8(d_ll, a_lo, b_lo, i_uu, acc);
-                    mma_i8(d_x, a_hi, b_lo, i_su, acc);
-                    mma_i8(d_x, a_lo, b_hi, i_us, 1u);
-                    mma_i8(d_hh, a_hi, b_hi, i_ss, acc);
+            constexpr uint32_t i_uu = i8_idesc(kBM, kBN, false, false);
+            constexpr uint32_t i_su = i8_idesc(kBM, kBN, true, false);
+            constexpr uint32_t i_us = i8_idesc(kBM, kBN, false, true);
+            constexpr uint32_t i_ss = i8_idesc(kBM, kBN, true, true);
+            constexpr uint32_t i_us2 = i8_idesc(kBM, 2 * kBN, false, true);
+            constexpr uint32_t i_ss2 = i8_idesc(kBM, 2 * kBN, true, true);
+            const uint32_t d_ll = tmem, d_x = tmem + kBN, d_hh = tmem + 2 * kBN;
+            int it = 0, ti = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x, ++ti) {
+                if (ti > 0 && !mbar_wait(&tmem_empty, (ti - 1) & 1, args.status, 3)) {
+                    ok = false;
+                    break;
                 }
-                mma_commit(&empty_bar[s]);
+                tc_fence_after();
+                for (int k = 0; k < num_k; ++k, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t round = it / kStages;
+                    if (!mbar_wait(&full_bar[s], round & 1, args.status, 2)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t base = smem_u32(smem + size_t(s) * kStageBytes);
+                    const uint32_t a_lo = base, a_hi = base + kABytes, b_lo = base + 2 * kABytes,
+                                   b_hi = b_lo + kBN * kBK;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 32; ++kk) {
+                        const uint32_t o = kk * 32;
+                        const bool first = k == 0 && kk == 0;
+                        if (args.signed_split) {
+                            mma_i8(d_ll, sw128_desc(a_lo + o), sw128_desc(b_lo + o), i_us2, first ? 0u : 1u);
+                            if (first) {
+                                mma_i8(d_x, sw128_desc(a_hi + o), sw128_desc(b_lo + o), i_ss, 1u);
+                                mma_i8(d_hh, sw128_desc(a_hi + o), sw128_desc(b_hi + o), i_ss, 0u);
+                            } else {
+                                mma_i8(d_x, sw128_desc(a_hi + o), sw128_desc(b_lo + o), i_ss2, 1u);
+                            }
+                        } else {
+                            const uint32_t acc = first ? 0u : 1u;
+                            mma_i8(d_ll, sw128_desc(a_lo + o), sw128_desc(b_lo + o), i_uu, acc);
+                            mma_i8(d_x, sw128_desc(a_hi + o), sw128_desc(b_lo + o), i_su, acc);
+                            mma_i8(d_x, sw128_desc(a_lo + o), sw128_desc(b_hi + o), i_us, 1u);
+                            mma_i8(d_hh, sw128_desc(a_hi + o), sw128_desc(b_hi + o), i_ss, acc);
+                        }
+                    }
+                    mma_commit(&empty_bar[s]);
+                }
+                if (!ok) break;
+                mma_commit(&tmem_full);
             }
-            consumed = k;
-            mma_commit(&accum_bar);
+            consumed = it;
         }
         __syncwarp();
     } else {
-        const bool ready = mbar_wait(&accum_bar, 0, args.status, 3);
-        tc_fence_after();
         const int quarter = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int cgroup = (warp - 2) >> 2;            // 0..3: columns [32 cgroup, 32 cgroup + 32)
         const int row = quarter * 32 + lane;
-        bool valid;
-        long long px;
-        int oy = 0, ox = 0;
-        if (SPATIAL) {
-            const int ty = row / args.tile_w, tx = row - ty * args.tile_w;
-            oy = y0 + ty;
-            ox = x0 + tx;
-            valid = oy < args.oh && ox < args.ow;
-            px = 0;
-        } else {
-            px = p0 + row;
-            valid = px < args.m_total;
-        }
-        valid = valid && ready;
-        constexpr int kHalfCols = BN / 2;
-        for (int col = half * kHalfCols; col < (half + 1) * kHalfCols; col += 16) {
-            uint32_t ll[16], xx[16], hh[16];
-            const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + col;
-            tmem_ld16(taddr, ll);
-            tmem_ld16(taddr + BN, xx);
-            tmem_ld16(taddr + 2 * BN, hh);
-            tmem_wait_ld();
-            const int cbase = co0 + col;
-            if (valid && cbase < args.co) store_chunk(args, ll, xx, hh, cbase, img, oy, ox, px, SPATIAL);
+        const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        const Act& out = args.out;
+        int ti = 0;
+        for (int tile = blockIdx.x; tile < args.total_tiles; tile += gridDim.x, ++ti) {
+            const TileCoord tc = tile_coord<SPATIAL>(args, tile);
+            bool valid;
+            long long opx = 0, rpx1 = 0, rpx2 = 0;
+            int oy = 0, ox = 0;
+            if (SPATIAL) {
+                const int ty = row / args.tile_w, tx = row - ty * args.tile_w;
+                oy = tc.y0 + ty;
+                ox = tc.x0 + tx;
+                valid = oy < args.oh && ox < args.ow;
+                if (MODE != kEpiShuffle2) opx = out.pixel(tc.img, oy, ox);
+                if (MODE == kEpiRes) {
+                    rpx1 = args.epi.res1.pixel(tc.img, oy, ox);
+                    rpx2 = args.epi.res2.pixel(tc.img, oy, ox);
+                }
+            } else {
+                opx = rpx1 = rpx2 = tc.p0 + row;
+                valid = opx < args.m_total;
+            }
+            if (!mbar_wait(&tmem_full, ti & 1, args.status, 4)) break;
+            tc_fence_after();
+            // phase 1: accumulators -> sat(rna(sum / 8192) + bias), 16 columns at a time
+            uint32_t packed[kCols / 2];
+#pragma unroll
+            for (int c = 0; c < kCols / 16; ++c) {
+                const int col = cgroup * kCols + c * 16;
+                uint32_t ll[16], xx[16], hh[16];
+                tmem_ld16(lane_addr + col, ll);
+                tmem_ld16(lane_addr + kBN + col, xx);
+                tmem_ld16(lane_addr + 2 * kBN + col, hh);
+                const int4* bq = reinterpret_cast<const int4*>(bias_s + tc.co0 + col);
+                const int4 b4[4] = {bq[0], bq[1], bq[2], bq[3]};
+                const int32_t* bias = reinterpret_cast<const int32_t*>(b4);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; j += 2) {
+                    int32_t r[2];
+#pragma unroll
+                    for (int t = 0; t < 2; ++t) {
+                        const int32_t L = static_cast<int32_t>(ll[j + t]), X = static_cast<int32_t>(xx[j + t]),
+                                      H = static_cast<int32_t>(hh[j + t]);
+                        if (args.wide) {
+                            const int64_t v = recombine64(L, X, H) + bias[j + t];
+                            r[t] = v < -32768 ? -32768 : (v > 32767 ? 32767 : static_cast<int32_t>(v));
+                        } else {
+                            const int64_t v = static_cast<int64_t>(recombine32(L, X, H)) + bias[j + t];
+                            r[t] = v < -32768 ? -32768 : (v > 32767 ? 32767 : static_cast<int32_t>(v));
+                        }
+                    }
+                    packed[c * 8 + j / 2] = pack2(r[0], r[1]);
+                }
+            }
+            // TMEM is free for the next tile's MMAs
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty);
+            // phase 2: fused elementwise steps and stores, overlapped with the next MMAs
+            if (valid) {
+#pragma unroll
+                for (int c = 0; c < kCols / 16; ++c) {
+                    const int cbase = tc.co0 + cgroup * kCols + c * 16;
+                    if (cbase >= args.co) break;
+                    const int n_valid = args.co - cbase < 16 ? args.co - cbase : 16;
+                    uint32_t p8[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) p8[i] = packed[c * 8 + i];
+                    if (MODE == kEpiShuffle2)
+                        store_shuffle2(out, p8, cbase, n_valid, tc.img, oy, ox);
+                    else
+                        finish16<MODE>(args, p8, cbase, n_valid, opx, rpx1, rpx2, out);
+                }
+            }
             __syncwarp();
         }
     }
@@ -326,21 +469,47 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
     tc_fence_before();
     __syncthreads();
     if (warp == 0 && lane == 0) {
-        // Drain TMA loads that were issued but never consumed (abort path only),
-        // so no copy into this CTA's shared memory outlives the CTA.
-        for (int k = consumed; k < issued; ++k) {
-            mbar_wait(&full_bar[k % S], (k / S) & 1, args.status, 4);
-        }
+        // abort path only: wait for TMA loads issued but never consumed, so no
+        // copy into this CTA's shared memory outlives the CTA
+        for (int k = consumed; k < issued; ++k) mbar_wait(&full_bar[k % kStages], (k / kStages) & 1, args.status, 5);
     }
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, Cfg::kTmemCols);
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// [co_tiles][2][128][kpad]: tile rows 0..127 low bytes, 128..255 high bytes.
+__global__ void prep_tc_weights_kernel(const int16_t* __restrict__ w, int co, int ci, int kh, int kw, int cpad,
+                                       int kpad, int co_tiles, int signed_split, uint8_t* __restrict__ planes) {
+    const long long total = static_cast<long long>(co_tiles) * 2 * kBN * kpad;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int k = static_cast<int>(i % kpad);
+        const long long rowg = i / kpad;  // tile * 256 + r
+        const int r = static_cast<int>(rowg % (2 * kBN));
+        const int tile = static_cast<int>(rowg / (2 * kBN));
+        const int plane = r / kBN;
+        const int o = tile * kBN + (r - plane * kBN);
+        const int tap = k / cpad, c = k - tap * cpad;
+        int32_t v = 0;
+        if (o < co && c < ci) {
+            const int ky = tap / kw, kx = tap - ky * kw;
+            v = w[((static_cast<long long>(o) * ci + c) * kh + ky) * kw + kx];
+        }
+        int32_t lo, hi;
+        if (signed_split) {
+            lo = ((v + 128) & 255) - 128;
+            hi = (v - lo) >> 8;
+        } else {
+            lo = v & 255;
+            hi = v >> 8;
+        }
+        planes[i] = static_cast<uint8_t>((plane ? hi : lo) & 0xff);
     }
 }
 
 // ------------------------------------------------------------------ host ----
-
-namespace {
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -378,30 +547,88 @@ bool encode(CUtensorMap* map, void* base, int rank, const cuuint64_t* dims, cons
     return true;
 }
 
-template <int BN, bool SPATIAL>
-cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b, const ConvTcArgs& args, dim3 grid,
-                   cudaStream_t stream) {
-    using Cfg = TcConfig<BN>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(conv_i16_tc_kernel<BN, SPATIAL>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(Cfg::kSmem));
-        if (e != cudaSuccess) return e;
-        configured = true;
+std::mutex g_dev_mutex;
+std::vector<int> g_sms;
+
+int sm_count(int device) {
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    if (static_cast<size_t>(device) >= g_sms.size()) g_sms.resize(device + 1, 0);
+    if (!g_sms[device]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) == cudaSuccess) g_sms[device] = n;
     }
-    conv_i16_tc_kernel<BN, SPATIAL><<<grid, kThreads, Cfg::kSmem, stream>>>(a, b, args);
+    return g_sms[device] > 0 ? g_sms[device] : 148;
+}
+
+template <bool SPATIAL, int MODE>
+cudaError_t launch_mode(const CUtensorMap& a, const CUtensorMap& b, const ConvTcArgs& args, cudaStream_t stream) {
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return e;
+    const size_t smem = kRingBytes + size_t(args.n_tiles) * kBN * sizeof(int32_t);
+    // the attribute is per function and device; setting it each launch is cheap
+    e = cudaFuncSetAttribute(conv_i16_tc_kernel<SPATIAL, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    const int sms = sm_count(device);
+    const int grid = args.total_tiles < sms ? args.total_tiles : sms;
+    conv_i16_tc_kernel<SPATIAL, MODE><<<grid, kThreads, smem, stream>>>(a, b, args);
     return cudaGetLastError();
+}
+
+template <bool SPATIAL>
+cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b, const ConvTcArgs& args, cudaStream_t stream) {
+    const Epilogue& e = args.epi;
+    if (e.shuffle2) return launch_mode<SPATIAL, kEpiShuffle2>(a, b, args, stream);
+    if (e.wsilu4) return launch_mode<SPATIAL, kEpiWsilu4>(a, b, args, stream);
+    if (e.lut) return launch_mode<SPATIAL, kEpiLut>(a, b, args, stream);
+    if (e.res1.base) return launch_mode<SPATIAL, kEpiRes>(a, b, args, stream);
+    return launch_mode<SPATIAL, kEpiPlain>(a, b, args, stream);
 }
 
 }  // namespace
 
-bool tc_weight_map(const TcWeights& w, int bn, CUtensorMap* map, std::string& err) {
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(w.kpad), static_cast<cuuint64_t>(w.co), 2};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(w.kpad),
-                                   static_cast<cuuint64_t>(w.kpad) * static_cast<cuuint64_t>(w.co)};
-    const cuuint32_t box[3] = {kBK, static_cast<cuuint32_t>(bn), 1};
-    return encode(map, w.planes, 3, dims, strides, box, err);
+size_t tc_weight_bytes(int co, int ci, int kh, int kw) {
+    const int cpad = (ci + kBK - 1) / kBK * kBK;
+    const int co_tiles = (co + kBN - 1) / kBN;
+    return static_cast<size_t>(co_tiles) * 2 * kBN * kh * kw * cpad;
+}
+
+bool tc_signed_split_ok(const int16_t* weight_host, size_t count) {
+    for (size_t i = 0; i < count; ++i)
+        if (weight_host[i] > 32639) return false;
+    return true;
+}
+
+bool tc_describe(TcWeights& w, int co, int ci, int kh, int kw, bool signed_split, uint8_t* planes, std::string& err) {
+    w.co = co;
+    w.ci = ci;
+    w.kh = kh;
+    w.kw = kw;
+    w.cpad = (ci + kBK - 1) / kBK * kBK;
+    w.kpad = kh * kw * w.cpad;
+    w.co_tiles = (co + kBN - 1) / kBN;
+    w.signed_split = signed_split;
+    w.planes = planes;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w.kpad), static_cast<cuuint64_t>(w.co_tiles) * 2 * kBN};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w.kpad)};
+    const cuuint32_t box[2] = {kBK, 2 * kBN};
+    return encode(&w.map, planes, 2, dims, strides, box, err);
+}
+
+bool tc_prepare(TcWeights& w, const int16_t* weight, int co, int ci, int kh, int kw, bool signed_split,
+                uint8_t* planes, cudaStream_t s, std::string& err) {
+    if (!tc_describe(w, co, ci, kh, kw, signed_split, planes, err)) return false;
+    const long long total = static_cast<long long>(w.co_tiles) * 2 * kBN * w.kpad;
+    const long long blocks = (total + 255) / 256;
+    prep_tc_weights_kernel<<<static_cast<unsigned>(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, s>>>(
+        weight, co, ci, kh, kw, w.cpad, w.kpad, w.co_tiles, signed_split ? 1 : 0, planes);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        err = std::string("weight preparation: ") + cudaGetErrorString(e);
+        return false;
+    }
+    return true;
 }
 
 int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogue& epi, int pad_h, int pad_w,
@@ -426,11 +653,18 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
             return -1;
         }
     }
-    if (epi.shuffle2 && (epi.lut || epi.wsilu4 || epi.res1.base || epi.res2.base || epi.mulq)) {
-        err = "pixel-shuffle store supports the plain epilogue only";
+    const int modes = (epi.shuffle2 ? 1 : 0) + (epi.wsilu4 ? 1 : 0) + (epi.lut && !epi.wsilu4 ? 1 : 0) +
+                      (epi.res1.base ? 1 : 0);
+    if (modes > 1 || epi.mulq || (epi.res2.base && !epi.res1.base)) {
+        err = "unsupported epilogue combination (one of lut, residual adds, wsilu4, pixel shuffle; no multiply)";
         return -1;
     }
-    if (static_cast<long long>(w.kh) * w.kw * w.ci > 32768) {
+    if (w.co_tiles * kBN * sizeof(int32_t) + kRingBytes > 227 * 1024) {
+        err = "too many output channels for the staged bias";
+        return -1;
+    }
+    const long long k_total = static_cast<long long>(w.kh) * w.kw * w.ci;
+    if (k_total > 32768) {
         err = "reduction exceeds the exact s32 accumulator bound";
         return -1;
     }
@@ -440,8 +674,6 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     ConvTcArgs args{};
     args.out = out;
     args.epi = epi;
-    args.res1 = epi.res1;
-    args.res2 = epi.res2;
     args.co = w.co;
     args.ci = w.ci;
     args.taps_h = w.kh;
@@ -449,22 +681,21 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     args.pad_h = pad_h;
     args.pad_w = pad_w;
     args.cpad = w.cpad;
-    args.n = in.n;
     args.oh = oh;
     args.ow = ow;
+    args.signed_split = w.signed_split ? 1 : 0;
+    args.wide = k_total >= 16384 ? 1 : 0;
     args.status = status;
-
-    const int bn = w.co <= 64 ? 64 : 128;
-    const CUtensorMap* bmap = bn == 128 ? &w.map128 : &w.map64;
+    args.n_tiles = w.co_tiles;
     CUtensorMap amap;
-    dim3 grid;
+    long long m_tiles;
     if (flat) {
         const cuuint64_t dims[3] = {static_cast<cuuint64_t>(in.c), 2, static_cast<cuuint64_t>(in.pixels())};
         const cuuint64_t strides[2] = {static_cast<cuuint64_t>(in.pitch), static_cast<cuuint64_t>(2 * in.pitch)};
         const cuuint32_t box[3] = {kBK, 1, kBM};
         if (!encode(&amap, in.base, 3, dims, strides, box, err)) return -1;
         args.m_total = in.pixels();
-        grid = dim3(static_cast<unsigned>((in.pixels() + kBM - 1) / kBM), (w.co + bn - 1) / bn, 1);
+        m_tiles = (in.pixels() + kBM - 1) / kBM;
     } else {
         const int tw = ow >= 12 ? 16 : 8;
         const int th = kBM / tw;
@@ -479,13 +710,15 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
                                        static_cast<cuuint64_t>(2 * in.pitch) * in.img_px};
         const cuuint32_t box[5] = {kBK, 1, static_cast<cuuint32_t>(tw), static_cast<cuuint32_t>(th), 1};
         if (!encode(&amap, in.base, 5, dims, strides, box, err)) return -1;
-        grid = dim3(static_cast<unsigned>(args.tiles_x * args.tiles_y * in.n), (w.co + bn - 1) / bn, 1);
+        m_tiles = static_cast<long long>(args.tiles_x) * args.tiles_y * in.n;
     }
-    cudaError_t e;
-    if (bn == 128)
-        e = flat ? launch<128, false>(amap, *bmap, args, grid, stream) : launch<128, true>(amap, *bmap, args, grid, stream);
-    else
-        e = flat ? launch<64, false>(amap, *bmap, args, grid, stream) : launch<64, true>(amap, *bmap, args, grid, stream);
+    const long long total = m_tiles * w.co_tiles;
+    if (total > INT32_MAX) {
+        err = "too many output tiles";
+        return -1;
+    }
+    args.total_tiles = static_cast<int>(total);
+    const cudaError_t e = flat ? launch<false>(amap, w.map, args, stream) : launch<true>(amap, w.map, args, stream);
     if (e != cudaSuccess) {
         err = std::string("conv launch failed: ") + cudaGetErrorString(e);
         return -1;

@@ -9,18 +9,37 @@
 
 namespace ufb {
 
-// Device-resident convolution weights prepared for the tensor-core kernel:
-// two planes [2][co][kpad] bytes -- plane 0 holds the low bytes (u8), plane 1
-// the high bytes (s8) -- with k = (ky * kw + kx) * cpad + c and zero padding
-// for c >= ci.  cpad = ci rounded up to 128, kpad = kh * kw * cpad.
+// Output channels per tensor-core tile (one 128-lane TMEM accumulator set).
+constexpr int kTcTileN = 128;
+
+// Device-resident convolution weights prepared for the tensor-core kernel.
+// Layout: [co_tiles][2][128][kpad] bytes -- per tile of 128 output channels,
+// 128 rows of the weights' low bytes followed by 128 rows of their high bytes,
+// k = (ky * kw + kx) * cpad + c, zero rows / columns as padding.
+//   unsigned split (any weights):   w = lo + 256 hi, lo u8 = w & 0xff, hi s8 = w >> 8
+//   signed split (w <= 32639):      w = lo + 256 hi, lo s8 in [-128, 127], hi s8
+// The signed split lets one MMA over the stacked 256 rows produce two partial
+// products (see conv_tc.cu), halving the MMA count.
 struct TcWeights {
     uint8_t* planes = nullptr;
-    int co = 0, ci = 0, kh = 0, kw = 0, cpad = 0, kpad = 0;
-    CUtensorMap map128{};  // TMA map with a 128-row box
-    CUtensorMap map64{};   // TMA map with a 64-row box
+    int co = 0, ci = 0, kh = 0, kw = 0, cpad = 0, kpad = 0, co_tiles = 0;
+    bool signed_split = false;
+    CUtensorMap map{};  // TMA map over the [co_tiles * 256][kpad] byte matrix, 256-row box
 };
 
-bool tc_weight_map(const TcWeights& w, int bn, CUtensorMap* map, std::string& err);
+// Bytes needed for the prepared planes of a [co, ci, kh, kw] convolution.
+size_t tc_weight_bytes(int co, int ci, int kh, int kw);
+
+// Describe already prepared planes (fields + TMA map; no device work).
+bool tc_describe(TcWeights& w, int co, int ci, int kh, int kw, bool signed_split, uint8_t* planes, std::string& err);
+
+// tc_describe plus the preparation of int16 weights already on the device
+// into `planes` (tc_weight_bytes bytes), launched on stream s.
+bool tc_prepare(TcWeights& w, const int16_t* weight, int co, int ci, int kh, int kw, bool signed_split,
+                uint8_t* planes, cudaStream_t s, std::string& err);
+
+// True when every weight allows the signed split (host data).
+bool tc_signed_split_ok(const int16_t* weight_host, size_t count);
 
 // out = epilogue(conv(in, w)), stride 1, zero padding (pad_h, pad_w).
 // Both views must have 16-byte aligned pitch and base.  Asynchronous on

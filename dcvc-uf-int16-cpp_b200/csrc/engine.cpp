@@ -122,6 +122,7 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
         return d;
     };
     const HostTensor *zc = nullptr, *zl = nullptr, *yc = nullptr, *yl = nullptr;
+    std::map<std::string, bool> signed_ok;  // every weight <= 32639: signed byte split allowed
     for (const auto& t : tensors) {
         names_.insert(t.name);
         size_t numel = 1;
@@ -134,6 +135,8 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
             L.kh = static_cast<int>(t.shape[2]);
             L.kw = static_cast<int>(t.shape[3]);
             L.weights16 = static_cast<int16_t*>(upload(t.data, numel * 2));
+            signed_ok[t.name.substr(0, t.name.size() - 7)] =
+                tc_signed_split_ok(static_cast<const int16_t*>(t.data), numel);
         } else if (ends(t.name, ".bias")) {
             if (t.dtype != 0 || t.shape.size() != 1) throw std::invalid_argument("bias must be int16 1-D: " + t.name);
             convs_[t.name.substr(0, t.name.size() - 5)].bias = static_cast<int16_t*>(upload(t.data, numel * 2));
@@ -175,20 +178,12 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
         if (!L.weights16) throw std::runtime_error("Missing prepared UF tensor: " + kv.first + ".weight");
         L.depthwise = L.ci == 1 && L.co > 1;
         if (L.depthwise || static_cast<long long>(L.ci) * L.kh * L.kw > 32768) continue;
-        L.tc.co = L.co;
-        L.tc.ci = L.ci;
-        L.tc.kh = L.kh;
-        L.tc.kw = L.kw;
-        L.tc.cpad = (L.ci + 127) / 128 * 128;
-        L.tc.kpad = L.kh * L.kw * L.tc.cpad;
         void* planes = nullptr;
-        ck(cudaMalloc(&planes, static_cast<size_t>(2) * L.co * L.tc.kpad), "weight planes");
+        ck(cudaMalloc(&planes, tc_weight_bytes(L.co, L.ci, L.kh, L.kw)), "weight planes");
         allocations_.push_back(planes);
-        L.tc.planes = static_cast<uint8_t*>(planes);
-        ck(prep_weights(L.weights16, L.co, L.ci, L.kh, L.kw, L.tc.cpad, L.tc.kpad, L.tc.planes, nullptr),
-           "weight preparation");
         std::string err;
-        if (!tc_weight_map(L.tc, 128, &L.tc.map128, err) || !tc_weight_map(L.tc, 64, &L.tc.map64, err))
+        if (!tc_prepare(L.tc, L.weights16, L.co, L.ci, L.kh, L.kw, signed_ok[kv.first], static_cast<uint8_t*>(planes),
+                        nullptr, err))
             throw std::runtime_error(err);
     }
     ck(cudaDeviceSynchronize(), "model upload");

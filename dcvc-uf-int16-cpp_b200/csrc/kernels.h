@@ -8,8 +8,6 @@
 
 namespace ufb {
 
-cudaError_t prep_weights(const int16_t* w, int co, int ci, int kh, int kw, int cpad, int kpad, uint8_t* planes,
-                         cudaStream_t s);
 cudaError_t nchw_to_split(const int16_t* x, int n, int c, int h, int w, int f, const Act& out, cudaStream_t s);
 cudaError_t split_to_nchw(const Act& in, int f, int16_t* out, cudaStream_t s);
 cudaError_t conv_direct(int16_t* out, const int16_t* x, const int16_t* weight, const void* bias, int bias32, int n,

@@ -1,4 +1,4 @@
-// Memory-bound INT16 kernels: weight preparation, layout conversion between
+// Memory-bound INT16 kernels: layout conversion between
 // the reference's NCHW tensors and split NHWC, the direct (grouped / strided /
 // depthwise) convolution, the elementwise operators of the reference's CUDA
 // extension (src/cuda/elementwise.cu:16-46) and the fixed-point warp.
@@ -16,25 +16,6 @@ constexpr int kBlock = 256;
 inline unsigned blocks_for(long long n, int per_thread = 1) {
     const long long t = (n + per_thread - 1) / per_thread;
     return static_cast<unsigned>((t + kBlock - 1) / kBlock);
-}
-
-// int16 [co][cig][kh][kw] -> planes [2][co][kpad], k = (ky*kw + kx)*cpad + c.
-__global__ void prep_weights_kernel(const int16_t* __restrict__ w, int co, int ci, int kh, int kw, int cpad,
-                                    int kpad, uint8_t* __restrict__ planes) {
-    const long long total = static_cast<long long>(co) * kpad;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int o = static_cast<int>(i / kpad);
-        const int k = static_cast<int>(i - static_cast<long long>(o) * kpad);
-        const int tap = k / cpad, c = k - tap * cpad;
-        int16_t v = 0;
-        if (c < ci) {
-            const int ky = tap / kw, kx = tap - ky * kw;
-            v = w[((static_cast<long long>(o) * ci + c) * kh + ky) * kw + kx];
-        }
-        planes[i] = static_cast<uint8_t>(v & 0xff);
-        planes[total + i] = static_cast<uint8_t>((v >> 8) & 0xff);
-    }
 }
 
 // NCHW int16 (n, c, h, w) -> split view of (n, h/f, w/f, c*f*f):
@@ -112,48 +93,84 @@ __global__ void conv_direct_kernel(int16_t* __restrict__ out, const int16_t* __r
 }
 
 // Depthwise 3x3, stride 1, zero padding 1 on split views (DepthConvBlock dc.2,
-// src/layers.cpp:96).  One thread per (pixel, 8 channels).
-__global__ void dwconv3x3_kernel(Act in, Act out, const int16_t* __restrict__ weight, const int16_t* __restrict__ bias) {
-    const int cg = in.c / 8;
-    const long long total = in.pixels() * cg;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int g = static_cast<int>(i % cg);
-        long long p = i / cg;
-        const int x = static_cast<int>(p % in.w);
-        p /= in.w;
-        const int y = static_cast<int>(p % in.h);
-        const int b = static_cast<int>(p / in.h);
-        const int c0 = g * 8;
-        int64_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+// src/layers.cpp:96; the reference runs it through its scalar `general`
+// kernel, src/cuda/conv.cu:44-60).  A CTA stages an (8 + 2) x (32 + 2) pixel
+// tile of 64 channels (both byte planes) in shared memory once, then each
+// thread produces 8 channels of 8 output pixels.  Accumulation stays in int32
+// by keeping the planes apart: S_lo = sum lo * w and S_hi = sum hi * w
+// (|S| < 2^27 for 9 taps), and the exact rna(S_lo + 256 S_hi, 8192) is formed
+// without 64-bit arithmetic.
+constexpr int kDwTileW = 32, kDwTileH = 8, kDwC = 64, kDwThreads = 256;
+constexpr int kDwInW = kDwTileW + 2, kDwInH = kDwTileH + 2;
+
+__device__ __forceinline__ int32_t rna8192_split(int32_t s_lo, int32_t s_hi) {
+    const int32_t R = ((s_hi & 31) << 8) + (s_lo & 8191);
+    const int32_t T = (s_hi >> 5) + (s_lo >> 13) + (R >> 13);
+    const int32_t Rl = R & 8191;
+    return T + ((Rl > 4096) | ((Rl == 4096) & (T >= 0)));
+}
+
+__global__ void __launch_bounds__(kDwThreads) dwconv3x3_kernel(Act in, Act out, const int16_t* __restrict__ weight,
+                                                               const int16_t* __restrict__ bias) {
+    __shared__ __align__(16) uint8_t tile[kDwInH * kDwInW][2 * kDwC];  // [pixel][lo 64 | hi 64]
+    __shared__ int32_t wsm[9][kDwC];
+    __shared__ int32_t bsm[kDwC];
+    const int x0 = blockIdx.x * kDwTileW, y0 = blockIdx.y * kDwTileH;
+    const int cgroups = (in.c + kDwC - 1) / kDwC;
+    const int b = blockIdx.z / cgroups, c0 = (blockIdx.z - b * cgroups) * kDwC;
+    const int cn = in.c - c0 < kDwC ? in.c - c0 : kDwC;  // channels in this group (multiple of 8)
+    for (int i = threadIdx.x; i < 9 * kDwC; i += kDwThreads) {
+        const int t = i / kDwC, c = i - t * kDwC;
+        wsm[t][c] = c < cn ? weight[(c0 + c) * 9 + t] : 0;
+    }
+    for (int c = threadIdx.x; c < kDwC; c += kDwThreads) bsm[c] = (bias && c < cn) ? bias[c0 + c] : 0;
+    // stage the input tile: 16-byte chunks, 4 per plane per pixel
+    for (int i = threadIdx.x; i < kDwInH * kDwInW * 8; i += kDwThreads) {
+        const int chunk = i & 7, p = i >> 3;
+        const int ty = p / kDwInW, tx = p - ty * kDwInW;
+        const int iy = y0 + ty - 1, ix = x0 + tx - 1;
+        const int plane = chunk >> 2, cc = (chunk & 3) * 16;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (iy >= 0 && iy < in.h && ix >= 0 && ix < in.w && cc < cn) {
+            const long long px = in.pixel(b, iy, ix);
+            v = *reinterpret_cast<const uint4*>((plane ? in.hi(px) : in.lo(px)) + c0 + cc);
+        }
+        *reinterpret_cast<uint4*>(&tile[p][plane * kDwC + cc]) = v;
+    }
+    __syncthreads();
+    const int g = threadIdx.x & 7;  // channel group of 8
+    if (g * 8 >= cn) return;
+    for (int item = threadIdx.x >> 3; item < kDwTileH * kDwTileW; item += kDwThreads / 8) {
+        const int ty = item / kDwTileW, tx = item - ty * kDwTileW;
+        const int oy = y0 + ty, ox = x0 + tx;
+        if (oy >= in.h || ox >= in.w) continue;
+        int32_t slo[8] = {0, 0, 0, 0, 0, 0, 0, 0}, shi[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-        for (int ky = 0; ky < 3; ++ky) {
-            const int iy = y + ky - 1;
-            if (iy < 0 || iy >= in.h) continue;
+        for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
             for (int kx = 0; kx < 3; ++kx) {
-                const int ix = x + kx - 1;
-                if (ix < 0 || ix >= in.w) continue;
-                const long long px = in.pixel(b, iy, ix);
-                const uint2 lo = *reinterpret_cast<const uint2*>(in.lo(px) + c0);
-                const uint2 hi = *reinterpret_cast<const uint2*>(in.hi(px) + c0);
+                const uint8_t* src = tile[(ty + ky) * kDwInW + tx + kx];
+                const uint2 lo = *reinterpret_cast<const uint2*>(src + g * 8);
+                const uint2 hi = *reinterpret_cast<const uint2*>(src + kDwC + g * 8);
                 const uint8_t* l = reinterpret_cast<const uint8_t*>(&lo);
-                const uint8_t* hh = reinterpret_cast<const uint8_t*>(&hi);
+                const int8_t* h = reinterpret_cast<const int8_t*>(&hi);
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    acc[j] += static_cast<int64_t>(join16(l[j], hh[j])) * __ldg(&weight[(c0 + j) * 9 + ky * 3 + kx]);
+                for (int j = 0; j < 8; ++j) {
+                    const int32_t wv = wsm[ky * 3 + kx][g * 8 + j];
+                    slo[j] += static_cast<int32_t>(l[j]) * wv;
+                    shi[j] += static_cast<int32_t>(h[j]) * wv;
+                }
             }
-        }
         uint8_t ol[8], oh8[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int16_t v = sat16(rna_div(acc[j], kWeightScale) + (bias ? bias[c0 + j] : 0));
+            const int16_t v = sat16i(rna8192_split(slo[j], shi[j]) + bsm[g * 8 + j]);
             ol[j] = static_cast<uint8_t>(v & 0xff);
             oh8[j] = static_cast<uint8_t>((v >> 8) & 0xff);
         }
-        const long long opx = out.pixel(b, y, x);
-        *reinterpret_cast<uint2*>(out.lo(opx) + c0) = *reinterpret_cast<const uint2*>(ol);
-        *reinterpret_cast<uint2*>(out.hi(opx) + c0) = *reinterpret_cast<const uint2*>(oh8);
+        const long long opx = out.pixel(b, oy, ox);
+        *reinterpret_cast<uint2*>(out.lo(opx) + c0 + g * 8) = *reinterpret_cast<const uint2*>(ol);
+        *reinterpret_cast<uint2*>(out.hi(opx) + c0 + g * 8) = *reinterpret_cast<const uint2*>(oh8);
     }
 }
 
@@ -252,13 +269,6 @@ unsigned grid_for(long long n) {
 
 }  // namespace
 
-cudaError_t prep_weights(const int16_t* w, int co, int ci, int kh, int kw, int cpad, int kpad, uint8_t* planes,
-                         cudaStream_t s) {
-    prep_weights_kernel<<<grid_for(static_cast<long long>(co) * kpad), kBlock, 0, s>>>(w, co, ci, kh, kw, cpad, kpad,
-                                                                                       planes);
-    return cudaGetLastError();
-}
-
 cudaError_t nchw_to_split(const int16_t* x, int n, int c, int h, int w, int f, const Act& out, cudaStream_t s) {
     nchw_to_split_kernel<<<grid_for(static_cast<long long>(n) * c * h * w), kBlock, 0, s>>>(x, n, c, h, w, f, out);
     return cudaGetLastError();
@@ -279,7 +289,13 @@ cudaError_t conv_direct(int16_t* out, const int16_t* x, const int16_t* weight, c
 }
 
 cudaError_t dwconv3x3(const Act& in, const Act& out, const int16_t* weight, const int16_t* bias, cudaStream_t s) {
-    dwconv3x3_kernel<<<grid_for(in.pixels() * (in.c / 8)), kBlock, 0, s>>>(in, out, weight, bias);
+    if (in.c % 8 || in.c != out.c || in.pitch % 16 || out.pitch % 16 ||
+        reinterpret_cast<uintptr_t>(in.base) % 16 || reinterpret_cast<uintptr_t>(out.base) % 16)
+        return cudaErrorInvalidValue;
+    const int cgroups = (in.c + kDwC - 1) / kDwC;
+    const dim3 grid((in.w + kDwTileW - 1) / kDwTileW, (in.h + kDwTileH - 1) / kDwTileH, in.n * cgroups);
+    if (grid.z > 65535) return cudaErrorInvalidValue;
+    dwconv3x3_kernel<<<grid, kDwThreads, 0, s>>>(in, out, weight, bias);
     return cudaGetLastError();
 }
 

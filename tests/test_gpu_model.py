@@ -206,3 +206,21 @@ def test_p_frame_without_reference_raises(ufb, models):
     with pytest.raises(ufb.UfbError) as e:
         c.decompress([b"\x00\x00\x80\x00"], W, H, 20, False)
     assert "no reference" in str(e.value)
+
+
+@pytest.mark.parametrize("extreme", [32639, 32767])
+def test_signed_split_weight_extremes(ufb, ref, syn, extreme):
+    """Weights at the edge of the signed byte split (<= 32639 uses it, 32767
+    forces the unsigned split) must give identical module outputs."""
+    t = dict(syn.prepared("htl", 2))
+    rng = np.random.default_rng(extreme)
+    for name in ("feature_extractor.conv.0.dc.0.weight", "feature_extractor.conv.0.ffn.0.weight",
+                 "feature_extractor.conv.1.ffn.2.weight"):
+        w = t[name].copy()
+        flat = w.reshape(-1)
+        idx = rng.choice(flat.size, flat.size // 3, replace=False)
+        flat[idx] = rng.choice(np.array([extreme, -32768, -1, 127, -128, 128, 255, -255], np.int16), idx.size)
+        t[name] = w
+    mine, theirs = ufb.Model("htl", t), ref.model("htl", t)
+    x = rng.integers(-6000, 6000, (1, 512, 6, 9)).astype(np.int16)
+    assert np.array_equal(mine.run("feature_extractor", x), theirs.run("feature_extractor", x))
