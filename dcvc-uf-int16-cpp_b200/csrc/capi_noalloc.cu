@@ -84,7 +84,7 @@ extern "C" int ufb_conv2d_noalloc(const int16_t* x, int n, int ci, int h, int w,
     }
     const int cip = round_up(ci, 16), cop = round_up(co, 16);
     const size_t x_bytes = align256(static_cast<size_t>(n) * h * w * 2 * cip);
-    const size_t w_bytes = align256(tc_weight_bytes(co, ci, kh, kw));
+    const size_t w_bytes = align256(tc_weight_bytes(co, ci, kh, kw, 128));
     const size_t o_bytes = align256(static_cast<size_t>(n) * oh * ow * 2 * cop);
     if (x_bytes + w_bytes + o_bytes > kNoAllocScratchBytes)
         return err(UFB_ERANGE, "convolution needs " + std::to_string(x_bytes + w_bytes + o_bytes) +
@@ -99,7 +99,7 @@ extern "C" int ufb_conv2d_noalloc(const int16_t* x, int n, int ci, int h, int w,
     TcWeights tw;
     std::string msg;
     // unsigned byte split: valid for any weights, needs no host inspection
-    if (!tc_prepare(tw, weight, co, ci, kh, kw, false, base + x_bytes, s, msg)) return err(UFB_ECUDA, msg);
+    if (!tc_prepare(tw, weight, co, ci, kh, kw, false, 128, base + x_bytes, s, msg)) return err(UFB_ECUDA, msg);
     const Act in = make_act(base, n, h, w, ci, cip);
     const Act ov = make_act(base + x_bytes + w_bytes, n, oh, ow, co, cop);
     if (!cuda_ok(nchw_to_split(x, n, ci, h, w, 1, in, s), "input layout")) return last_code();

@@ -55,13 +55,13 @@ int conv_tc_path(const int16_t* x, int n, int ci, int h, int w, const int16_t* w
     if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return last_code();
     const int cip = round_up(ci, 16), cop = round_up(co, 16);
     StreamBuffer xs(static_cast<size_t>(n) * h * w * 2 * cip, s);
-    StreamBuffer wp(tc_weight_bytes(co, ci, kh, kw), s);
+    StreamBuffer wp(tc_weight_bytes(co, ci, kh, kw, 128), s);
     StreamBuffer os(static_cast<size_t>(n) * oh * ow * 2 * cop, s);
     if (!xs.ok() || !wp.ok() || !os.ok()) return err(UFB_ECUDA, "cudaMallocAsync failed for convolution scratch");
     TcWeights tw;
     std::string msg;
     // unsigned byte split: valid for any weights, needs no host inspection
-    if (!tc_prepare(tw, weight, co, ci, kh, kw, false, wp.get<uint8_t>(), s, msg)) return err(UFB_ECUDA, msg);
+    if (!tc_prepare(tw, weight, co, ci, kh, kw, false, 128, wp.get<uint8_t>(), s, msg)) return err(UFB_ECUDA, msg);
     const Act in = make_act(xs.get<uint8_t>(), n, h, w, ci, cip);
     const Act ov = make_act(os.get<uint8_t>(), n, oh, ow, co, cop);
     if (!cuda_ok(nchw_to_split(x, n, ci, h, w, 1, in, s), "input layout")) return last_code();
@@ -231,7 +231,7 @@ int ufb_from_split(const uint8_t* x, int n, int c, int h, int w, int pitch, int 
 
 int64_t ufb_weight_bytes(int co, int ci, int kh, int kw) {
     if (co <= 0 || ci <= 0 || kh <= 0 || kw <= 0) return 0;
-    return static_cast<int64_t>(tc_weight_bytes(co, ci, kh, kw));
+    return static_cast<int64_t>(tc_weight_bytes(co, ci, kh, kw, 128));
 }
 
 int ufb_prepare_weights(const int16_t* weight, int co, int ci, int kh, int kw, uint8_t* planes, void* stream) {
@@ -239,7 +239,7 @@ int ufb_prepare_weights(const int16_t* weight, int co, int ci, int kh, int kw, u
     if (!weight || !planes || co <= 0 || ci <= 0 || kh <= 0 || kw <= 0) return err(UFB_EINVAL, "invalid weights");
     TcWeights tw;
     std::string msg;
-    if (!tc_prepare(tw, weight, co, ci, kh, kw, false, planes, static_cast<cudaStream_t>(stream), msg))
+    if (!tc_prepare(tw, weight, co, ci, kh, kw, false, 128, planes, static_cast<cudaStream_t>(stream), msg))
         return err(UFB_ECUDA, msg);
     return UFB_OK;
 }
@@ -259,7 +259,7 @@ int ufb_conv2d_split(const uint8_t* x, int n, int ci, int h, int w, int x_pitch,
     if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return last_code();
     TcWeights tw;
     std::string msg;
-    if (!tc_describe(tw, co, ci, kh, kw, false, const_cast<uint8_t*>(planes), msg)) return err(UFB_ECUDA, msg);
+    if (!tc_describe(tw, co, ci, kh, kw, false, 128, const_cast<uint8_t*>(planes), msg)) return err(UFB_ECUDA, msg);
     const Act in = make_act(const_cast<uint8_t*>(x), n, h, w, ci, x_pitch);
     const Act ov = make_act(out, n, oh, ow, co, out_pitch);
     Epilogue epi{};

@@ -44,16 +44,25 @@ namespace {
 
 constexpr int kBM = 128;                                    // output pixels per tile
 constexpr int kBK = 128;                                    // input channels per K block
-constexpr int kBN = kTcTileN;                               // output channels per tile
-constexpr int kStages = 3;
 constexpr int kEpiWarps = 16;                               // four per TMEM lane quarter
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr uint32_t kABytes = kBM * kBK;                     // one activation plane tile
-constexpr uint32_t kBBytes = 2 * kBN * kBK;                 // stacked low / high weight rows
-constexpr uint32_t kStageBytes = 2 * kABytes + kBBytes;     // 64 KB
-constexpr uint32_t kTmemCols = 512;                         // LL [0,128) X [128,256) HH [256,384)
-constexpr size_t kRingBytes = size_t(kStages) * kStageBytes + 1024;
-constexpr int kCols = kBN / 4;                              // accumulator columns per epilogue warp
+constexpr uint32_t kTmemCols = 512;
+
+// Tile shape per output-channel width BN:
+//   BN = 128: one accumulator set LL [0,128) X [128,256) HH [256,384), 3 x 64 KB ring
+//   BN = 64:  two accumulator sets (at columns 0 and 256) so the epilogue of one
+//             tile overlaps the MMAs of the next, 4 x 48 KB ring
+template <int BN>
+struct Tile {
+    static constexpr uint32_t kBBytes = 2 * BN * kBK;       // stacked low / high weight rows
+    static constexpr uint32_t kStageBytes = 2 * kABytes + kBBytes;
+    static constexpr int kStages = BN == 128 ? 3 : 4;
+    static constexpr int kBuffers = BN == 128 ? 1 : 2;
+    static constexpr uint32_t kBufferStride = 256;          // TMEM columns between accumulator sets
+    static constexpr size_t kRingBytes = size_t(kStages) * kStageBytes + 1024;
+    static constexpr int kCols = BN / 4;                    // accumulator columns per epilogue warp
+};
 
 // Fused elementwise step applied by the epilogue (compile-time, so each
 // instantiation is short straight-line code).
@@ -77,11 +86,11 @@ struct TileCoord {
     long long p0;
 };
 
-template <bool SPATIAL>
+template <bool SPATIAL, int BN>
 __device__ __forceinline__ TileCoord tile_coord(const ConvTcArgs& a, int tile) {
     TileCoord t{};
     const int m = tile / a.n_tiles;
-    t.co0 = (tile - m * a.n_tiles) * kBN;
+    t.co0 = (tile - m * a.n_tiles) * BN;
     if (SPATIAL) {
         int r = m;
         const int tx = r % a.tiles_x;
@@ -247,17 +256,20 @@ __device__ __forceinline__ void store_shuffle2(const Act& out, const uint32_t (&
     }
 }
 
-template <bool SPATIAL, int MODE>
+template <bool SPATIAL, int MODE, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    const ConvTcArgs args) {
+    using T = Tile<BN>;
+    constexpr int S = T::kStages;
+    constexpr int NB = T::kBuffers;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    int32_t* bias_s = reinterpret_cast<int32_t*>(smem + size_t(kStages) * kStageBytes);  // [n_tiles * 128]
-    __shared__ __align__(8) uint64_t full_bar[kStages];
-    __shared__ __align__(8) uint64_t empty_bar[kStages];
-    __shared__ __align__(8) uint64_t tmem_full;
-    __shared__ __align__(8) uint64_t tmem_empty;
+    int32_t* bias_s = reinterpret_cast<int32_t*>(smem + size_t(S) * T::kStageBytes);  // [n_tiles * BN]
+    __shared__ __align__(8) uint64_t full_bar[S];
+    __shared__ __align__(8) uint64_t empty_bar[S];
+    __shared__ __align__(8) uint64_t tmem_full[NB];
+    __shared__ __align__(8) uint64_t tmem_empty[NB];
     __shared__ uint32_t tmem_holder;
     __shared__ int consumed;
 
@@ -266,12 +278,14 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
     const int num_k = args.taps_h * args.taps_w * kb_per_tap;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
-        mbar_init(&tmem_full, 1);
-        mbar_init(&tmem_empty, kEpiWarps);
+        for (int b = 0; b < NB; ++b) {
+            mbar_init(&tmem_full[b], 1);
+            mbar_init(&tmem_empty[b], kEpiWarps);
+        }
         consumed = 0;
         fence_mbar_init();
     }
@@ -280,7 +294,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         tmem_relinquish();
     }
     // the whole bias vector, zero padded to the tile grid, once per CTA
-    for (int i = threadIdx.x; i < args.n_tiles * kBN; i += kThreads) {
+    for (int i = threadIdx.x; i < args.n_tiles * BN; i += kThreads) {
         int32_t b = 0;
         if (args.epi.bias && i < args.co)
             b = args.epi.bias32 ? static_cast<const int32_t*>(args.epi.bias)[i]
@@ -300,18 +314,18 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
             int it = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x) {
-                const TileCoord tc = tile_coord<SPATIAL>(args, tile);
+                const TileCoord tc = tile_coord<SPATIAL, BN>(args, tile);
                 for (int k = 0; k < num_k; ++k, ++it) {
-                    const int s = it % kStages;
-                    const uint32_t round = it / kStages;
-                    if (it >= kStages && !mbar_wait(&empty_bar[s], (round - 1) & 1, args.status, 1)) {
+                    const int s = it % S;
+                    const uint32_t round = it / S;
+                    if (it >= S && !mbar_wait(&empty_bar[s], (round - 1) & 1, args.status, 1)) {
                         ok = false;
                         break;
                     }
                     const int tap = k / kb_per_tap, cb = k - tap * kb_per_tap;
                     const int ky = tap / args.taps_w, kx = tap - ky * args.taps_w;
-                    uint8_t* st = smem + size_t(s) * kStageBytes;
-                    mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+                    uint8_t* st = smem + size_t(s) * T::kStageBytes;
+                    mbar_arrive_expect_tx(&full_bar[s], T::kStageBytes);
                     const int c0 = cb * kBK;
                     if (SPATIAL) {
                         const int ix = tc.x0 + kx - args.pad_w, iy = tc.y0 + ky - args.pad_h;
@@ -321,7 +335,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         tma_load_3d(st, &mapA, &full_bar[s], c0, 0, static_cast<int>(tc.p0));
                         tma_load_3d(st + kABytes, &mapA, &full_bar[s], c0, 1, static_cast<int>(tc.p0));
                     }
-                    tma_load_2d(st + 2 * kABytes, &mapB, &full_bar[s], tap * args.cpad + c0, (tc.co0 / kBN) * 2 * kBN);
+                    tma_load_2d(st + 2 * kABytes, &mapB, &full_bar[s], tap * args.cpad + c0, (tc.co0 / BN) * 2 * BN);
                     issued = it + 1;
                 }
             }
@@ -329,32 +343,33 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t i_uu = i8_idesc(kBM, kBN, false, false);
-            constexpr uint32_t i_su = i8_idesc(kBM, kBN, true, false);
-            constexpr uint32_t i_us = i8_idesc(kBM, kBN, false, true);
-            constexpr uint32_t i_ss = i8_idesc(kBM, kBN, true, true);
-            constexpr uint32_t i_us2 = i8_idesc(kBM, 2 * kBN, false, true);
-            constexpr uint32_t i_ss2 = i8_idesc(kBM, 2 * kBN, true, true);
-            const uint32_t d_ll = tmem, d_x = tmem + kBN, d_hh = tmem + 2 * kBN;
+            constexpr uint32_t i_uu = i8_idesc(kBM, BN, false, false);
+            constexpr uint32_t i_su = i8_idesc(kBM, BN, true, false);
+            constexpr uint32_t i_us = i8_idesc(kBM, BN, false, true);
+            constexpr uint32_t i_ss = i8_idesc(kBM, BN, true, true);
+            constexpr uint32_t i_us2 = i8_idesc(kBM, 2 * BN, false, true);
+            constexpr uint32_t i_ss2 = i8_idesc(kBM, 2 * BN, true, true);
             int it = 0, ti = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x, ++ti) {
-                if (ti > 0 && !mbar_wait(&tmem_empty, (ti - 1) & 1, args.status, 3)) {
+                const int buf = ti % NB, use = ti / NB;
+                if (use > 0 && !mbar_wait(&tmem_empty[buf], (use - 1) & 1, args.status, 3)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                const uint32_t d_ll = tmem + buf * T::kBufferStride, d_x = d_ll + BN, d_hh = d_ll + 2 * BN;
                 for (int k = 0; k < num_k; ++k, ++it) {
-                    const int s = it % kStages;
-                    const uint32_t round = it / kStages;
+                    const int s = it % S;
+                    const uint32_t round = it / S;
                     if (!mbar_wait(&full_bar[s], round & 1, args.status, 2)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t base = smem_u32(smem + size_t(s) * kStageBytes);
+                    const uint32_t base = smem_u32(smem + size_t(s) * T::kStageBytes);
                     const uint32_t a_lo = base, a_hi = base + kABytes, b_lo = base + 2 * kABytes,
-                                   b_hi = b_lo + kBN * kBK;
+                                   b_hi = b_lo + BN * kBK;
 #pragma unroll
                     for (int kk = 0; kk < kBK / 32; ++kk) {
                         const uint32_t o = kk * 32;
@@ -378,20 +393,22 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     mma_commit(&empty_bar[s]);
                 }
                 if (!ok) break;
-                mma_commit(&tmem_full);
+                mma_commit(&tmem_full[buf]);
             }
             consumed = it;
         }
         __syncwarp();
     } else {
+        constexpr int kC = T::kCols;                   // 32 (BN 128) or 16 (BN 64)
         const int quarter = warp & 3;
-        const int cgroup = (warp - 2) >> 2;            // 0..3: columns [32 cgroup, 32 cgroup + 32)
+        const int cgroup = (warp - 2) >> 2;            // columns [kC * cgroup, kC * cgroup + kC)
         const int row = quarter * 32 + lane;
         const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         const Act& out = args.out;
         int ti = 0;
         for (int tile = blockIdx.x; tile < args.total_tiles; tile += gridDim.x, ++ti) {
-            const TileCoord tc = tile_coord<SPATIAL>(args, tile);
+            const int buf = ti % NB, use = ti / NB;
+            const TileCoord tc = tile_coord<SPATIAL, BN>(args, tile);
             bool valid;
             long long opx = 0, rpx1 = 0, rpx2 = 0;
             int oy = 0, ox = 0;
@@ -409,17 +426,18 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                 opx = rpx1 = rpx2 = tc.p0 + row;
                 valid = opx < args.m_total;
             }
-            if (!mbar_wait(&tmem_full, ti & 1, args.status, 4)) break;
+            if (!mbar_wait(&tmem_full[buf], use & 1, args.status, 4)) break;
             tc_fence_after();
+            const uint32_t acc_addr = lane_addr + buf * T::kBufferStride;
             // phase 1: accumulators -> sat(rna(sum / 8192) + bias), 16 columns at a time
-            uint32_t packed[kCols / 2];
+            uint32_t packed[kC / 2];
 #pragma unroll
-            for (int c = 0; c < kCols / 16; ++c) {
-                const int col = cgroup * kCols + c * 16;
+            for (int c = 0; c < kC / 16; ++c) {
+                const int col = cgroup * kC + c * 16;
                 uint32_t ll[16], xx[16], hh[16];
-                tmem_ld16(lane_addr + col, ll);
-                tmem_ld16(lane_addr + kBN + col, xx);
-                tmem_ld16(lane_addr + 2 * kBN + col, hh);
+                tmem_ld16(acc_addr + col, ll);
+                tmem_ld16(acc_addr + BN + col, xx);
+                tmem_ld16(acc_addr + 2 * BN + col, hh);
                 const int4* bq = reinterpret_cast<const int4*>(bias_s + tc.co0 + col);
                 const int4 b4[4] = {bq[0], bq[1], bq[2], bq[3]};
                 const int32_t* bias = reinterpret_cast<const int32_t*>(b4);
@@ -442,15 +460,15 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     packed[c * 8 + j / 2] = pack2(r[0], r[1]);
                 }
             }
-            // TMEM is free for the next tile's MMAs
+            // this accumulator set is free for the MMAs of the tile after next
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_empty);
-            // phase 2: fused elementwise steps and stores, overlapped with the next MMAs
+            if (lane == 0) mbar_arrive(&tmem_empty[buf]);
+            // phase 2: fused elementwise steps and stores, overlapped with MMAs
             if (valid) {
 #pragma unroll
-                for (int c = 0; c < kCols / 16; ++c) {
-                    const int cbase = tc.co0 + cgroup * kCols + c * 16;
+                for (int c = 0; c < kC / 16; ++c) {
+                    const int cbase = tc.co0 + cgroup * kC + c * 16;
                     if (cbase >= args.co) break;
                     const int n_valid = args.co - cbase < 16 ? args.co - cbase : 16;
                     uint32_t p8[8];
@@ -471,7 +489,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
     if (warp == 0 && lane == 0) {
         // abort path only: wait for TMA loads issued but never consumed, so no
         // copy into this CTA's shared memory outlives the CTA
-        for (int k = consumed; k < issued; ++k) mbar_wait(&full_bar[k % kStages], (k / kStages) & 1, args.status, 5);
+        for (int k = consumed; k < issued; ++k) mbar_wait(&full_bar[k % S], (k / S) & 1, args.status, 5);
     }
     if (warp == 1) {
         tc_fence_after();
@@ -479,18 +497,18 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
     }
 }
 
-// [co_tiles][2][128][kpad]: tile rows 0..127 low bytes, 128..255 high bytes.
+// [co_tiles][2][bn][kpad]: tile rows 0..bn-1 low bytes, bn..2bn-1 high bytes.
 __global__ void prep_tc_weights_kernel(const int16_t* __restrict__ w, int co, int ci, int kh, int kw, int cpad,
-                                       int kpad, int co_tiles, int signed_split, uint8_t* __restrict__ planes) {
-    const long long total = static_cast<long long>(co_tiles) * 2 * kBN * kpad;
+                                       int kpad, int co_tiles, int bn, int signed_split, uint8_t* __restrict__ planes) {
+    const long long total = static_cast<long long>(co_tiles) * 2 * bn * kpad;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
         const int k = static_cast<int>(i % kpad);
-        const long long rowg = i / kpad;  // tile * 256 + r
-        const int r = static_cast<int>(rowg % (2 * kBN));
-        const int tile = static_cast<int>(rowg / (2 * kBN));
-        const int plane = r / kBN;
-        const int o = tile * kBN + (r - plane * kBN);
+        const long long rowg = i / kpad;  // tile * 2bn + r
+        const int r = static_cast<int>(rowg % (2 * bn));
+        const int tile = static_cast<int>(rowg / (2 * bn));
+        const int plane = r / bn;
+        const int o = tile * bn + (r - plane * bn);
         const int tap = k / cpad, c = k - tap * cpad;
         int32_t v = 0;
         if (o < co && c < ci) {
@@ -560,38 +578,50 @@ int sm_count(int device) {
     return g_sms[device] > 0 ? g_sms[device] : 148;
 }
 
-template <bool SPATIAL, int MODE>
+template <bool SPATIAL, int MODE, int BN>
 cudaError_t launch_mode(const CUtensorMap& a, const CUtensorMap& b, const ConvTcArgs& args, cudaStream_t stream) {
     int device = 0;
     cudaError_t e = cudaGetDevice(&device);
     if (e != cudaSuccess) return e;
-    const size_t smem = kRingBytes + size_t(args.n_tiles) * kBN * sizeof(int32_t);
+    const size_t smem = Tile<BN>::kRingBytes + size_t(args.n_tiles) * BN * sizeof(int32_t);
     // the attribute is per function and device; setting it each launch is cheap
-    e = cudaFuncSetAttribute(conv_i16_tc_kernel<SPATIAL, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(conv_i16_tc_kernel<SPATIAL, MODE, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     const int sms = sm_count(device);
     const int grid = args.total_tiles < sms ? args.total_tiles : sms;
-    conv_i16_tc_kernel<SPATIAL, MODE><<<grid, kThreads, smem, stream>>>(a, b, args);
+    conv_i16_tc_kernel<SPATIAL, MODE, BN><<<grid, kThreads, smem, stream>>>(a, b, args);
     return cudaGetLastError();
 }
 
-template <bool SPATIAL>
-cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b, const ConvTcArgs& args, cudaStream_t stream) {
+template <bool SPATIAL, int BN>
+cudaError_t launch_bn(const CUtensorMap& a, const CUtensorMap& b, const ConvTcArgs& args, cudaStream_t stream) {
     const Epilogue& e = args.epi;
-    if (e.shuffle2) return launch_mode<SPATIAL, kEpiShuffle2>(a, b, args, stream);
-    if (e.wsilu4) return launch_mode<SPATIAL, kEpiWsilu4>(a, b, args, stream);
-    if (e.lut) return launch_mode<SPATIAL, kEpiLut>(a, b, args, stream);
-    if (e.res1.base) return launch_mode<SPATIAL, kEpiRes>(a, b, args, stream);
-    return launch_mode<SPATIAL, kEpiPlain>(a, b, args, stream);
+    if (e.shuffle2) return launch_mode<SPATIAL, kEpiShuffle2, BN>(a, b, args, stream);
+    if (e.wsilu4) return launch_mode<SPATIAL, kEpiWsilu4, BN>(a, b, args, stream);
+    if (e.lut) return launch_mode<SPATIAL, kEpiLut, BN>(a, b, args, stream);
+    if (e.res1.base) return launch_mode<SPATIAL, kEpiRes, BN>(a, b, args, stream);
+    return launch_mode<SPATIAL, kEpiPlain, BN>(a, b, args, stream);
+}
+
+template <bool SPATIAL>
+cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b, const ConvTcArgs& args, int bn, cudaStream_t stream) {
+    return bn == 64 ? launch_bn<SPATIAL, 64>(a, b, args, stream) : launch_bn<SPATIAL, 128>(a, b, args, stream);
 }
 
 }  // namespace
 
-size_t tc_weight_bytes(int co, int ci, int kh, int kw) {
+size_t tc_weight_bytes(int co, int ci, int kh, int kw, int bn) {
     const int cpad = (ci + kBK - 1) / kBK * kBK;
-    const int co_tiles = (co + kBN - 1) / kBN;
-    return static_cast<size_t>(co_tiles) * 2 * kBN * kh * kw * cpad;
+    const int co_tiles = (co + bn - 1) / bn;
+    return static_cast<size_t>(co_tiles) * 2 * bn * kh * kw * cpad;
+}
+
+int tc_choose_bn(int ci, int kh, int kw, bool signed_split) {
+    // reductions of up to 512 are dominated by the per-tile epilogue: the
+    // 64-wide tile double-buffers TMEM so the epilogue overlaps the MMAs; the
+    // signed split keeps its MMAs 128 wide (full rate)
+    return signed_split && static_cast<long long>(ci) * kh * kw <= 512 ? 64 : 128;
 }
 
 bool tc_signed_split_ok(const int16_t* weight_host, size_t count) {
@@ -600,29 +630,35 @@ bool tc_signed_split_ok(const int16_t* weight_host, size_t count) {
     return true;
 }
 
-bool tc_describe(TcWeights& w, int co, int ci, int kh, int kw, bool signed_split, uint8_t* planes, std::string& err) {
+bool tc_describe(TcWeights& w, int co, int ci, int kh, int kw, bool signed_split, int bn, uint8_t* planes,
+                 std::string& err) {
+    if (bn != 64 && bn != 128) {
+        err = "tile width must be 64 or 128";
+        return false;
+    }
+    w.bn = bn;
     w.co = co;
     w.ci = ci;
     w.kh = kh;
     w.kw = kw;
     w.cpad = (ci + kBK - 1) / kBK * kBK;
     w.kpad = kh * kw * w.cpad;
-    w.co_tiles = (co + kBN - 1) / kBN;
+    w.co_tiles = (co + bn - 1) / bn;
     w.signed_split = signed_split;
     w.planes = planes;
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w.kpad), static_cast<cuuint64_t>(w.co_tiles) * 2 * kBN};
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w.kpad), static_cast<cuuint64_t>(w.co_tiles) * 2 * bn};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w.kpad)};
-    const cuuint32_t box[2] = {kBK, 2 * kBN};
+    const cuuint32_t box[2] = {kBK, static_cast<cuuint32_t>(2 * bn)};
     return encode(&w.map, planes, 2, dims, strides, box, err);
 }
 
-bool tc_prepare(TcWeights& w, const int16_t* weight, int co, int ci, int kh, int kw, bool signed_split,
+bool tc_prepare(TcWeights& w, const int16_t* weight, int co, int ci, int kh, int kw, bool signed_split, int bn,
                 uint8_t* planes, cudaStream_t s, std::string& err) {
-    if (!tc_describe(w, co, ci, kh, kw, signed_split, planes, err)) return false;
-    const long long total = static_cast<long long>(w.co_tiles) * 2 * kBN * w.kpad;
+    if (!tc_describe(w, co, ci, kh, kw, signed_split, bn, planes, err)) return false;
+    const long long total = static_cast<long long>(w.co_tiles) * 2 * bn * w.kpad;
     const long long blocks = (total + 255) / 256;
     prep_tc_weights_kernel<<<static_cast<unsigned>(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, s>>>(
-        weight, co, ci, kh, kw, w.cpad, w.kpad, w.co_tiles, signed_split ? 1 : 0, planes);
+        weight, co, ci, kh, kw, w.cpad, w.kpad, w.co_tiles, bn, signed_split ? 1 : 0, planes);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         err = std::string("weight preparation: ") + cudaGetErrorString(e);
@@ -659,7 +695,8 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
         err = "unsupported epilogue combination (one of lut, residual adds, wsilu4, pixel shuffle; no multiply)";
         return -1;
     }
-    if (w.co_tiles * kBN * sizeof(int32_t) + kRingBytes > 227 * 1024) {
+    const size_t ring = w.bn == 64 ? Tile<64>::kRingBytes : Tile<128>::kRingBytes;
+    if (w.co_tiles * w.bn * sizeof(int32_t) + ring > 227 * 1024) {
         err = "too many output channels for the staged bias";
         return -1;
     }
@@ -718,7 +755,8 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
         return -1;
     }
     args.total_tiles = static_cast<int>(total);
-    const cudaError_t e = flat ? launch<false>(amap, w.map, args, stream) : launch<true>(amap, w.map, args, stream);
+    const cudaError_t e =
+        flat ? launch<false>(amap, w.map, args, w.bn, stream) : launch<true>(amap, w.map, args, w.bn, stream);
     if (e != cudaSuccess) {
         err = std::string("conv launch failed: ") + cudaGetErrorString(e);
         return -1;

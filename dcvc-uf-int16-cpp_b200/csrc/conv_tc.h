@@ -9,12 +9,9 @@
 
 namespace ufb {
 
-// Output channels per tensor-core tile (one 128-lane TMEM accumulator set).
-constexpr int kTcTileN = 128;
-
 // Device-resident convolution weights prepared for the tensor-core kernel.
-// Layout: [co_tiles][2][128][kpad] bytes -- per tile of 128 output channels,
-// 128 rows of the weights' low bytes followed by 128 rows of their high bytes,
+// Layout: [co_tiles][2][bn][kpad] bytes -- per tile of bn (64 or 128) output
+// channels, bn rows of the weights' low bytes followed by bn rows of their high bytes,
 // k = (ky * kw + kx) * cpad + c, zero rows / columns as padding.
 //   unsigned split (any weights):   w = lo + 256 hi, lo u8 = w & 0xff, hi s8 = w >> 8
 //   signed split (w <= 32639):      w = lo + 256 hi, lo s8 in [-128, 127], hi s8
@@ -22,20 +19,25 @@ constexpr int kTcTileN = 128;
 // products (see conv_tc.cu), halving the MMA count.
 struct TcWeights {
     uint8_t* planes = nullptr;
-    int co = 0, ci = 0, kh = 0, kw = 0, cpad = 0, kpad = 0, co_tiles = 0;
+    int co = 0, ci = 0, kh = 0, kw = 0, cpad = 0, kpad = 0, co_tiles = 0, bn = 128;
     bool signed_split = false;
-    CUtensorMap map{};  // TMA map over the [co_tiles * 256][kpad] byte matrix, 256-row box
+    CUtensorMap map{};  // TMA map over the [co_tiles * 2bn][kpad] byte matrix, 2bn-row box
 };
 
 // Bytes needed for the prepared planes of a [co, ci, kh, kw] convolution.
-size_t tc_weight_bytes(int co, int ci, int kh, int kw);
+size_t tc_weight_bytes(int co, int ci, int kh, int kw, int bn);
+
+// Tile width used for a layer (64: double-buffered accumulators, for small
+// reductions with the signed split; otherwise 128).
+int tc_choose_bn(int ci, int kh, int kw, bool signed_split);
 
 // Describe already prepared planes (fields + TMA map; no device work).
-bool tc_describe(TcWeights& w, int co, int ci, int kh, int kw, bool signed_split, uint8_t* planes, std::string& err);
+bool tc_describe(TcWeights& w, int co, int ci, int kh, int kw, bool signed_split, int bn, uint8_t* planes,
+                 std::string& err);
 
 // tc_describe plus the preparation of int16 weights already on the device
 // into `planes` (tc_weight_bytes bytes), launched on stream s.
-bool tc_prepare(TcWeights& w, const int16_t* weight, int co, int ci, int kh, int kw, bool signed_split,
+bool tc_prepare(TcWeights& w, const int16_t* weight, int co, int ci, int kh, int kw, bool signed_split, int bn,
                 uint8_t* planes, cudaStream_t s, std::string& err);
 
 // True when every weight allows the signed split (host data).

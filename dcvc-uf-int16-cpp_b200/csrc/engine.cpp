@@ -178,12 +178,14 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
         if (!L.weights16) throw std::runtime_error("Missing prepared UF tensor: " + kv.first + ".weight");
         L.depthwise = L.ci == 1 && L.co > 1;
         if (L.depthwise || static_cast<long long>(L.ci) * L.kh * L.kw > 32768) continue;
+        const bool sgn = signed_ok[kv.first];
+        const int bn = tc_choose_bn(L.ci, L.kh, L.kw, sgn);
         void* planes = nullptr;
-        ck(cudaMalloc(&planes, tc_weight_bytes(L.co, L.ci, L.kh, L.kw)), "weight planes");
+        ck(cudaMalloc(&planes, tc_weight_bytes(L.co, L.ci, L.kh, L.kw, bn)), "weight planes");
         allocations_.push_back(planes);
         std::string err;
-        if (!tc_prepare(L.tc, L.weights16, L.co, L.ci, L.kh, L.kw, signed_ok[kv.first], static_cast<uint8_t*>(planes),
-                        nullptr, err))
+        if (!tc_prepare(L.tc, L.weights16, L.co, L.ci, L.kh, L.kw, sgn, bn, static_cast<uint8_t*>(planes), nullptr,
+                        err))
             throw std::runtime_error(err);
     }
     ck(cudaDeviceSynchronize(), "model upload");
