@@ -53,11 +53,12 @@ def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=2)
-    p.add_argument("--warmup", type=int, default=1)
+    p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="decode", choices=["decode", "conv"])
     p.add_argument("--seqs", type=int, default=SEQS,
                    help="sequences in the job (default: BASELINE config 5's 64); smaller values are for profiling")
+    p.add_argument("--shapes", action="store_true", help="print per launch shape convolution time to stderr")
     return p.parse_args()
 
 
@@ -126,6 +127,22 @@ def reduce_over_ranks(value, world, device, op):
     t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
     return float(t.item())
+
+
+def print_shapes(codecs, frames):
+    """Per launch shape convolution time of the timed steps, to stderr."""
+    table = {}
+    for c in codecs:
+        for k, (n, macs, ms) in c.shape_table().items():
+            t = table.setdefault(k, [0, 0.0, 0.0])
+            t[0] += n
+            t[1] += macs
+            t[2] += ms
+    total = sum(t[2] for t in table.values())
+    print(f"# shape  launches  ms  share  int8-TOPS  ({frames} frames)", file=sys.stderr)
+    for k, (n, macs, ms) in sorted(table.items(), key=lambda kv: -kv[1][2]):
+        tops = 8 * macs / (ms * 1e-3) / 1e12 if ms else 0.0
+        print(f"{k:40s} {n:6d} {ms:9.2f} {ms / total * 100:5.1f}% {tops:7.0f}", file=sys.stderr)
 
 
 def load_traffic(key):
@@ -241,6 +258,8 @@ def bench_decode_ours(args, rank, world, local):
         torch.cuda.nvtx.range_pop()
         barrier(world)
         st = {"launches": 0, "conv_launches": 0, "conv_int16_macs": 0.0, "conv_ms": 0.0}
+        if args.shapes and not yuv:
+            print_shapes([c for pair in decoders for c in pair], frames)
         for pair in decoders:
             for c in pair:
                 s = c.stats()

@@ -51,6 +51,7 @@ def library():
         L.ufb_wsilu4.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp]
         L.ufb_warp.argtypes = [vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp]
         L.ufb_device_status.argtypes = [C.c_int]
+        L.ufb_set_conv_max_ctas.argtypes = [C.c_int]
         _LIB = L
     return _LIB
 
@@ -68,6 +69,11 @@ def _cuda(t: torch.Tensor, dtype, what: str) -> torch.Tensor:
     if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == dtype):
         raise UfbError(-1, f"{what}: CUDA {dtype} tensor required")
     return t.contiguous()
+
+
+def set_conv_max_ctas(n: int) -> None:
+    """Testing aid: cap the persistent convolution grid at n CTAs (0: one per SM)."""
+    _check(library().ufb_set_conv_max_ctas(int(n)))
 
 
 def device_status(device: int = 0) -> int:
@@ -213,6 +219,7 @@ def _engine_lib():
     L.ufb_codec_profile.argtypes = [vp, ci]
     L.ufb_codec_stats.argtypes = [vp, ci, C.POINTER(i64), C.POINTER(i64), C.POINTER(C.c_double),
                                   C.POINTER(C.c_double)]
+    L.ufb_codec_shape_table.argtypes = [vp, C.c_char_p, i64, C.POINTER(i64)]
     L._engine_ready = True
     return L
 
@@ -385,3 +392,16 @@ class Codec:
         m, t = C.c_double(), C.c_double()
         _check(self.L.ufb_codec_stats(self.h, int(reset), C.byref(a), C.byref(b), C.byref(m), C.byref(t)))
         return {"launches": a.value, "conv_launches": b.value, "conv_int16_macs": m.value, "conv_ms": t.value}
+
+    def shape_table(self):
+        """Profiled convolution time per launch shape since the last stats reset:
+        {shape: (launches, int16 MACs, ms)} (profiling must be on)."""
+        n = C.c_int64()
+        _check(self.L.ufb_codec_shape_table(self.h, None, 0, C.byref(n)))
+        buf = C.create_string_buffer(n.value + 1)
+        _check(self.L.ufb_codec_shape_table(self.h, buf, n.value + 1, C.byref(n)))
+        table = {}
+        for line in buf.value.decode().splitlines():
+            shape, launches, macs, ms = line.split("\t")
+            table[shape] = (int(launches), float(macs), float(ms))
+        return table

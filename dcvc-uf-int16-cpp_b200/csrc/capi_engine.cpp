@@ -7,6 +7,8 @@
 #include "engine_kernels.h"
 #include "kernels.h"
 
+#include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <memory>
 #include <new>
@@ -261,9 +263,27 @@ int ufb_codec_stats(ufb_codec* c, int reset, int64_t* launches, int64_t* conv_la
         if (conv_launches) *conv_launches = st.conv_launches;
         if (conv_int16_macs) *conv_int16_macs = st.conv_int16_macs;
         if (conv_ms) *conv_ms = st.conv_ms;
-        if (reset) {
-            st.launches = st.conv_launches = 0;
-            st.conv_int16_macs = st.conv_ms = 0;
+        if (reset) st.reset();
+        return 0;
+    });
+}
+
+int ufb_codec_shape_table(ufb_codec* c, char* text, int64_t capacity, int64_t* length) {
+    return guarded([&] {
+        if (!c || !length) throw std::invalid_argument("codec or length is null");
+        EngineStats& st = c->c->stats();
+        std::string out;
+        char line[192];
+        for (const auto& kv : st.shapes) {
+            snprintf(line, sizeof(line), "%s\t%lld\t%.6g\t%.6f\n", kv.first.c_str(), kv.second.launches,
+                     kv.second.int16_macs, kv.second.ms);
+            out += line;
+        }
+        *length = static_cast<int64_t>(out.size());
+        if (text && capacity > 0) {
+            const size_t n = std::min<size_t>(out.size(), static_cast<size_t>(capacity - 1));
+            memcpy(text, out.data(), n);
+            text[n] = 0;
         }
         return 0;
     });

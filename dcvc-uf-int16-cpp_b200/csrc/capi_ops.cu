@@ -82,7 +82,7 @@ int conv_dispatch(const int16_t* x, int n, int ci, int h, int w, const int16_t* 
     if (!check_conv(x, n, ci, h, w, weight, co, kh, kw, bias_bits, sh, sw, ph, pw, groups, out, oh, ow))
         return last_code();
     auto s = static_cast<cudaStream_t>(stream);
-    const bool tc_ok = allow_tc && groups == 1 && sh == 1 && sw == 1 && static_cast<long long>(ci) * kh * kw <= 32768;
+    const bool tc_ok = allow_tc && groups == 1 && sh == 1 && sw == 1 && static_cast<long long>(ci) * kh * kw <= kTcMaxReduction;
     if (tc_ok) return conv_tc_path(x, n, ci, h, w, weight, co, kh, kw, bias, bias_bits, ph, pw, oh, ow, out, s);
     if (!allow_direct && !allow_tc) return err(UFB_EINVAL, "no convolution path");
     return conv_direct_path(x, n, ci, h, w, weight, co, kh, kw, bias, bias_bits, sh, sw, ph, pw, groups, oh, ow, out,
@@ -94,6 +94,13 @@ int conv_dispatch(const int16_t* x, int n, int ci, int h, int w, const int16_t* 
 extern "C" {
 
 int ufb_version(void) { return 100; }
+
+int ufb_set_conv_max_ctas(int n) {
+    clear_error();
+    if (n < 0) return err(UFB_EINVAL, "CTA cap must be >= 0");
+    tc_set_max_ctas(n);
+    return UFB_OK;
+}
 
 const char* ufb_last_error(void) { return last_message(); }
 
@@ -254,7 +261,7 @@ int ufb_conv2d_split(const uint8_t* x, int n, int ci, int h, int w, int x_pitch,
     if (!check_conv(reinterpret_cast<const int16_t*>(x), n, ci, h, w, reinterpret_cast<const int16_t*>(planes), co,
                     kh, kw, bias_bits, 1, 1, pad_h, pad_w, 1, reinterpret_cast<int16_t*>(out), oh, ow))
         return last_code();
-    if (static_cast<long long>(ci) * kh * kw > 32768) return err(UFB_ERANGE, "reduction exceeds 32768");
+    if (static_cast<long long>(ci) * kh * kw > kTcMaxReduction) return err(UFB_ERANGE, "reduction exceeds 8192");
     int device = 0;
     if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return last_code();
     TcWeights tw;

@@ -14,7 +14,8 @@
 //     low rows over its 128 high rows, so one N=256 MMA A_lo x [wl; wh]
 //     yields [LL | xl wh] and one N=256 MMA A_hi x [wl; wh], written 128
 //     columns further on, adds xh wl onto X and yields HH: two MMAs per step.
-// For K <= 32768 every partial sum fits s32 (|X| <= 383 * 128 * K).
+// For K <= 8192 every partial sum fits s32 and the recombination runs in
+// 32-bit arithmetic; longer reductions take the int64 SIMT path.
 //
 // GEMM orientation: M = 128 output pixels (TMEM lanes), N = 128 output
 // channels per tile, K = taps x input channels.  Activations are split NHWC in
@@ -23,17 +24,22 @@
 // zero fill is the convolution's zero padding.
 //
 // Persistent CTAs (one per SM) walk the output tiles.  Warp 0 issues TMA into a
-// 3-stage ring that runs ahead across tiles, warp 1 owns TMEM and issues the
-// MMAs, warps 2-9 run the epilogue in two phases: phase 1 reads the three
-// accumulators, rounds, adds the bias and saturates into registers, then
-// releases TMEM so the next tile's MMAs start; phase 2 applies the fused
-// elementwise steps (LUT, residual adds, QP multiply, WSiLU4, pixel shuffle)
-// and stores while those MMAs run.
+// 3 x 64 KB ring that runs ahead across tiles (about 1.4 us of L2 round trip
+// per stage needs that much in flight), warp 1 owns TMEM and issues the MMAs,
+// warps 4-19 run the epilogue (registers re-balanced towards them): they first
+// copy their 3 x 32 accumulator
+// columns into registers and release TMEM at once, so the next tile's MMAs
+// start while they recombine, add the bias, saturate, apply the fused
+// elementwise step and write the tile.  Output tiles leave through a 16 KB
+// shared-memory stage (128-byte swizzle, one byte plane at a time) and TMA
+// stores, which write whole lines; per-thread pixel-row stores reach only a
+// third of the bandwidth.
 #include "umma.cuh"
-#include "uf_common.cuh"
+#include "conv_epi.cuh"
 #include "conv_tc.h"
 
 #include <cuda_runtime.h>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -43,30 +49,25 @@ namespace ufb {
 namespace {
 
 constexpr int kBM = 128;                                    // output pixels per tile
+constexpr int kBN = 128;                                    // output channels per tile
 constexpr int kBK = 128;                                    // input channels per K block
 constexpr int kEpiWarps = 16;                               // four per TMEM lane quarter
-constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr int kFirstEpiWarp = 2;
+constexpr int kThreads = (kFirstEpiWarp + kEpiWarps) * 32;  // 576
 constexpr uint32_t kABytes = kBM * kBK;                     // one activation plane tile
-constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kBBytes = 2 * kBN * kBK;                 // stacked low / high weight rows
+constexpr uint32_t kStageBytes = 2 * kABytes + kBBytes;     // 64 KB
+constexpr int kStages = 3;
+constexpr uint32_t kStagingBytes = kBM * kBN;               // one byte plane of an output tile
+constexpr uint32_t kTmemCols = 512;                         // two staggered accumulator sets
+constexpr size_t kSmemLimit = 225 * 1024;  // dynamic shared memory: 227 KB less static barriers and slack
 
-// Tile shape per output-channel width BN:
-//   BN = 128: one accumulator set LL [0,128) X [128,256) HH [256,384), 3 x 64 KB ring
-//   BN = 64:  two accumulator sets (at columns 0 and 256) so the epilogue of one
-//             tile overlaps the MMAs of the next, 4 x 48 KB ring
-template <int BN>
-struct Tile {
-    static constexpr uint32_t kBBytes = 2 * BN * kBK;       // stacked low / high weight rows
-    static constexpr uint32_t kStageBytes = 2 * kABytes + kBBytes;
-    static constexpr int kStages = BN == 128 ? 3 : 4;
-    static constexpr int kBuffers = BN == 128 ? 1 : 2;
-    static constexpr uint32_t kBufferStride = 256;          // TMEM columns between accumulator sets
-    static constexpr size_t kRingBytes = size_t(kStages) * kStageBytes + 1024;
-    static constexpr int kCols = BN / 4;                    // accumulator columns per epilogue warp
+// How an output tile is written.
+enum StoreKind : int {
+    kStoreTma = 0,      // both planes through the stage, 128-channel boxes
+    kStoreTmaQuarter,   // wsilu4: 32 output channels per tile, both planes in one stage
+    kStoreThreads,      // pixel shuffle: per-thread stores to four target pixels
 };
-
-// Fused elementwise step applied by the epilogue (compile-time, so each
-// instantiation is short straight-line code).
-enum EpiMode : int { kEpiPlain = 0, kEpiLut = 1, kEpiRes = 2, kEpiWsilu4 = 3, kEpiShuffle2 = 4 };
 
 struct ConvTcArgs {
     Act out;
@@ -77,7 +78,6 @@ struct ConvTcArgs {
     long long m_total;  // flat mode: output pixels
     int n_tiles, total_tiles;
     int signed_split;
-    int wide;           // K >= 16384: int64 recombination
     int* status;
 };
 
@@ -86,11 +86,11 @@ struct TileCoord {
     long long p0;
 };
 
-template <bool SPATIAL, int BN>
+template <bool SPATIAL>
 __device__ __forceinline__ TileCoord tile_coord(const ConvTcArgs& a, int tile) {
     TileCoord t{};
     const int m = tile / a.n_tiles;
-    t.co0 = (tile - m * a.n_tiles) * BN;
+    t.co0 = (tile - m * a.n_tiles) * kBN;
     if (SPATIAL) {
         int r = m;
         const int tx = r % a.tiles_x;
@@ -103,128 +103,6 @@ __device__ __forceinline__ TileCoord tile_coord(const ConvTcArgs& a, int tile) {
         t.p0 = static_cast<long long>(m) * kBM;
     }
     return t;
-}
-
-// rna(S / 8192) of S = L + 256 X + 65536 H without 64-bit arithmetic (valid
-// for K < 16384, where 8 |H| < 2^31): S = 8192 T + Rl with 0 <= Rl < 8192, and
-// round-half-away gives T + (Rl > 4096 || (Rl == 4096 && T >= 0)).
-__device__ __forceinline__ int32_t recombine32(int32_t L, int32_t X, int32_t H) {
-    const int32_t R = ((X & 31) << 8) + (L & 8191);
-    const int32_t T = H * 8 + (X >> 5) + (L >> 13) + (R >> 13);
-    const int32_t Rl = R & 8191;
-    return T + ((Rl > 4096) | ((Rl == 4096) & (T >= 0)));
-}
-
-__device__ __forceinline__ int64_t recombine64(int32_t L, int32_t X, int32_t H) {
-    return rna_shift(static_cast<int64_t>(L) + 256 * static_cast<int64_t>(X) + 65536 * static_cast<int64_t>(H), 13);
-}
-
-__device__ __forceinline__ int32_t clamp16(int32_t v) { return v < -32768 ? -32768 : (v > 32767 ? 32767 : v); }
-
-__device__ __forceinline__ uint32_t pack2(int32_t a, int32_t b) {
-    return (static_cast<uint32_t>(a) & 0xffffu) | (static_cast<uint32_t>(b) << 16);
-}
-
-__device__ __forceinline__ int32_t lo16(uint32_t p) { return static_cast<int16_t>(p & 0xffffu); }
-__device__ __forceinline__ int32_t hi16(uint32_t p) { return static_cast<int16_t>(p >> 16); }
-
-// 16 packed int16 values (8 words) -> 16 low bytes + 16 high bytes.
-__device__ __forceinline__ void split_bytes(const uint32_t (&p)[8], uint4& lo, uint4& hi) {
-    lo.x = __byte_perm(p[0], p[1], 0x6420);
-    lo.y = __byte_perm(p[2], p[3], 0x6420);
-    lo.z = __byte_perm(p[4], p[5], 0x6420);
-    lo.w = __byte_perm(p[6], p[7], 0x6420);
-    hi.x = __byte_perm(p[0], p[1], 0x7531);
-    hi.y = __byte_perm(p[2], p[3], 0x7531);
-    hi.z = __byte_perm(p[4], p[5], 0x7531);
-    hi.w = __byte_perm(p[6], p[7], 0x7531);
-}
-
-// 4 low bytes + 4 high bytes -> 2 packed words of int16 pairs.
-__device__ __forceinline__ void join_bytes(uint32_t lo, uint32_t hi, uint32_t& p0, uint32_t& p1) {
-    p0 = __byte_perm(lo, hi, 0x5140);
-    p1 = __byte_perm(lo, hi, 0x7362);
-}
-
-// Phase 2 of 16 conv outputs (packed pairs p) of one pixel, output channels
-// cbase .. cbase + 15, in the order of src/layers.cpp:91-104.
-template <int MODE>
-__device__ __forceinline__ void finish16(const ConvTcArgs& a, uint32_t (&p)[8], int cbase, int n_valid,
-                                         long long opx, long long rpx1, long long rpx2, const Act& out) {
-    const Epilogue& e = a.epi;
-    if (MODE == kEpiLut) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-            p[i] = pack2(__ldg(&e.lut[lo16(p[i]) + 32768]), __ldg(&e.lut[hi16(p[i]) + 32768]));
-    }
-    if (MODE == kEpiRes) {
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const Act& res = r == 0 ? e.res1 : e.res2;
-            if (r == 1 && !res.base) break;
-            const long long rp = r == 0 ? rpx1 : rpx2;
-            uint4 rl, rh;
-            if (n_valid >= 16) {
-                rl = *reinterpret_cast<const uint4*>(res.lo(rp) + cbase);
-                rh = *reinterpret_cast<const uint4*>(res.hi(rp) + cbase);
-            } else {
-                uint8_t bl[16], bh[16];
-                for (int j = 0; j < 16; ++j) {
-                    bl[j] = j < n_valid ? res.lo(rp)[cbase + j] : 0;
-                    bh[j] = j < n_valid ? res.hi(rp)[cbase + j] : 0;
-                }
-                rl = *reinterpret_cast<const uint4*>(bl);
-                rh = *reinterpret_cast<const uint4*>(bh);
-            }
-            const uint32_t lw[4] = {rl.x, rl.y, rl.z, rl.w}, hw[4] = {rh.x, rh.y, rh.z, rh.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                uint32_t q0, q1;
-                join_bytes(lw[k], hw[k], q0, q1);
-                p[2 * k] = pack2(clamp16(lo16(p[2 * k]) + lo16(q0)), clamp16(hi16(p[2 * k]) + hi16(q0)));
-                p[2 * k + 1] = pack2(clamp16(lo16(p[2 * k + 1]) + lo16(q1)), clamp16(hi16(p[2 * k + 1]) + hi16(q1)));
-            }
-        }
-    }
-    if (MODE == kEpiWsilu4) {
-        // out[c] = sat(sum_{k<4} lut[v[4c + k]]): four output channels cbase / 4 ..
-        int32_t r[4];
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            const int32_t s = __ldg(&e.lut[lo16(p[2 * g]) + 32768]) + __ldg(&e.lut[hi16(p[2 * g]) + 32768]) +
-                              __ldg(&e.lut[lo16(p[2 * g + 1]) + 32768]) + __ldg(&e.lut[hi16(p[2 * g + 1]) + 32768]);
-            r[g] = clamp16(s);
-        }
-        const uint32_t w0 = pack2(r[0], r[1]), w1 = pack2(r[2], r[3]);
-        uint8_t* dl = out.lo(opx) + (cbase >> 2);
-        uint8_t* dh = out.hi(opx) + (cbase >> 2);
-        if (n_valid >= 16) {
-            *reinterpret_cast<uint32_t*>(dl) = __byte_perm(w0, w1, 0x6420);
-            *reinterpret_cast<uint32_t*>(dh) = __byte_perm(w0, w1, 0x7531);
-        } else {
-            for (int g = 0; g < 4 && 4 * g < n_valid; ++g) {
-                dl[g] = static_cast<uint8_t>(r[g] & 0xff);
-                dh[g] = static_cast<uint8_t>((r[g] >> 8) & 0xff);
-            }
-        }
-        return;
-    }
-    if (MODE == kEpiShuffle2) return;  // stored by the caller, which knows the four target pixels
-    uint4 lo, hi;
-    split_bytes(p, lo, hi);
-    uint8_t* dl = out.lo(opx) + cbase;
-    uint8_t* dh = out.hi(opx) + cbase;
-    if (n_valid >= 16) {
-        *reinterpret_cast<uint4*>(dl) = lo;
-        *reinterpret_cast<uint4*>(dh) = hi;
-    } else {
-        const uint8_t* bl = reinterpret_cast<const uint8_t*>(&lo);
-        const uint8_t* bh = reinterpret_cast<const uint8_t*>(&hi);
-        for (int j = 0; j < n_valid; ++j) {
-            dl[j] = bl[j];
-            dh[j] = bh[j];
-        }
-    }
 }
 
 // pixel_shuffle(2) store: channel 4c + 2i + j of pixel (oy, ox) -> channel c
@@ -256,20 +134,53 @@ __device__ __forceinline__ void store_shuffle2(const Act& out, const uint32_t (&
     }
 }
 
-template <bool SPATIAL, int MODE, int BN>
+// Hands the drained accumulator columns back to the MMA warp.
+__device__ __forceinline__ void release_tmem(uint64_t* bar, int lane) {
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+}
+
+// rna(S / 8192) from V = 8 HH + (X >> 5) and U = LL + 256 (X & 31) + 4096
+// (recombine32 split in two halves).
+__device__ __forceinline__ int32_t finish_rna(int32_t V, int32_t U) {
+    const int32_t T = V + (U >> 13);
+    return T - static_cast<int32_t>(((U & 8191) == 0) & (T <= 0));
+}
+
+// Bounded barrier among the epilogue warps (an mbarrier round, so a warp that
+// gave up on a pipeline wait cannot leave the others blocked forever).
+__device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, int lane, int* status) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+    const bool ok = mbar_wait(bar, phase, status, 6);
+    phase ^= 1;
+    __syncwarp();
+    return ok;
+}
+
+template <bool SPATIAL>
+__device__ __forceinline__ void tma_store_tile(const CUtensorMap* map, const void* src, const TileCoord& tc, int c0,
+                                               int plane) {
+    if (SPATIAL)
+        tma_store_5d(map, src, c0, plane, tc.x0, tc.y0, tc.img);
+    else
+        tma_store_3d(map, src, c0, plane, static_cast<int>(tc.p0));
+}
+
+template <bool SPATIAL, int MODE, int SIGNED>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-                   const ConvTcArgs args) {
-    using T = Tile<BN>;
-    constexpr int S = T::kStages;
-    constexpr int NB = T::kBuffers;
+                   const __grid_constant__ CUtensorMap mapOut, const ConvTcArgs args) {
+    constexpr int STORE = MODE == kEpiShuffle2 ? kStoreThreads : (MODE == kEpiWsilu4 ? kStoreTmaQuarter : kStoreTma);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    int32_t* bias_s = reinterpret_cast<int32_t*>(smem + size_t(S) * T::kStageBytes);  // [n_tiles * BN]
-    __shared__ __align__(8) uint64_t full_bar[S];
-    __shared__ __align__(8) uint64_t empty_bar[S];
-    __shared__ __align__(8) uint64_t tmem_full[NB];
-    __shared__ __align__(8) uint64_t tmem_empty[NB];
+    uint8_t* staging = smem + size_t(kStages) * kStageBytes;                           // 1024-aligned
+    int32_t* bias_s = reinterpret_cast<int32_t*>(staging + kStagingBytes);             // [n_tiles * 128]
+    int16_t* lut_s = reinterpret_cast<int16_t*>(bias_s + args.n_tiles * kBN);          // LUT window
+    __shared__ __align__(8) uint64_t full_bar[kStages];
+    __shared__ __align__(8) uint64_t empty_bar[kStages];
+    __shared__ __align__(8) uint64_t tmem_full, tmem_empty, epi_bar;
     __shared__ uint32_t tmem_holder;
     __shared__ int consumed;
 
@@ -278,14 +189,13 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
     const int num_k = args.taps_h * args.taps_w * kb_per_tap;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
-        for (int b = 0; b < NB; ++b) {
-            mbar_init(&tmem_full[b], 1);
-            mbar_init(&tmem_empty[b], kEpiWarps);
-        }
+        mbar_init(&tmem_full, 1);
+        mbar_init(&tmem_empty, kEpiWarps);
+        mbar_init(&epi_bar, kEpiWarps);
         consumed = 0;
         fence_mbar_init();
     }
@@ -294,12 +204,18 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         tmem_relinquish();
     }
     // the whole bias vector, zero padded to the tile grid, once per CTA
-    for (int i = threadIdx.x; i < args.n_tiles * BN; i += kThreads) {
-        int32_t b = 0;
+    for (int i = threadIdx.x; i < args.n_tiles * kBN; i += kThreads) {
+        long long b = 0;
         if (args.epi.bias && i < args.co)
             b = args.epi.bias32 ? static_cast<const int32_t*>(args.epi.bias)[i]
                                 : static_cast<const int16_t*>(args.epi.bias)[i];
-        bias_s[i] = b;
+        bias_s[i] = stage_bias(b);
+    }
+    LutView lut{args.epi.lut, nullptr, 0, 0, 0};
+    if ((MODE == kEpiLut || MODE == kEpiWsilu4) && args.epi.lut_n > 0) {
+        for (int i = threadIdx.x; i < args.epi.lut_n; i += kThreads)
+            lut_s[i] = args.epi.lut[args.epi.lut_start + 32768 + i];
+        lut = LutView{args.epi.lut, lut_s, args.epi.lut_start, args.epi.lut_n, args.epi.lut_hi};
     }
     tc_fence_before();
     __syncthreads();
@@ -311,21 +227,19 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         if (lane == 0) {
             prefetch_tmap(&mapA);
             prefetch_tmap(&mapB);
-            int it = 0;
+            int it = 0, s = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x) {
-                const TileCoord tc = tile_coord<SPATIAL, BN>(args, tile);
+                const TileCoord tc = tile_coord<SPATIAL>(args, tile);
                 for (int k = 0; k < num_k; ++k, ++it) {
-                    const int s = it % S;
-                    const uint32_t round = it / S;
-                    if (it >= S && !mbar_wait(&empty_bar[s], (round - 1) & 1, args.status, 1)) {
+                    if (it >= kStages && !mbar_wait(&empty_bar[s], ((it / kStages) - 1) & 1, args.status, 1)) {
                         ok = false;
                         break;
                     }
                     const int tap = k / kb_per_tap, cb = k - tap * kb_per_tap;
                     const int ky = tap / args.taps_w, kx = tap - ky * args.taps_w;
-                    uint8_t* st = smem + size_t(s) * T::kStageBytes;
-                    mbar_arrive_expect_tx(&full_bar[s], T::kStageBytes);
+                    uint8_t* st = smem + size_t(s) * kStageBytes;
+                    mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
                     const int c0 = cb * kBK;
                     if (SPATIAL) {
                         const int ix = tc.x0 + kx - args.pad_w, iy = tc.y0 + ky - args.pad_h;
@@ -335,46 +249,44 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         tma_load_3d(st, &mapA, &full_bar[s], c0, 0, static_cast<int>(tc.p0));
                         tma_load_3d(st + kABytes, &mapA, &full_bar[s], c0, 1, static_cast<int>(tc.p0));
                     }
-                    tma_load_2d(st + 2 * kABytes, &mapB, &full_bar[s], tap * args.cpad + c0, (tc.co0 / BN) * 2 * BN);
+                    tma_load_2d(st + 2 * kABytes, &mapB, &full_bar[s], tap * args.cpad + c0, (tc.co0 / kBN) * 2 * kBN);
                     issued = it + 1;
+                    if (++s == kStages) s = 0;
                 }
             }
         }
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t i_uu = i8_idesc(kBM, BN, false, false);
-            constexpr uint32_t i_su = i8_idesc(kBM, BN, true, false);
-            constexpr uint32_t i_us = i8_idesc(kBM, BN, false, true);
-            constexpr uint32_t i_ss = i8_idesc(kBM, BN, true, true);
-            constexpr uint32_t i_us2 = i8_idesc(kBM, 2 * BN, false, true);
-            constexpr uint32_t i_ss2 = i8_idesc(kBM, 2 * BN, true, true);
-            int it = 0, ti = 0;
+            constexpr uint32_t i_uu = i8_idesc(kBM, kBN, false, false);
+            constexpr uint32_t i_su = i8_idesc(kBM, kBN, true, false);
+            constexpr uint32_t i_us = i8_idesc(kBM, kBN, false, true);
+            constexpr uint32_t i_ss = i8_idesc(kBM, kBN, true, true);
+            constexpr uint32_t i_us2 = i8_idesc(kBM, 2 * kBN, false, true);
+            constexpr uint32_t i_ss2 = i8_idesc(kBM, 2 * kBN, true, true);
+            int it = 0, s = 0, ti = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x, ++ti) {
-                const int buf = ti % NB, use = ti / NB;
-                if (use > 0 && !mbar_wait(&tmem_empty[buf], (use - 1) & 1, args.status, 3)) {
+                if (ti > 0 && !mbar_wait(&tmem_empty, (ti - 1) & 1, args.status, 3)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_ll = tmem + buf * T::kBufferStride, d_x = d_ll + BN, d_hh = d_ll + 2 * BN;
+                const uint32_t d_ll = tmem + (ti & 1) * kBN, d_x = d_ll + kBN, d_hh = d_ll + 2 * kBN;
                 for (int k = 0; k < num_k; ++k, ++it) {
-                    const int s = it % S;
-                    const uint32_t round = it / S;
-                    if (!mbar_wait(&full_bar[s], round & 1, args.status, 2)) {
+                    if (!mbar_wait(&full_bar[s], (it / kStages) & 1, args.status, 2)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t base = smem_u32(smem + size_t(s) * T::kStageBytes);
+                    const uint32_t base = smem_u32(smem + size_t(s) * kStageBytes);
                     const uint32_t a_lo = base, a_hi = base + kABytes, b_lo = base + 2 * kABytes,
-                                   b_hi = b_lo + BN * kBK;
+                                   b_hi = b_lo + kBN * kBK;
 #pragma unroll
                     for (int kk = 0; kk < kBK / 32; ++kk) {
                         const uint32_t o = kk * 32;
                         const bool first = k == 0 && kk == 0;
-                        if (args.signed_split) {
+                        if (SIGNED) {
                             mma_i8(d_ll, sw128_desc(a_lo + o), sw128_desc(b_lo + o), i_us2, first ? 0u : 1u);
                             if (first) {
                                 mma_i8(d_x, sw128_desc(a_hi + o), sw128_desc(b_lo + o), i_ss, 1u);
@@ -391,97 +303,214 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         }
                     }
                     mma_commit(&empty_bar[s]);
+                    if (++s == kStages) s = 0;
                 }
                 if (!ok) break;
-                mma_commit(&tmem_full[buf]);
+                mma_commit(&tmem_full);
             }
             consumed = it;
         }
         __syncwarp();
-    } else {
-        constexpr int kC = T::kCols;                   // 32 (BN 128) or 16 (BN 64)
+    } else if (warp >= kFirstEpiWarp) {
         const int quarter = warp & 3;
-        const int cgroup = (warp - 2) >> 2;            // columns [kC * cgroup, kC * cgroup + kC)
-        const int row = quarter * 32 + lane;
-        const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        const int cgroup = (warp - kFirstEpiWarp) >> 2;  // accumulator columns [32 cgroup, 32 cgroup + 32)
+        const int row = quarter * 32 + lane;            // TMEM lane = pixel of the tile
+        const uint32_t acc = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + cgroup * 32;  // + set offset
+        const bool issuer = warp == kFirstEpiWarp && lane == 0;
         const Act& out = args.out;
+        uint32_t sync_phase = 0;
         int ti = 0;
         for (int tile = blockIdx.x; tile < args.total_tiles; tile += gridDim.x, ++ti) {
-            const int buf = ti % NB, use = ti / NB;
-            const TileCoord tc = tile_coord<SPATIAL, BN>(args, tile);
+            if (!mbar_wait(&tmem_full, ti & 1, args.status, 4)) break;
+            tc_fence_after();
+            const TileCoord tc = tile_coord<SPATIAL>(args, tile);
+            const int cbase = tc.co0 + cgroup * 32;
+            const int4* bq = reinterpret_cast<const int4*>(bias_s + cbase);
+            uint32_t p[16];
+            if ((ti & 1) == 0) {
+                // set at [0, 384); the next tile's set [128, 512) overlaps X and HH
+                const uint32_t a = acc;
+                uint32_t xx[32], hh[32];
+                tmem_ld32(a + kBN, xx);
+                tmem_ld32(a + 2 * kBN, hh);
+                tmem_wait_ld();
+                release_tmem(&tmem_empty, lane);
+                // V = 8 HH + (X >> 5); X & 31 kept as 5-bit fields, six per word
+                int32_t V[32];
+                uint32_t F[6] = {0, 0, 0, 0, 0, 0};
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    V[j] = static_cast<int32_t>(hh[j]) * 8 + (static_cast<int32_t>(xx[j]) >> 5);
+                    F[j / 6] |= (xx[j] & 31u) << (5 * (j % 6));
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t ll[16];
+                    tmem_ld16(a + 16 * h, ll);  // LL stays clear of the next tile's set
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int4 b = bq[4 * h + q];
+                        const int bb[4] = {b.x, b.y, b.z, b.w};
+                        int32_t r[4];
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            const int j = 16 * h + 4 * q + t;
+                            const int32_t f = static_cast<int32_t>((F[j / 6] >> (5 * (j % 6))) & 31u);
+                            r[t] = clamp16(finish_rna(V[j], static_cast<int32_t>(ll[4 * q + t]) + (f << 8) + 4096) + bb[t]);
+                        }
+                        p[8 * h + 2 * q] = pack2(r[0], r[1]);
+                        p[8 * h + 2 * q + 1] = pack2(r[2], r[3]);
+                    }
+                }
+            } else {
+                // set at [128, 512); the next tile's set [0, 384) overlaps LL and X
+                const uint32_t a = acc + kBN;
+                uint32_t ll[32], xx[32];
+                tmem_ld32(a, ll);
+                tmem_ld32(a + kBN, xx);
+                tmem_wait_ld();
+                release_tmem(&tmem_empty, lane);
+                // U = LL + 256 (X & 31) + 4096, W = (X >> 5) + (U >> 13), tie bit (U % 8192 == 0)
+                int32_t W[32];
+                uint32_t ties = 0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int32_t x = static_cast<int32_t>(xx[j]);
+                    const int32_t U = static_cast<int32_t>(ll[j]) + ((x & 31) << 8) + 4096;
+                    W[j] = (x >> 5) + (U >> 13);
+                    ties |= static_cast<uint32_t>((U & 8191) == 0) << j;
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t hh[16];
+                    tmem_ld16(a + 2 * kBN + 16 * h, hh);  // HH stays clear of the next tile's set
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int4 b = bq[4 * h + q];
+                        const int bb[4] = {b.x, b.y, b.z, b.w};
+                        int32_t r[4];
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            const int j = 16 * h + 4 * q + t;
+                            const int32_t T = static_cast<int32_t>(hh[4 * q + t]) * 8 + W[j];
+                            r[t] = clamp16(T - static_cast<int32_t>(((ties >> j) & 1u) & (T <= 0)) + bb[t]);
+                        }
+                        p[8 * h + 2 * q] = pack2(r[0], r[1]);
+                        p[8 * h + 2 * q + 1] = pack2(r[2], r[3]);
+                    }
+                }
+            }
             bool valid;
-            long long opx = 0, rpx1 = 0, rpx2 = 0;
+            long long rpx1 = 0, rpx2 = 0;
             int oy = 0, ox = 0;
             if (SPATIAL) {
                 const int ty = row / args.tile_w, tx = row - ty * args.tile_w;
                 oy = tc.y0 + ty;
                 ox = tc.x0 + tx;
                 valid = oy < args.oh && ox < args.ow;
-                if (MODE != kEpiShuffle2) opx = out.pixel(tc.img, oy, ox);
                 if (MODE == kEpiRes) {
                     rpx1 = args.epi.res1.pixel(tc.img, oy, ox);
                     rpx2 = args.epi.res2.pixel(tc.img, oy, ox);
                 }
             } else {
-                opx = rpx1 = rpx2 = tc.p0 + row;
-                valid = opx < args.m_total;
+                rpx1 = rpx2 = tc.p0 + row;
+                valid = rpx1 < args.m_total;
             }
-            if (!mbar_wait(&tmem_full[buf], use & 1, args.status, 4)) break;
-            tc_fence_after();
-            const uint32_t acc_addr = lane_addr + buf * T::kBufferStride;
-            // phase 1: accumulators -> sat(rna(sum / 8192) + bias), 16 columns at a time
-            uint32_t packed[kC / 2];
+            const int n_valid = args.co - cbase < 0 ? 0 : (args.co - cbase < 32 ? args.co - cbase : 32);
+            if (STORE == kStoreThreads) {
+                if (valid) {
 #pragma unroll
-            for (int c = 0; c < kC / 16; ++c) {
-                const int col = cgroup * kC + c * 16;
-                uint32_t ll[16], xx[16], hh[16];
-                tmem_ld16(acc_addr + col, ll);
-                tmem_ld16(acc_addr + BN + col, xx);
-                tmem_ld16(acc_addr + 2 * BN + col, hh);
-                const int4* bq = reinterpret_cast<const int4*>(bias_s + tc.co0 + col);
-                const int4 b4[4] = {bq[0], bq[1], bq[2], bq[3]};
-                const int32_t* bias = reinterpret_cast<const int32_t*>(b4);
-                tmem_wait_ld();
+                    for (int h = 0; h < 2; ++h) {
+                        if (16 * h >= n_valid) break;
+                        uint32_t p8[8];
 #pragma unroll
-                for (int j = 0; j < 16; j += 2) {
-                    int32_t r[2];
-#pragma unroll
-                    for (int t = 0; t < 2; ++t) {
-                        const int32_t L = static_cast<int32_t>(ll[j + t]), X = static_cast<int32_t>(xx[j + t]),
-                                      H = static_cast<int32_t>(hh[j + t]);
-                        if (args.wide) {
-                            const int64_t v = recombine64(L, X, H) + bias[j + t];
-                            r[t] = v < -32768 ? -32768 : (v > 32767 ? 32767 : static_cast<int32_t>(v));
-                        } else {
-                            const int64_t v = static_cast<int64_t>(recombine32(L, X, H)) + bias[j + t];
-                            r[t] = v < -32768 ? -32768 : (v > 32767 ? 32767 : static_cast<int32_t>(v));
-                        }
+                        for (int i = 0; i < 8; ++i) p8[i] = p[8 * h + i];
+                        store_shuffle2(out, p8, cbase + 16 * h, n_valid - 16 * h < 16 ? n_valid - 16 * h : 16,
+                                       tc.img, oy, ox);
                     }
-                    packed[c * 8 + j / 2] = pack2(r[0], r[1]);
                 }
+                continue;
             }
-            // this accumulator set is free for the MMAs of the tile after next
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_empty[buf]);
-            // phase 2: fused elementwise steps and stores, overlapped with MMAs
-            if (valid) {
+            // fused elementwise step (residual rows outside the image read nothing)
+            if (MODE == kEpiLut) {
 #pragma unroll
-                for (int c = 0; c < kC / 16; ++c) {
-                    const int cbase = tc.co0 + cgroup * kC + c * 16;
-                    if (cbase >= args.co) break;
-                    const int n_valid = args.co - cbase < 16 ? args.co - cbase : 16;
+                for (int i = 0; i < 16; ++i) p[i] = pack2(lut(lo16(p[i])), lut(hi16(p[i])));
+            }
+            if (MODE == kEpiRes && valid) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    if (16 * h >= n_valid) break;
                     uint32_t p8[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) p8[i] = packed[c * 8 + i];
-                    if (MODE == kEpiShuffle2)
-                        store_shuffle2(out, p8, cbase, n_valid, tc.img, oy, ox);
-                    else
-                        finish16<MODE>(args, p8, cbase, n_valid, opx, rpx1, rpx2, out);
+                    for (int i = 0; i < 8; ++i) p8[i] = p[8 * h + i];
+                    add_residuals(args.epi, p8, cbase + 16 * h, n_valid - 16 * h < 16 ? n_valid - 16 * h : 16, rpx1,
+                                  rpx2);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) p[8 * h + i] = p8[i];
                 }
             }
-            __syncwarp();
+            if (STORE == kStoreTma) {
+                // one byte plane at a time through the 128-byte-swizzled stage:
+                // row r holds the tile's 128 channels of pixel r, 16-byte chunk c
+                // at position c ^ (r & 7)
+                uint4 lo[2], hi[2];
+                uint32_t p8a[8], p8b[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    p8a[i] = p[i];
+                    p8b[i] = p[8 + i];
+                }
+                split_bytes(p8a, lo[0], hi[0]);
+                split_bytes(p8b, lo[1], hi[1]);
+                bool ok = true;
+#pragma unroll
+                for (int plane = 0; plane < 2; ++plane) {
+                    ok = ok && epi_sync(&epi_bar, sync_phase, lane, args.status);  // stage is free
+                    if (!ok) break;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int chunk = cgroup * 2 + h;
+                        *reinterpret_cast<uint4*>(staging + row * 128 + ((chunk ^ (row & 7)) << 4)) =
+                            plane ? hi[h] : lo[h];
+                    }
+                    fence_proxy_async_smem();
+                    ok = epi_sync(&epi_bar, sync_phase, lane, args.status);
+                    if (!ok) break;
+                    if (issuer) {
+                        tma_store_tile<SPATIAL>(&mapOut, staging, tc, tc.co0, plane);
+                        bulk_commit();
+                        bulk_wait_read();
+                    }
+                }
+                if (!ok) break;
+            } else {
+                // wsilu4: 8 output channels per thread, both planes staged at once
+                // as [plane][pixel][32 channels] (unswizzled, 32-byte rows)
+                int32_t r[8];
+#pragma unroll
+                for (int g = 0; g < 8; ++g)
+                    r[g] = clamp16(lut(lo16(p[2 * g])) + lut(hi16(p[2 * g])) + lut(lo16(p[2 * g + 1])) +
+                                   lut(hi16(p[2 * g + 1])));
+                const uint32_t w0 = pack2(r[0], r[1]), w1 = pack2(r[2], r[3]), w2 = pack2(r[4], r[5]),
+                               w3 = pack2(r[6], r[7]);
+                const uint2 lo = make_uint2(__byte_perm(w0, w1, 0x6420), __byte_perm(w2, w3, 0x6420));
+                const uint2 hi = make_uint2(__byte_perm(w0, w1, 0x7531), __byte_perm(w2, w3, 0x7531));
+                if (!epi_sync(&epi_bar, sync_phase, lane, args.status)) break;
+                *reinterpret_cast<uint2*>(staging + row * 32 + cgroup * 8) = lo;
+                *reinterpret_cast<uint2*>(staging + kBM * 32 + row * 32 + cgroup * 8) = hi;
+                fence_proxy_async_smem();
+                if (!epi_sync(&epi_bar, sync_phase, lane, args.status)) break;
+                if (issuer) {
+                    tma_store_tile<SPATIAL>(&mapOut, staging, tc, tc.co0 / 4, 0);
+                    tma_store_tile<SPATIAL>(&mapOut, staging + kBM * 32, tc, tc.co0 / 4, 1);
+                    bulk_commit();
+                    bulk_wait_read();
+                }
+            }
         }
+        if (issuer) bulk_wait_all();
     }
 
     tc_fence_before();
@@ -489,7 +518,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
     if (warp == 0 && lane == 0) {
         // abort path only: wait for TMA loads issued but never consumed, so no
         // copy into this CTA's shared memory outlives the CTA
-        for (int k = consumed; k < issued; ++k) mbar_wait(&full_bar[k % S], (k / S) & 1, args.status, 5);
+        for (int k = consumed; k < issued; ++k) mbar_wait(&full_bar[k % kStages], (k / kStages) & 1, args.status, 5);
     }
     if (warp == 1) {
         tc_fence_after();
@@ -548,7 +577,7 @@ EncodeTiledFn encode_fn() {
 }
 
 bool encode(CUtensorMap* map, void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
-            const cuuint32_t* box, std::string& err) {
+            const cuuint32_t* box, std::string& err, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     auto fn = encode_fn();
     if (!fn) {
         err = "cuTensorMapEncodeTiled is unavailable";
@@ -556,13 +585,19 @@ bool encode(CUtensorMap* map, void* base, int rank, const cuuint64_t* dims, cons
     }
     cuuint32_t elem[5] = {1, 1, 1, 1, 1};
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, base, dims, strides, box, elem,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         err = "cuTensorMapEncodeTiled failed with code " + std::to_string(static_cast<int>(r));
         return false;
     }
     return true;
+}
+
+std::atomic<int> g_max_ctas{0};
+
+int current_device() {
+    int device = 0;
+    return cudaGetDevice(&device) == cudaSuccess ? device : 0;
 }
 
 std::mutex g_dev_mutex;
@@ -578,38 +613,46 @@ int sm_count(int device) {
     return g_sms[device] > 0 ? g_sms[device] : 148;
 }
 
-template <bool SPATIAL, int MODE, int BN>
-cudaError_t launch_mode(const CUtensorMap& a, const CUtensorMap& b, const ConvTcArgs& args, cudaStream_t stream) {
-    int device = 0;
-    cudaError_t e = cudaGetDevice(&device);
-    if (e != cudaSuccess) return e;
-    const size_t smem = Tile<BN>::kRingBytes + size_t(args.n_tiles) * BN * sizeof(int32_t);
+template <bool SPATIAL, int MODE, int SIGNED>
+cudaError_t launch_mode(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const ConvTcArgs& args,
+                        size_t smem, int sms, cudaStream_t stream) {
+    auto kernel = conv_i16_tc_kernel<SPATIAL, MODE, SIGNED>;
     // the attribute is per function and device; setting it each launch is cheap
-    e = cudaFuncSetAttribute(conv_i16_tc_kernel<SPATIAL, MODE, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    const int sms = sm_count(device);
-    const int grid = args.total_tiles < sms ? args.total_tiles : sms;
-    conv_i16_tc_kernel<SPATIAL, MODE, BN><<<grid, kThreads, smem, stream>>>(a, b, args);
+    int grid = args.total_tiles < sms ? args.total_tiles : sms;
+    const int cap = g_max_ctas.load(std::memory_order_relaxed);
+    if (cap > 0 && grid > cap) grid = cap;
+    kernel<<<grid, kThreads, smem, stream>>>(a, b, o, args);
     return cudaGetLastError();
 }
 
-template <bool SPATIAL, int BN>
-cudaError_t launch_bn(const CUtensorMap& a, const CUtensorMap& b, const ConvTcArgs& args, cudaStream_t stream) {
+template <bool SPATIAL, int SIGNED>
+cudaError_t launch_signed(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const ConvTcArgs& args,
+                          size_t smem, int sms, cudaStream_t stream) {
     const Epilogue& e = args.epi;
-    if (e.shuffle2) return launch_mode<SPATIAL, kEpiShuffle2, BN>(a, b, args, stream);
-    if (e.wsilu4) return launch_mode<SPATIAL, kEpiWsilu4, BN>(a, b, args, stream);
-    if (e.lut) return launch_mode<SPATIAL, kEpiLut, BN>(a, b, args, stream);
-    if (e.res1.base) return launch_mode<SPATIAL, kEpiRes, BN>(a, b, args, stream);
-    return launch_mode<SPATIAL, kEpiPlain, BN>(a, b, args, stream);
+    if (e.shuffle2) return launch_mode<SPATIAL, kEpiShuffle2, SIGNED>(a, b, o, args, smem, sms, stream);
+    if (e.wsilu4) return launch_mode<SPATIAL, kEpiWsilu4, SIGNED>(a, b, o, args, smem, sms, stream);
+    if (e.lut) return launch_mode<SPATIAL, kEpiLut, SIGNED>(a, b, o, args, smem, sms, stream);
+    if (e.res1.base) return launch_mode<SPATIAL, kEpiRes, SIGNED>(a, b, o, args, smem, sms, stream);
+    return launch_mode<SPATIAL, kEpiPlain, SIGNED>(a, b, o, args, smem, sms, stream);
 }
 
 template <bool SPATIAL>
-cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b, const ConvTcArgs& args, int bn, cudaStream_t stream) {
-    return bn == 64 ? launch_bn<SPATIAL, 64>(a, b, args, stream) : launch_bn<SPATIAL, 128>(a, b, args, stream);
+cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const ConvTcArgs& args,
+                   size_t smem, int sms, cudaStream_t stream) {
+    return args.signed_split ? launch_signed<SPATIAL, 1>(a, b, o, args, smem, sms, stream)
+                             : launch_signed<SPATIAL, 0>(a, b, o, args, smem, sms, stream);
 }
 
 }  // namespace
+
+void tc_set_max_ctas(int n) { g_max_ctas.store(n > 0 ? n : 0, std::memory_order_relaxed); }
+
+bool tc_encode_map(CUtensorMap* map, void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                   const cuuint32_t* box, std::string& err) {
+    return encode(map, base, rank, dims, strides, box, err);
+}
 
 size_t tc_weight_bytes(int co, int ci, int kh, int kw, int bn) {
     const int cpad = (ci + kBK - 1) / kBK * kBK;
@@ -617,11 +660,18 @@ size_t tc_weight_bytes(int co, int ci, int kh, int kw, int bn) {
     return static_cast<size_t>(co_tiles) * 2 * bn * kh * kw * cpad;
 }
 
-int tc_choose_bn(int ci, int kh, int kw, bool signed_split) {
-    // reductions of up to 512 are dominated by the per-tile epilogue: the
-    // 64-wide tile double-buffers TMEM so the epilogue overlaps the MMAs; the
-    // signed split keeps its MMAs 128 wide (full rate)
-    return signed_split && static_cast<long long>(ci) * kh * kw <= 512 ? 64 : 128;
+int tc_choose_bn(int, int, int, bool) { return kBN; }
+
+void tc_lut_window(const int16_t* table, int& start, int& n, int& hi) {
+    int first_nonzero = 32768, last_moved = -32769;
+    for (int v = -32768; v <= 32767; ++v) {
+        if (table[v + 32768] != 0 && first_nonzero == 32768) first_nonzero = v;
+        if (table[v + 32768] != v) last_moved = v;
+    }
+    start = first_nonzero > -32768 ? first_nonzero - 1 : -32768;  // lut[start] == 0 unless start == -32768
+    hi = last_moved;
+    const int end = last_moved < 32767 ? last_moved + 1 : 32767;   // inclusive
+    n = end >= start && end - start + 1 <= 8192 ? end - start + 1 : 0;
 }
 
 bool tc_signed_split_ok(const int16_t* weight_host, size_t count) {
@@ -678,6 +728,10 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
         err = "input channels do not match weights";
         return -1;
     }
+    if (w.bn != kBN) {
+        err = "weights must be prepared in 128-wide tiles";
+        return -1;
+    }
     if ((in.pitch % 16) || (reinterpret_cast<uintptr_t>(in.base) % 16) || (out.pitch % 16) ||
         (reinterpret_cast<uintptr_t>(out.base) % 16)) {
         err = "split activations need 16-byte aligned pitch and channel offset";
@@ -695,14 +749,18 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
         err = "unsupported epilogue combination (one of lut, residual adds, wsilu4, pixel shuffle; no multiply)";
         return -1;
     }
-    const size_t ring = w.bn == 64 ? Tile<64>::kRingBytes : Tile<128>::kRingBytes;
-    if (w.co_tiles * w.bn * sizeof(int32_t) + ring > 227 * 1024) {
+    if (epi.wsilu4 && (w.co % 4 || out.c != w.co / 4)) {
+        err = "wsilu4 output must have a quarter of the convolution's channels";
+        return -1;
+    }
+    const size_t base_smem = 1024 + size_t(kStages) * kStageBytes + kStagingBytes + size_t(w.co_tiles) * kBN * 4;
+    if (base_smem > kSmemLimit) {
         err = "too many output channels for the staged bias";
         return -1;
     }
     const long long k_total = static_cast<long long>(w.kh) * w.kw * w.ci;
-    if (k_total > 32768) {
-        err = "reduction exceeds the exact s32 accumulator bound";
+    if (k_total > kTcMaxReduction) {
+        err = "reduction longer than the tensor-core path's 32-bit recombination bound";
         return -1;
     }
     const bool flat = w.kh == 1 && w.kw == 1 && pad_h == 0 && pad_w == 0 && in.dense() && out.dense() &&
@@ -711,6 +769,10 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     ConvTcArgs args{};
     args.out = out;
     args.epi = epi;
+    // the LUT window rides in shared memory after the bias when it fits
+    const size_t lut_bytes = (static_cast<size_t>(epi.lut_n) * 2 + 15) / 16 * 16;
+    if (!epi.lut || epi.lut_n <= 0 || base_smem + lut_bytes > kSmemLimit) args.epi.lut_n = 0;
+    const size_t smem = base_smem + (args.epi.lut_n > 0 ? lut_bytes : 0);
     args.co = w.co;
     args.ci = w.ci;
     args.taps_h = w.kh;
@@ -721,16 +783,23 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     args.oh = oh;
     args.ow = ow;
     args.signed_split = w.signed_split ? 1 : 0;
-    args.wide = k_total >= 16384 ? 1 : 0;
     args.status = status;
     args.n_tiles = w.co_tiles;
-    CUtensorMap amap;
+    // output box: 128 channels of one plane (128-byte swizzle), or 32 channels
+    // (wsilu4, unswizzled); the map's extent is the view's, so tails are clipped
+    const cuuint32_t out_box_c = epi.wsilu4 ? kBN / 4 : kBN;
+    const CUtensorMapSwizzle out_swizzle = epi.wsilu4 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B;
+    CUtensorMap amap, omap;
     long long m_tiles;
     if (flat) {
         const cuuint64_t dims[3] = {static_cast<cuuint64_t>(in.c), 2, static_cast<cuuint64_t>(in.pixels())};
         const cuuint64_t strides[2] = {static_cast<cuuint64_t>(in.pitch), static_cast<cuuint64_t>(2 * in.pitch)};
         const cuuint32_t box[3] = {kBK, 1, kBM};
         if (!encode(&amap, in.base, 3, dims, strides, box, err)) return -1;
+        const cuuint64_t odims[3] = {static_cast<cuuint64_t>(out.c), 2, static_cast<cuuint64_t>(out.pixels())};
+        const cuuint64_t ostrides[2] = {static_cast<cuuint64_t>(out.pitch), static_cast<cuuint64_t>(2 * out.pitch)};
+        const cuuint32_t obox[3] = {out_box_c, 1, kBM};
+        if (!encode(&omap, out.base, 3, odims, ostrides, obox, err, out_swizzle)) return -1;
         args.m_total = in.pixels();
         m_tiles = (in.pixels() + kBM - 1) / kBM;
     } else {
@@ -747,6 +816,18 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
                                        static_cast<cuuint64_t>(2 * in.pitch) * in.img_px};
         const cuuint32_t box[5] = {kBK, 1, static_cast<cuuint32_t>(tw), static_cast<cuuint32_t>(th), 1};
         if (!encode(&amap, in.base, 5, dims, strides, box, err)) return -1;
+        if (!epi.shuffle2) {
+            const cuuint64_t odims[5] = {static_cast<cuuint64_t>(out.c), 2, static_cast<cuuint64_t>(out.w),
+                                         static_cast<cuuint64_t>(out.h), static_cast<cuuint64_t>(out.n)};
+            const cuuint64_t ostrides[4] = {static_cast<cuuint64_t>(out.pitch),
+                                            static_cast<cuuint64_t>(2 * out.pitch),
+                                            static_cast<cuuint64_t>(2 * out.pitch) * out.row_px,
+                                            static_cast<cuuint64_t>(2 * out.pitch) * out.img_px};
+            const cuuint32_t obox[5] = {out_box_c, 1, static_cast<cuuint32_t>(tw), static_cast<cuuint32_t>(th), 1};
+            if (!encode(&omap, out.base, 5, odims, ostrides, obox, err, out_swizzle)) return -1;
+        } else {
+            omap = amap;  // unused: pixel-shuffled tiles are stored by the threads
+        }
         m_tiles = static_cast<long long>(args.tiles_x) * args.tiles_y * in.n;
     }
     const long long total = m_tiles * w.co_tiles;
@@ -755,8 +836,9 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
         return -1;
     }
     args.total_tiles = static_cast<int>(total);
-    const cudaError_t e =
-        flat ? launch<false>(amap, w.map, args, w.bn, stream) : launch<true>(amap, w.map, args, w.bn, stream);
+    const int sms = sm_count(current_device());
+    const cudaError_t e = flat ? launch<false>(amap, w.map, omap, args, smem, sms, stream)
+                               : launch<true>(amap, w.map, omap, args, smem, sms, stream);
     if (e != cudaSuccess) {
         err = std::string("conv launch failed: ") + cudaGetErrorString(e);
         return -1;

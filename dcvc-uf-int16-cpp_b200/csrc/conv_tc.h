@@ -9,8 +9,13 @@
 
 namespace ufb {
 
+// Longest reduction (taps x input channels) the tensor-core kernel takes: its
+// epilogue recombines the byte-product accumulators in 32-bit arithmetic.
+// Longer reductions run on the int64 SIMT path.
+constexpr long long kTcMaxReduction = 8192;
+
 // Device-resident convolution weights prepared for the tensor-core kernel.
-// Layout: [co_tiles][2][bn][kpad] bytes -- per tile of bn (64 or 128) output
+// Layout: [co_tiles][2][bn][kpad] bytes -- per tile of bn (128) output
 // channels, bn rows of the weights' low bytes followed by bn rows of their high bytes,
 // k = (ky * kw + kx) * cpad + c, zero rows / columns as padding.
 //   unsigned split (any weights):   w = lo + 256 hi, lo u8 = w & 0xff, hi s8 = w >> 8
@@ -27,8 +32,7 @@ struct TcWeights {
 // Bytes needed for the prepared planes of a [co, ci, kh, kw] convolution.
 size_t tc_weight_bytes(int co, int ci, int kh, int kw, int bn);
 
-// Tile width used for a layer (64: double-buffered accumulators, for small
-// reductions with the signed split; otherwise 128).
+// Tile width used for a layer (the kernel runs 128-wide output tiles).
 int tc_choose_bn(int ci, int kh, int kw, bool signed_split);
 
 // Describe already prepared planes (fields + TMA map; no device work).
@@ -40,8 +44,22 @@ bool tc_describe(TcWeights& w, int co, int ci, int kh, int kw, bool signed_split
 bool tc_prepare(TcWeights& w, const int16_t* weight, int co, int ci, int kh, int kw, bool signed_split, int bn,
                 uint8_t* planes, cudaStream_t s, std::string& err);
 
+// Shared-memory window of a 65536-entry lookup table (host data, index
+// v + 32768): lut[v] == 0 for every v < start + 1, lut[v] == v for every
+// v > hi, and entries [start, start + n) cover the rest (n == 0: no window;
+// kernels then read the global table).
+void tc_lut_window(const int16_t* table, int& start, int& n, int& hi);
+
 // True when every weight allows the signed split (host data).
 bool tc_signed_split_ok(const int16_t* weight_host, size_t count);
+
+// cuTensorMapEncodeTiled for a byte tensor with the 128-byte swizzle.
+bool tc_encode_map(CUtensorMap* map, void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                   const cuuint32_t* box, std::string& err);
+
+// Caps the persistent grid at n CTAs (0: one per SM).  A testing aid: with few
+// CTAs every CTA walks many tiles, which exercises both TMEM accumulator sets.
+void tc_set_max_ctas(int n);
 
 // out = epilogue(conv(in, w)), stride 1, zero padding (pad_h, pad_w).
 // Both views must have 16-byte aligned pitch and base.  Asynchronous on

@@ -1,5 +1,7 @@
 #include "engine.h"
 
+#include <cstdio>
+
 #include "engine_kernels.h"
 #include "kernels.h"
 
@@ -91,20 +93,40 @@ void* Pinned::get(size_t bytes) {
 
 EngineStats::~EngineStats() {
     for (auto& e : pending) {
-        cudaEventDestroy(e.first);
-        cudaEventDestroy(e.second);
+        cudaEventDestroy(e.start);
+        cudaEventDestroy(e.stop);
     }
     for (auto e : spare) cudaEventDestroy(e);
+}
+
+cudaEvent_t EngineStats::take_event() {
+    cudaEvent_t ev = nullptr;
+    if (!spare.empty()) {
+        ev = spare.back();
+        spare.pop_back();
+    } else {
+        ck(cudaEventCreate(&ev), "event");
+    }
+    return ev;
 }
 
 void EngineStats::collect() {
     for (auto& e : pending) {
         float ms = 0;
-        if (cudaEventElapsedTime(&ms, e.first, e.second) == cudaSuccess) conv_ms += ms;
-        spare.push_back(e.first);
-        spare.push_back(e.second);
+        if (cudaEventElapsedTime(&ms, e.start, e.stop) == cudaSuccess) {
+            if (e.tensor_core) conv_ms += ms;
+            shapes[e.shape].ms += ms;
+        }
+        spare.push_back(e.start);
+        spare.push_back(e.stop);
     }
     pending.clear();
+}
+
+void EngineStats::reset() {
+    launches = conv_launches = 0;
+    conv_int16_macs = conv_ms = 0;
+    shapes.clear();
 }
 
 // ----------------------------------------------------------------- model ----
@@ -149,6 +171,7 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
         } else if (t.name == "tables.wsilu") {
             if (t.dtype != 0 || numel != 65536) throw std::invalid_argument("invalid WSiLU table");
             wsilu_ = static_cast<int16_t*>(upload(t.data, numel * 2));
+            tc_lut_window(static_cast<const int16_t*>(t.data), wsilu_start_, wsilu_n_, wsilu_hi_);
         } else if (t.name == "tables.scale_index") {
             if (t.dtype != 1 || numel != 65536) throw std::invalid_argument("invalid scale-index table");
             scale_index_ = static_cast<uint8_t*>(upload(t.data, numel));
@@ -177,7 +200,7 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
         ConvLayer& L = kv.second;
         if (!L.weights16) throw std::runtime_error("Missing prepared UF tensor: " + kv.first + ".weight");
         L.depthwise = L.ci == 1 && L.co > 1;
-        if (L.depthwise || static_cast<long long>(L.ci) * L.kh * L.kw > 32768) continue;
+        if (L.depthwise || static_cast<long long>(L.ci) * L.kh * L.kw > kTcMaxReduction) continue;
         const bool sgn = signed_ok[kv.first];
         const int bn = tc_choose_bn(L.ci, L.kh, L.kw, sgn);
         void* planes = nullptr;
@@ -252,7 +275,22 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
     if (grouped) {
         if (L->kh != 3 || L->kw != 3 || stride != 1 || f.lut || f.wsilu4 || f.shuffle2 || f.res1 || f.mulq)
             throw std::invalid_argument("unsupported depthwise configuration in " + name);
+        cudaEvent_t ev0 = nullptr;
+        if (stats_ && stats_->profile) {
+            ev0 = stats_->take_event();
+            ck(cudaEventRecord(ev0, s_), "event");
+        }
         ck(dwconv3x3(in.a, out.a, L->weights16, L->bias, s_), "depthwise conv");
+        if (ev0) {
+            cudaEvent_t ev1 = stats_->take_event();
+            ck(cudaEventRecord(ev1, s_), "event");
+            char key[96];
+            snprintf(key, sizeof(key), "depthwise %d 3x3 @ %lld", L->co, static_cast<long long>(in.a.n) * oh * ow);
+            stats_->pending.push_back({ev0, ev1, key, false});
+            auto& sh = stats_->shapes[key];
+            ++sh.launches;
+            sh.int16_macs += static_cast<double>(in.a.n) * oh * ow * L->co * 9;
+        }
         count();
         return out;
     }
@@ -261,34 +299,38 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
         e.bias = L->bias;
         e.bias32 = 0;
         e.lut = (f.lut || f.wsilu4) ? m_.wsilu() : nullptr;
+        e.lut_start = m_.wsilu_start();
+        e.lut_n = m_.wsilu_n();
+        e.lut_hi = m_.wsilu_hi();
         e.wsilu4 = f.wsilu4;
         e.shuffle2 = f.shuffle2;
         if (f.res1) e.res1 = f.res1->a;
         if (f.res2) e.res2 = f.res2->a;
         e.mulq = f.mulq;
         std::string err;
-        cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+        const double macs = static_cast<double>(in.a.n) * oh * ow * L->co * L->ci * L->kh * L->kw;
+        cudaEvent_t ev0 = nullptr;
         if (stats_ && stats_->profile) {
-            for (cudaEvent_t* ev : {&ev0, &ev1}) {
-                if (!stats_->spare.empty()) {
-                    *ev = stats_->spare.back();
-                    stats_->spare.pop_back();
-                } else {
-                    ck(cudaEventCreate(ev), "event");
-                }
-            }
+            ev0 = stats_->take_event();
             ck(cudaEventRecord(ev0, s_), "event");
         }
         if (conv_tc_run(L->tc, in.a, out.a, e, pad, pad, s_, status_, err) != 0)
             throw std::runtime_error(name + ": " + err);
         if (ev0) {
+            cudaEvent_t ev1 = stats_->take_event();
             ck(cudaEventRecord(ev1, s_), "event");
-            stats_->pending.emplace_back(ev0, ev1);
+            char key[96];
+            snprintf(key, sizeof(key), "conv %d>%d %dx%d @ %lld", L->ci, L->co, L->kh, L->kw,
+                     static_cast<long long>(in.a.n) * oh * ow);
+            stats_->pending.push_back({ev0, ev1, key, true});
+            auto& sh = stats_->shapes[key];
+            ++sh.launches;
+            sh.int16_macs += macs;
         }
         if (stats_) {
             ++stats_->launches;
             ++stats_->conv_launches;
-            stats_->conv_int16_macs += static_cast<double>(in.a.n) * oh * ow * L->co * L->ci * L->kh * L->kw;
+            stats_->conv_int16_macs += macs;
         }
         return out;
     }

@@ -95,6 +95,10 @@ public:
     bool has(const std::string& name) const { return names_.count(name) != 0; }
     bool has_child(const std::string& prefix) const;
     const int16_t* wsilu() const { return wsilu_; }
+    // shared-memory window of the WSiLU table (Epilogue::lut_start / lut_n / lut_hi)
+    int wsilu_start() const { return wsilu_start_; }
+    int wsilu_n() const { return wsilu_n_; }
+    int wsilu_hi() const { return wsilu_hi_; }
     const uint8_t* scale_index() const { return scale_index_; }
     const RansTables& z_table() const { return z_table_; }
     const RansTables& y_table() const { return y_table_; }
@@ -107,6 +111,7 @@ private:
     std::map<std::string, ParamTable> params_;
     std::vector<void*> allocations_;
     int16_t* wsilu_ = nullptr;
+    int wsilu_start_ = 0, wsilu_n_ = 0, wsilu_hi_ = 0;
     uint8_t* scale_index_ = nullptr;
     RansTables z_table_, y_table_;
 };
@@ -119,9 +124,24 @@ struct EngineStats {
     double conv_int16_macs = 0;    // algorithmic int16 MACs of those launches
     double conv_ms = 0;            // summed event time of those launches (profiling on)
     bool profile = false;
-    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;
+    // per launch shape ("conv ci>co kh x kw @ pixels", "depthwise c @ pixels"),
+    // filled while profiling is on
+    struct Shape {
+        long long launches = 0;
+        double int16_macs = 0;
+        double ms = 0;
+    };
+    std::map<std::string, Shape> shapes;
+    struct Pending {
+        cudaEvent_t start, stop;
+        std::string shape;
+        bool tensor_core;
+    };
+    std::vector<Pending> pending;
     std::vector<cudaEvent_t> spare;
+    cudaEvent_t take_event();
     void collect();                // adds the elapsed time of completed launches
+    void reset();
     ~EngineStats();
 };
 

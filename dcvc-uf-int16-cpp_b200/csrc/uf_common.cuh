@@ -88,6 +88,9 @@ struct Epilogue {
     const void* bias;    // int16 or int32 per output channel, or null
     int bias32;          // 1 when bias is int32
     const int16_t* lut;  // 65536-entry table applied after the bias (or wsilu4 table)
+    int lut_start;       // lut_n > 0: entries [lut_start, lut_start + lut_n) hold every value
+    int lut_n;           //   that is not lut[lut_start] (v below) or v itself (v > lut_hi),
+    int lut_hi;          //   so kernels may stage just that window in shared memory
     int wsilu4;          // 1: reduce groups of four channels through lut
     int shuffle2;        // 1: pixel-shuffle(2) store
     Act res1, res2;      // residual inputs in output coordinates (base == null: none)

@@ -41,6 +41,11 @@ int ufb_version(void);
 /* Message of the last failing call on this thread ("" if none). */
 const char* ufb_last_error(void);
 
+/* Testing aid (no reference counterpart): caps the persistent tensor-core
+ * convolution grid at n CTAs per launch (0 restores one CTA per SM), so small
+ * problems still run many tiles per CTA.  Process-wide; not for production. */
+int ufb_set_conv_max_ctas(int n);
+
 /* Synchronise `device` and return then clear its kernel status word:
  * 0 when no kernel reported a pipeline timeout since the last call, else the
  * first recorded code (1..4 = TMA producer / MMA / epilogue / drain wait). */
@@ -57,7 +62,7 @@ int ufb_device_status(int device);
  * x [n, ci, h, w], weight [co, ci/groups, kh, kw], bias [co] or NULL with
  * bias_bits 16 (int16, the reference's type) or 32 (int32, widened exactly as
  * src/int16_ops.cpp:163-167 does on the CPU path), out [n, co, oh, ow].
- * groups == 1, stride 1 and ci*kh*kw <= 32768 run on the tcgen05 tensor cores;
+ * groups == 1, stride 1 and ci*kh*kw <= 8192 run on the tcgen05 tensor cores;
  * other geometries use the direct int64 kernel (as the reference does). */
 int ufb_conv2d(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
                const void* bias, int bias_bits, int stride_h, int stride_w, int pad_h, int pad_w, int groups,
@@ -127,7 +132,7 @@ int64_t ufb_weight_bytes(int co, int ci, int kh, int kw);
 int ufb_prepare_weights(const int16_t* weight, int co, int ci, int kh, int kw, uint8_t* planes, void* stream);
 
 /* uf_conv on split activations with prepared weights: stride 1, zero padding
- * (pad_h, pad_w), groups 1, ci*kh*kw <= 32768.  Uses no scratch memory. */
+ * (pad_h, pad_w), groups 1, ci*kh*kw <= 8192.  Uses no scratch memory. */
 int ufb_conv2d_split(const uint8_t* x, int n, int ci, int h, int w, int x_pitch, const uint8_t* planes, int co,
                      int kh, int kw, const void* bias, int bias_bits, int pad_h, int pad_w, uint8_t* out,
                      int out_pitch, void* stream);
@@ -243,6 +248,11 @@ int ufb_codec_set_stream(ufb_codec* c, void* stream);
 int ufb_codec_profile(ufb_codec* c, int enable);
 int ufb_codec_stats(ufb_codec* c, int reset, int64_t* launches, int64_t* conv_launches, double* conv_int16_macs,
                     double* conv_ms);
+/* Per launch shape breakdown of the profiled convolutions (tensor-core and
+ * depthwise) since the last reset, one tab-separated line per shape:
+ * "<shape>\t<launches>\t<int16 MACs>\t<ms>".  Writes at most capacity - 1 bytes
+ * plus a terminating zero and sets *length to the full text length. */
+int ufb_codec_shape_table(ufb_codec* c, char* text, int64_t capacity, int64_t* length);
 
 /* ---------------------------------------------------------------------------
  * No-allocation convolution (no counterpart in the reference: its uf_conv
@@ -263,7 +273,7 @@ int ufb_codec_stats(ufb_codec* c, int reset, int64_t* launches, int64_t* conv_la
  * in one fixed device array of UFB_NOALLOC_SCRATCH_BYTES that the library
  * holds on every GPU it is loaded on until the process exits; a call whose
  * staging would exceed it fails with UFB_ERANGE and a message giving the
- * needed size.  Other geometries (grouped, strided, K > 32768) use the direct
+ * needed size.  Other geometries (grouped, strided, K > 8192) use the direct
  * kernel, which needs no scratch.
  *
  * The first call on a device resolves the array's device address with that

@@ -41,13 +41,20 @@ def rnd(rng, shape, lo=-3000, hi=3000):
     ("recon_head.conv.3", [(1, 512, 8, 8)], None),
     ("hyper_encoder", [(1, 256, 8, 8)], None),
 ])
-def test_htl_module_parity(models, module, shapes, q):
+@pytest.mark.parametrize("ctas", [0, 1])
+def test_htl_module_parity(ufb, models, module, shapes, q, ctas):
+    """ctas=1 runs every convolution on one persistent CTA, so each one walks
+    all its tiles and alternates between the two TMEM accumulator sets."""
     mine, theirs = models["htl"]
     rng = np.random.default_rng(abs(hash(module)) % 1000)
     args = [rnd(rng, s) for s in shapes]
     qp = 20
     want = theirs.run(module, *(args + ([theirs.parameter(q, qp)] if q else [])))
-    got = mine.run(module, *args, q_name=q, qp=qp)
+    ufb.set_conv_max_ctas(ctas)
+    try:
+        got = mine.run(module, *args, q_name=q, qp=qp)
+    finally:
+        ufb.set_conv_max_ctas(0)
     assert got.shape == want.shape
     assert np.array_equal(got, want)
 

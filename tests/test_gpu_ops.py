@@ -120,21 +120,44 @@ def test_accumulator_extremes(ufb, ora, dev, kernel, sign, ci):
         assert np.array_equal(N(got), ora.conv2d(x, w, b, 1, kernel // 2))
 
 
-def test_unsigned_low_byte_bound(ufb, ora, dev):
-    # low bytes 255 everywhere (value = 255 + 256 * hi) stress the u8 x u8 accumulator
-    ci = 3584  # K = 3584 * 9 = 32256 <= 32768, the exactness bound
+@pytest.mark.parametrize("ci,kernel", [(910, 3), (8192, 1)])
+def test_unsigned_low_byte_bound(ufb, ora, dev, ci, kernel):
+    # low bytes 255 everywhere (value = 255 + 256 * hi) stress the u8 x u8
+    # accumulator at the tensor-core path's longest reduction (K <= 8192)
     x = np.full((1, ci, 3, 3), 255, np.int16)
-    w = np.full((16, ci, 3, 3), 255, np.int16)
-    got = ufb.conv2d(T(x, dev), T(w, dev), None, 1, 1, 1, 1)
-    assert np.array_equal(N(got), ora.conv2d(x, w, None, 1, 1))
+    w = np.full((16, ci, kernel, kernel), 255, np.int16)
+    x.reshape(-1)[::7] = -32768
+    got = ufb.conv2d(T(x, dev), T(w, dev), None, 1, 1, kernel // 2, kernel // 2)
+    assert np.array_equal(N(got), ora.conv2d(x, w, None, 1, kernel // 2))
 
 
 def test_large_reduction_uses_direct_path(ufb, ora, dev):
     rng = np.random.default_rng(5)
-    x = rng.integers(-32768, 32768, (1, 4000, 3, 3)).astype(np.int16)  # 36000 > 32768
+    x = rng.integers(-32768, 32768, (1, 4000, 3, 3)).astype(np.int16)  # 36000 > 8192
     w = rng.integers(-32768, 32768, (4, 4000, 3, 3)).astype(np.int16)
     got = ufb.conv2d(T(x, dev), T(w, dev), None, 1, 1, 1, 1)
     assert np.array_equal(N(got), ora.conv2d(x, w, None, 1, 1))
+
+
+@pytest.mark.parametrize("ctas", [0, 3])
+@pytest.mark.parametrize("kernel", [1, 3])
+def test_conv_many_tiles(ufb, ora, dev, kernel, ctas):
+    """Hundreds of output tiles per launch, so every CTA alternates between the
+    two TMEM accumulator sets; about 1 in 8192 outputs is an exact rounding
+    tie, so both tie signs occur many times."""
+    rng = np.random.default_rng(11 + kernel)
+    hw = (160, 128) if kernel == 1 else (48, 40)
+    ci = 128 if kernel == 1 else 64
+    x = rng.integers(-32768, 32768, (2, ci) + hw).astype(np.int16)
+    w = rng.integers(-32768, 32768, (192, ci, kernel, kernel)).astype(np.int16)
+    b = rng.integers(-32768, 32768, (192,)).astype(np.int16)
+    ufb.set_conv_max_ctas(ctas)
+    try:
+        got = ufb.conv2d(T(x, dev), T(w, dev), T(b, dev), 1, 1, kernel // 2, kernel // 2)
+    finally:
+        ufb.set_conv_max_ctas(0)
+    assert np.array_equal(N(got), ora.conv2d(x, w, b, 1, kernel // 2))
+    _status_clean(ufb)
 
 
 def test_depthwise_and_stride2(ufb, ora, dev):
