@@ -32,6 +32,14 @@ __host__ __device__ __forceinline__ int32_t stage_bias(long long b) {
     return static_cast<int32_t>(b < -kMax ? -kMax : (b > kMax ? kMax : b));
 }
 
+// (sat16(lo) | sat16(hi) << 16): two saturating narrowings and the packing in
+// one instruction (PTX cvt.pack.sat puts its first source in the upper half).
+__device__ __forceinline__ uint32_t pack2_sat(int32_t lo, int32_t hi) {
+    uint32_t d;
+    asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(d) : "r"(hi), "r"(lo));
+    return d;
+}
+
 __device__ __forceinline__ uint32_t pack2(int32_t a, int32_t b) {
     return __byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x5410);
 }

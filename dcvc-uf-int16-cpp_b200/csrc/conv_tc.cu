@@ -51,9 +51,12 @@ namespace {
 constexpr int kBM = 128;                                    // output pixels per tile
 constexpr int kBN = 128;                                    // output channels per tile
 constexpr int kBK = 128;                                    // input channels per K block
-constexpr int kEpiWarps = 16;                               // four per TMEM lane quarter
+// Eight epilogue warps, two per TMEM lane quarter, 64 accumulator columns
+// each: with ten warps per CTA (at most three per SM sub-partition) a thread
+// may hold 168 registers, enough for two drained 64-column slices.
+constexpr int kEpiWarps = 8;
 constexpr int kFirstEpiWarp = 2;
-constexpr int kThreads = (kFirstEpiWarp + kEpiWarps) * 32;  // 576
+constexpr int kThreads = (kFirstEpiWarp + kEpiWarps) * 32;  // 320
 constexpr uint32_t kABytes = kBM * kBK;                     // one activation plane tile
 constexpr uint32_t kBBytes = 2 * kBN * kBK;                 // stacked low / high weight rows
 constexpr uint32_t kStageBytes = 2 * kABytes + kBBytes;     // 64 KB
@@ -134,6 +137,41 @@ __device__ __forceinline__ void store_shuffle2(const Act& out, const uint32_t (&
     }
 }
 
+// v = sat(v + res) for 16 packed outputs of one pixel at a ragged channel tail
+// (n_valid < 16 channels are real; src/layers.cpp:98-104).
+__device__ __forceinline__ void add_one_residual(const Act& res, uint32_t (&p)[8], int cbase, int n_valid,
+                                                 long long rp) {
+    uint32_t wl[4] = {0, 0, 0, 0}, wh[4] = {0, 0, 0, 0};
+    for (int j = 0; j < n_valid; ++j) {
+        wl[j >> 2] |= static_cast<uint32_t>(res.lo(rp)[cbase + j]) << (8 * (j & 3));
+        wh[j >> 2] |= static_cast<uint32_t>(res.hi(rp)[cbase + j]) << (8 * (j & 3));
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        uint32_t q0, q1;
+        join_bytes(wl[k], wh[k], q0, q1);
+        p[2 * k] = pack2_sat(lo16(p[2 * k]) + lo16(q0), hi16(p[2 * k]) + hi16(q0));
+        p[2 * k + 1] = pack2_sat(lo16(p[2 * k + 1]) + lo16(q1), hi16(p[2 * k + 1]) + hi16(q1));
+    }
+}
+
+// L2 prefetch of both planes of a tile's residual rows.
+template <bool SPATIAL>
+__device__ __forceinline__ void prefetch_residuals(const CUtensorMap* m1, const CUtensorMap* m2, const ConvTcArgs& a,
+                                                   int tile) {
+    const TileCoord tc = tile_coord<SPATIAL>(a, tile);
+#pragma unroll
+    for (int plane = 0; plane < 2; ++plane) {
+        if (SPATIAL) {
+            tma_prefetch_5d(m1, tc.co0, plane, tc.x0, tc.y0, tc.img);
+            if (a.epi.res2.base) tma_prefetch_5d(m2, tc.co0, plane, tc.x0, tc.y0, tc.img);
+        } else {
+            tma_prefetch_3d(m1, tc.co0, plane, static_cast<int>(tc.p0));
+            if (a.epi.res2.base) tma_prefetch_3d(m2, tc.co0, plane, static_cast<int>(tc.p0));
+        }
+    }
+}
+
 // Hands the drained accumulator columns back to the MMA warp.
 __device__ __forceinline__ void release_tmem(uint64_t* bar, int lane) {
     tc_fence_before();
@@ -171,7 +209,8 @@ __device__ __forceinline__ void tma_store_tile(const CUtensorMap* map, const voi
 template <bool SPATIAL, int MODE, int SIGNED>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-                   const __grid_constant__ CUtensorMap mapOut, const ConvTcArgs args) {
+                   const __grid_constant__ CUtensorMap mapOut, const __grid_constant__ CUtensorMap mapRes1,
+                   const __grid_constant__ CUtensorMap mapRes2, const ConvTcArgs args) {
     constexpr int STORE = MODE == kEpiShuffle2 ? kStoreThreads : (MODE == kEpiWsilu4 ? kStoreTmaQuarter : kStoreTma);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -312,41 +351,55 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         }
         __syncwarp();
     } else if (warp >= kFirstEpiWarp) {
+        constexpr int kCols = kBN / (kEpiWarps / 4);  // accumulator columns (output channels) per thread
+        constexpr int kWords = kCols / 2;              // packed int16 pairs per thread
+        constexpr int kLd = kCols / 32;                // 32-column TMEM loads per slice
         const int quarter = warp & 3;
-        const int cgroup = (warp - kFirstEpiWarp) >> 2;  // accumulator columns [32 cgroup, 32 cgroup + 32)
+        const int cgroup = (warp - kFirstEpiWarp) >> 2;  // columns [kCols cgroup, kCols cgroup + kCols)
         const int row = quarter * 32 + lane;            // TMEM lane = pixel of the tile
-        const uint32_t acc = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + cgroup * 32;  // + set offset
+        const uint32_t acc = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + cgroup * kCols;  // + set offset
         const bool issuer = warp == kFirstEpiWarp && lane == 0;
         const Act& out = args.out;
         uint32_t sync_phase = 0;
         int ti = 0;
+        if (MODE == kEpiRes && issuer && blockIdx.x < args.total_tiles)
+            prefetch_residuals<SPATIAL>(&mapRes1, &mapRes2, args, blockIdx.x);
         for (int tile = blockIdx.x; tile < args.total_tiles; tile += gridDim.x, ++ti) {
+            // residual rows of this CTA's next tile into L2 while this one finishes
+            if (MODE == kEpiRes && issuer && tile + static_cast<int>(gridDim.x) < args.total_tiles)
+                prefetch_residuals<SPATIAL>(&mapRes1, &mapRes2, args, tile + gridDim.x);
             if (!mbar_wait(&tmem_full, ti & 1, args.status, 4)) break;
             tc_fence_after();
             const TileCoord tc = tile_coord<SPATIAL>(args, tile);
-            const int cbase = tc.co0 + cgroup * 32;
+            const int cbase = tc.co0 + cgroup * kCols;
             const int4* bq = reinterpret_cast<const int4*>(bias_s + cbase);
-            uint32_t p[16];
+            uint32_t p[kWords];
             if ((ti & 1) == 0) {
-                // set at [0, 384); the next tile's set [128, 512) overlaps X and HH
-                const uint32_t a = acc;
-                uint32_t xx[32], hh[32];
-                tmem_ld32(a + kBN, xx);
-                tmem_ld32(a + 2 * kBN, hh);
-                tmem_wait_ld();
-                release_tmem(&tmem_empty, lane);
-                // V = 8 HH + (X >> 5); X & 31 kept as 5-bit fields, six per word
-                int32_t V[32];
-                uint32_t F[6] = {0, 0, 0, 0, 0, 0};
+                // set at [0, 384); the next tile's set [128, 512) overlaps X and HH.
+                // Drain them 32 columns at a time, folding each pair into
+                // V = 8 HH + (X >> 5) and 5-bit fields X & 31 (six per word).
+                int32_t V[kCols];
+                uint32_t F[(kCols + 5) / 6];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    V[j] = static_cast<int32_t>(hh[j]) * 8 + (static_cast<int32_t>(xx[j]) >> 5);
-                    F[j / 6] |= (xx[j] & 31u) << (5 * (j % 6));
+                for (int i = 0; i < (kCols + 5) / 6; ++i) F[i] = 0;
+#pragma unroll
+                for (int i = 0; i < kLd; ++i) {
+                    uint32_t xx[32], hh[32];
+                    tmem_ld32(acc + kBN + 32 * i, xx);
+                    tmem_ld32(acc + 2 * kBN + 32 * i, hh);
+                    tmem_wait_ld();
+                    if (i == kLd - 1) release_tmem(&tmem_empty, lane);
+#pragma unroll
+                    for (int t = 0; t < 32; ++t) {
+                        const int j = 32 * i + t;
+                        V[j] = static_cast<int32_t>(hh[t]) * 8 + (static_cast<int32_t>(xx[t]) >> 5);
+                        F[j / 6] |= (xx[t] & 31u) << (5 * (j % 6));
+                    }
                 }
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < kCols / 16; ++h) {
                     uint32_t ll[16];
-                    tmem_ld16(a + 16 * h, ll);  // LL stays clear of the next tile's set
+                    tmem_ld16(acc + 16 * h, ll);  // LL stays clear of the next tile's set
                     tmem_wait_ld();
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
@@ -357,32 +410,37 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         for (int t = 0; t < 4; ++t) {
                             const int j = 16 * h + 4 * q + t;
                             const int32_t f = static_cast<int32_t>((F[j / 6] >> (5 * (j % 6))) & 31u);
-                            r[t] = clamp16(finish_rna(V[j], static_cast<int32_t>(ll[4 * q + t]) + (f << 8) + 4096) + bb[t]);
+                            r[t] = finish_rna(V[j], static_cast<int32_t>(ll[4 * q + t]) + (f << 8) + 4096) + bb[t];
                         }
-                        p[8 * h + 2 * q] = pack2(r[0], r[1]);
-                        p[8 * h + 2 * q + 1] = pack2(r[2], r[3]);
+                        p[8 * h + 2 * q] = pack2_sat(r[0], r[1]);
+                        p[8 * h + 2 * q + 1] = pack2_sat(r[2], r[3]);
                     }
                 }
             } else {
-                // set at [128, 512); the next tile's set [0, 384) overlaps LL and X
+                // set at [128, 512); the next tile's set [0, 384) overlaps LL and X.
+                // Drain them 32 columns at a time into U = LL + 256 (X & 31) + 4096,
+                // W = (X >> 5) + (U >> 13) and a tie bit (U % 8192 == 0).
                 const uint32_t a = acc + kBN;
-                uint32_t ll[32], xx[32];
-                tmem_ld32(a, ll);
-                tmem_ld32(a + kBN, xx);
-                tmem_wait_ld();
-                release_tmem(&tmem_empty, lane);
-                // U = LL + 256 (X & 31) + 4096, W = (X >> 5) + (U >> 13), tie bit (U % 8192 == 0)
-                int32_t W[32];
-                uint32_t ties = 0;
+                int32_t W[kCols];
+                uint32_t ties[kLd];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int32_t x = static_cast<int32_t>(xx[j]);
-                    const int32_t U = static_cast<int32_t>(ll[j]) + ((x & 31) << 8) + 4096;
-                    W[j] = (x >> 5) + (U >> 13);
-                    ties |= static_cast<uint32_t>((U & 8191) == 0) << j;
+                for (int i = 0; i < kLd; ++i) {
+                    uint32_t ll[32], xx[32];
+                    tmem_ld32(a + 32 * i, ll);
+                    tmem_ld32(a + kBN + 32 * i, xx);
+                    tmem_wait_ld();
+                    if (i == kLd - 1) release_tmem(&tmem_empty, lane);
+                    ties[i] = 0;
+#pragma unroll
+                    for (int t = 0; t < 32; ++t) {
+                        const int32_t x = static_cast<int32_t>(xx[t]);
+                        const int32_t U = static_cast<int32_t>(ll[t]) + ((x & 31) << 8) + 4096;
+                        W[32 * i + t] = (x >> 5) + (U >> 13);
+                        ties[i] |= static_cast<uint32_t>((U & 8191) == 0) << t;
+                    }
                 }
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < kCols / 16; ++h) {
                     uint32_t hh[16];
                     tmem_ld16(a + 2 * kBN + 16 * h, hh);  // HH stays clear of the next tile's set
                     tmem_wait_ld();
@@ -395,13 +453,14 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         for (int t = 0; t < 4; ++t) {
                             const int j = 16 * h + 4 * q + t;
                             const int32_t T = static_cast<int32_t>(hh[4 * q + t]) * 8 + W[j];
-                            r[t] = clamp16(T - static_cast<int32_t>(((ties >> j) & 1u) & (T <= 0)) + bb[t]);
+                            r[t] = T - static_cast<int32_t>(((ties[j / 32] >> (j % 32)) & 1u) & (T <= 0)) + bb[t];
                         }
-                        p[8 * h + 2 * q] = pack2(r[0], r[1]);
-                        p[8 * h + 2 * q + 1] = pack2(r[2], r[3]);
+                        p[8 * h + 2 * q] = pack2_sat(r[0], r[1]);
+                        p[8 * h + 2 * q + 1] = pack2_sat(r[2], r[3]);
                     }
                 }
             }
+            const int n_valid = args.co - cbase < 0 ? 0 : (args.co - cbase < kCols ? args.co - cbase : kCols);
             bool valid;
             long long rpx1 = 0, rpx2 = 0;
             int oy = 0, ox = 0;
@@ -418,11 +477,10 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                 rpx1 = rpx2 = tc.p0 + row;
                 valid = rpx1 < args.m_total;
             }
-            const int n_valid = args.co - cbase < 0 ? 0 : (args.co - cbase < 32 ? args.co - cbase : 32);
             if (STORE == kStoreThreads) {
                 if (valid) {
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
+                    for (int h = 0; h < kCols / 16; ++h) {
                         if (16 * h >= n_valid) break;
                         uint32_t p8[8];
 #pragma unroll
@@ -436,44 +494,69 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
             // fused elementwise step (residual rows outside the image read nothing)
             if (MODE == kEpiLut) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) p[i] = pack2(lut(lo16(p[i])), lut(hi16(p[i])));
+                for (int i = 0; i < kWords; ++i) p[i] = pack2(lut(lo16(p[i])), lut(hi16(p[i])));
             }
             if (MODE == kEpiRes && valid) {
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    if (16 * h >= n_valid) break;
-                    uint32_t p8[8];
+                for (int r = 0; r < 2; ++r) {
+                    const Act& res = r == 0 ? args.epi.res1 : args.epi.res2;
+                    if (r == 1 && !res.base) break;
+                    const long long rp = r == 0 ? rpx1 : rpx2;
+                    if (n_valid == kCols) {
+                        // all loads of the pixel's channels first, then the adds
+                        uint4 rl[kCols / 16], rh[kCols / 16];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) p8[i] = p[8 * h + i];
-                    add_residuals(args.epi, p8, cbase + 16 * h, n_valid - 16 * h < 16 ? n_valid - 16 * h : 16, rpx1,
-                                  rpx2);
+                        for (int h = 0; h < kCols / 16; ++h) {
+                            rl[h] = reinterpret_cast<const uint4*>(res.lo(rp) + cbase)[h];
+                            rh[h] = reinterpret_cast<const uint4*>(res.hi(rp) + cbase)[h];
+                        }
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) p[8 * h + i] = p8[i];
+                        for (int h = 0; h < kCols / 16; ++h) {
+                            const uint32_t lw[4] = {rl[h].x, rl[h].y, rl[h].z, rl[h].w};
+                            const uint32_t hw[4] = {rh[h].x, rh[h].y, rh[h].z, rh[h].w};
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                uint32_t q0, q1;
+                                join_bytes(lw[k], hw[k], q0, q1);
+                                uint32_t& a0 = p[8 * h + 2 * k];
+                                uint32_t& a1 = p[8 * h + 2 * k + 1];
+                                a0 = pack2_sat(lo16(a0) + lo16(q0), hi16(a0) + hi16(q0));
+                                a1 = pack2_sat(lo16(a1) + lo16(q1), hi16(a1) + hi16(q1));
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int h = 0; h < kCols / 16; ++h) {
+                            if (16 * h >= n_valid) break;
+                            uint32_t p8[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) p8[i] = p[8 * h + i];
+                            add_one_residual(res, p8, cbase + 16 * h, n_valid - 16 * h < 16 ? n_valid - 16 * h : 16,
+                                             rp);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) p[8 * h + i] = p8[i];
+                        }
+                    }
                 }
             }
             if (STORE == kStoreTma) {
                 // one byte plane at a time through the 128-byte-swizzled stage:
                 // row r holds the tile's 128 channels of pixel r, 16-byte chunk c
                 // at position c ^ (r & 7)
-                uint4 lo[2], hi[2];
-                uint32_t p8a[8], p8b[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    p8a[i] = p[i];
-                    p8b[i] = p[8 + i];
-                }
-                split_bytes(p8a, lo[0], hi[0]);
-                split_bytes(p8b, lo[1], hi[1]);
                 bool ok = true;
 #pragma unroll
                 for (int plane = 0; plane < 2; ++plane) {
                     ok = ok && epi_sync(&epi_bar, sync_phase, lane, args.status);  // stage is free
                     if (!ok) break;
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int chunk = cgroup * 2 + h;
-                        *reinterpret_cast<uint4*>(staging + row * 128 + ((chunk ^ (row & 7)) << 4)) =
-                            plane ? hi[h] : lo[h];
+                    for (int h = 0; h < kCols / 16; ++h) {
+                        uint32_t p8[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) p8[i] = p[8 * h + i];
+                        uint4 lo, hi;
+                        split_bytes(p8, lo, hi);
+                        const int chunk = cgroup * (kCols / 16) + h;
+                        *reinterpret_cast<uint4*>(staging + row * 128 + ((chunk ^ (row & 7)) << 4)) = plane ? hi : lo;
                     }
                     fence_proxy_async_smem();
                     ok = epi_sync(&epi_bar, sync_phase, lane, args.status);
@@ -486,20 +569,22 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                 }
                 if (!ok) break;
             } else {
-                // wsilu4: 8 output channels per thread, both planes staged at once
-                // as [plane][pixel][32 channels] (unswizzled, 32-byte rows)
-                int32_t r[8];
-#pragma unroll
-                for (int g = 0; g < 8; ++g)
-                    r[g] = clamp16(lut(lo16(p[2 * g])) + lut(hi16(p[2 * g])) + lut(lo16(p[2 * g + 1])) +
-                                   lut(hi16(p[2 * g + 1])));
-                const uint32_t w0 = pack2(r[0], r[1]), w1 = pack2(r[2], r[3]), w2 = pack2(r[4], r[5]),
-                               w3 = pack2(r[6], r[7]);
-                const uint2 lo = make_uint2(__byte_perm(w0, w1, 0x6420), __byte_perm(w2, w3, 0x6420));
-                const uint2 hi = make_uint2(__byte_perm(w0, w1, 0x7531), __byte_perm(w2, w3, 0x7531));
+                // wsilu4: kCols / 4 output channels per thread, both planes staged at
+                // once as [plane][pixel][32 channels] (unswizzled, 32-byte rows)
                 if (!epi_sync(&epi_bar, sync_phase, lane, args.status)) break;
-                *reinterpret_cast<uint2*>(staging + row * 32 + cgroup * 8) = lo;
-                *reinterpret_cast<uint2*>(staging + kBM * 32 + row * 32 + cgroup * 8) = hi;
+#pragma unroll
+                for (int h = 0; h < kCols / 16; ++h) {
+                    int32_t r[4];
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        const uint32_t a0 = p[8 * h + 2 * g], a1 = p[8 * h + 2 * g + 1];
+                        r[g] = clamp16(lut(lo16(a0)) + lut(hi16(a0)) + lut(lo16(a1)) + lut(hi16(a1)));
+                    }
+                    const uint32_t w0 = pack2(r[0], r[1]), w1 = pack2(r[2], r[3]);
+                    const int c4 = cgroup * (kCols / 4) + 4 * h;  // first wsilu4 channel of the group
+                    *reinterpret_cast<uint32_t*>(staging + row * 32 + c4) = __byte_perm(w0, w1, 0x6420);
+                    *reinterpret_cast<uint32_t*>(staging + kBM * 32 + row * 32 + c4) = __byte_perm(w0, w1, 0x7531);
+                }
                 fence_proxy_async_smem();
                 if (!epi_sync(&epi_bar, sync_phase, lane, args.status)) break;
                 if (issuer) {
@@ -613,9 +698,12 @@ int sm_count(int device) {
     return g_sms[device] > 0 ? g_sms[device] : 148;
 }
 
+struct ConvMaps {
+    CUtensorMap a, b, out, res1, res2;
+};
+
 template <bool SPATIAL, int MODE, int SIGNED>
-cudaError_t launch_mode(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const ConvTcArgs& args,
-                        size_t smem, int sms, cudaStream_t stream) {
+cudaError_t launch_mode(const ConvMaps& m, const ConvTcArgs& args, size_t smem, int sms, cudaStream_t stream) {
     auto kernel = conv_i16_tc_kernel<SPATIAL, MODE, SIGNED>;
     // the attribute is per function and device; setting it each launch is cheap
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -623,26 +711,43 @@ cudaError_t launch_mode(const CUtensorMap& a, const CUtensorMap& b, const CUtens
     int grid = args.total_tiles < sms ? args.total_tiles : sms;
     const int cap = g_max_ctas.load(std::memory_order_relaxed);
     if (cap > 0 && grid > cap) grid = cap;
-    kernel<<<grid, kThreads, smem, stream>>>(a, b, o, args);
+    kernel<<<grid, kThreads, smem, stream>>>(m.a, m.b, m.out, m.res1, m.res2, args);
     return cudaGetLastError();
 }
 
 template <bool SPATIAL, int SIGNED>
-cudaError_t launch_signed(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const ConvTcArgs& args,
-                          size_t smem, int sms, cudaStream_t stream) {
+cudaError_t launch_signed(const ConvMaps& m, const ConvTcArgs& args, size_t smem, int sms, cudaStream_t stream) {
     const Epilogue& e = args.epi;
-    if (e.shuffle2) return launch_mode<SPATIAL, kEpiShuffle2, SIGNED>(a, b, o, args, smem, sms, stream);
-    if (e.wsilu4) return launch_mode<SPATIAL, kEpiWsilu4, SIGNED>(a, b, o, args, smem, sms, stream);
-    if (e.lut) return launch_mode<SPATIAL, kEpiLut, SIGNED>(a, b, o, args, smem, sms, stream);
-    if (e.res1.base) return launch_mode<SPATIAL, kEpiRes, SIGNED>(a, b, o, args, smem, sms, stream);
-    return launch_mode<SPATIAL, kEpiPlain, SIGNED>(a, b, o, args, smem, sms, stream);
+    if (e.shuffle2) return launch_mode<SPATIAL, kEpiShuffle2, SIGNED>(m, args, smem, sms, stream);
+    if (e.wsilu4) return launch_mode<SPATIAL, kEpiWsilu4, SIGNED>(m, args, smem, sms, stream);
+    if (e.lut) return launch_mode<SPATIAL, kEpiLut, SIGNED>(m, args, smem, sms, stream);
+    if (e.res1.base) return launch_mode<SPATIAL, kEpiRes, SIGNED>(m, args, smem, sms, stream);
+    return launch_mode<SPATIAL, kEpiPlain, SIGNED>(m, args, smem, sms, stream);
 }
 
 template <bool SPATIAL>
-cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const ConvTcArgs& args,
-                   size_t smem, int sms, cudaStream_t stream) {
-    return args.signed_split ? launch_signed<SPATIAL, 1>(a, b, o, args, smem, sms, stream)
-                             : launch_signed<SPATIAL, 0>(a, b, o, args, smem, sms, stream);
+cudaError_t launch(const ConvMaps& m, const ConvTcArgs& args, size_t smem, int sms, cudaStream_t stream) {
+    return args.signed_split ? launch_signed<SPATIAL, 1>(m, args, smem, sms, stream)
+                             : launch_signed<SPATIAL, 0>(m, args, smem, sms, stream);
+}
+
+// Tensor map of a split-NHWC view in tile order: flat {c, plane, pixels} or
+// spatial {c, plane, w, h, n}, box of `box_c` channels of one plane.
+bool act_map(CUtensorMap* map, const Act& v, bool flat, int tw, int th, cuuint32_t box_c,
+             CUtensorMapSwizzle swizzle, std::string& err) {
+    if (flat) {
+        const cuuint64_t dims[3] = {static_cast<cuuint64_t>(v.c), 2, static_cast<cuuint64_t>(v.pixels())};
+        const cuuint64_t strides[2] = {static_cast<cuuint64_t>(v.pitch), static_cast<cuuint64_t>(2 * v.pitch)};
+        const cuuint32_t box[3] = {box_c, 1, kBM};
+        return encode(map, v.base, 3, dims, strides, box, err, swizzle);
+    }
+    const cuuint64_t dims[5] = {static_cast<cuuint64_t>(v.c), 2, static_cast<cuuint64_t>(v.w),
+                                static_cast<cuuint64_t>(v.h), static_cast<cuuint64_t>(v.n)};
+    const cuuint64_t strides[4] = {static_cast<cuuint64_t>(v.pitch), static_cast<cuuint64_t>(2 * v.pitch),
+                                   static_cast<cuuint64_t>(2 * v.pitch) * v.row_px,
+                                   static_cast<cuuint64_t>(2 * v.pitch) * v.img_px};
+    const cuuint32_t box[5] = {box_c, 1, static_cast<cuuint32_t>(tw), static_cast<cuuint32_t>(th), 1};
+    return encode(map, v.base, 5, dims, strides, box, err, swizzle);
 }
 
 }  // namespace
@@ -789,47 +894,34 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     // (wsilu4, unswizzled); the map's extent is the view's, so tails are clipped
     const cuuint32_t out_box_c = epi.wsilu4 ? kBN / 4 : kBN;
     const CUtensorMapSwizzle out_swizzle = epi.wsilu4 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B;
-    CUtensorMap amap, omap;
+    ConvMaps maps{};
+    maps.b = w.map;
     long long m_tiles;
+    int tw = 0, th = 0;
     if (flat) {
-        const cuuint64_t dims[3] = {static_cast<cuuint64_t>(in.c), 2, static_cast<cuuint64_t>(in.pixels())};
-        const cuuint64_t strides[2] = {static_cast<cuuint64_t>(in.pitch), static_cast<cuuint64_t>(2 * in.pitch)};
-        const cuuint32_t box[3] = {kBK, 1, kBM};
-        if (!encode(&amap, in.base, 3, dims, strides, box, err)) return -1;
-        const cuuint64_t odims[3] = {static_cast<cuuint64_t>(out.c), 2, static_cast<cuuint64_t>(out.pixels())};
-        const cuuint64_t ostrides[2] = {static_cast<cuuint64_t>(out.pitch), static_cast<cuuint64_t>(2 * out.pitch)};
-        const cuuint32_t obox[3] = {out_box_c, 1, kBM};
-        if (!encode(&omap, out.base, 3, odims, ostrides, obox, err, out_swizzle)) return -1;
         args.m_total = in.pixels();
         m_tiles = (in.pixels() + kBM - 1) / kBM;
     } else {
-        const int tw = ow >= 12 ? 16 : 8;
-        const int th = kBM / tw;
+        tw = ow >= 12 ? 16 : 8;
+        th = kBM / tw;
         args.tile_w = tw;
         args.tile_h = th;
         args.tiles_x = (ow + tw - 1) / tw;
         args.tiles_y = (oh + th - 1) / th;
-        const cuuint64_t dims[5] = {static_cast<cuuint64_t>(in.c), 2, static_cast<cuuint64_t>(in.w),
-                                    static_cast<cuuint64_t>(in.h), static_cast<cuuint64_t>(in.n)};
-        const cuuint64_t strides[4] = {static_cast<cuuint64_t>(in.pitch), static_cast<cuuint64_t>(2 * in.pitch),
-                                       static_cast<cuuint64_t>(2 * in.pitch) * in.row_px,
-                                       static_cast<cuuint64_t>(2 * in.pitch) * in.img_px};
-        const cuuint32_t box[5] = {kBK, 1, static_cast<cuuint32_t>(tw), static_cast<cuuint32_t>(th), 1};
-        if (!encode(&amap, in.base, 5, dims, strides, box, err)) return -1;
-        if (!epi.shuffle2) {
-            const cuuint64_t odims[5] = {static_cast<cuuint64_t>(out.c), 2, static_cast<cuuint64_t>(out.w),
-                                         static_cast<cuuint64_t>(out.h), static_cast<cuuint64_t>(out.n)};
-            const cuuint64_t ostrides[4] = {static_cast<cuuint64_t>(out.pitch),
-                                            static_cast<cuuint64_t>(2 * out.pitch),
-                                            static_cast<cuuint64_t>(2 * out.pitch) * out.row_px,
-                                            static_cast<cuuint64_t>(2 * out.pitch) * out.img_px};
-            const cuuint32_t obox[5] = {out_box_c, 1, static_cast<cuuint32_t>(tw), static_cast<cuuint32_t>(th), 1};
-            if (!encode(&omap, out.base, 5, odims, ostrides, obox, err, out_swizzle)) return -1;
-        } else {
-            omap = amap;  // unused: pixel-shuffled tiles are stored by the threads
-        }
         m_tiles = static_cast<long long>(args.tiles_x) * args.tiles_y * in.n;
     }
+    // the activation box is the tile's input window (shifted per tap in spatial mode)
+    if (!act_map(&maps.a, in, flat, tw, th, kBK, CU_TENSOR_MAP_SWIZZLE_128B, err)) return -1;
+    if (!epi.shuffle2) {
+        if (!act_map(&maps.out, out, flat, tw, th, out_box_c, out_swizzle, err)) return -1;
+    } else {
+        maps.out = maps.a;  // unused: pixel-shuffled tiles are stored by the threads
+    }
+    maps.res1 = maps.res2 = maps.a;  // unused unless residuals are fused
+    if (epi.res1.base && !act_map(&maps.res1, epi.res1, flat, tw, th, kBN, CU_TENSOR_MAP_SWIZZLE_NONE, err))
+        return -1;
+    if (epi.res2.base && !act_map(&maps.res2, epi.res2, flat, tw, th, kBN, CU_TENSOR_MAP_SWIZZLE_NONE, err))
+        return -1;
     const long long total = m_tiles * w.co_tiles;
     if (total > INT32_MAX) {
         err = "too many output tiles";
@@ -837,8 +929,8 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     }
     args.total_tiles = static_cast<int>(total);
     const int sms = sm_count(current_device());
-    const cudaError_t e = flat ? launch<false>(amap, w.map, omap, args, smem, sms, stream)
-                               : launch<true>(amap, w.map, omap, args, smem, sms, stream);
+    const cudaError_t e =
+        flat ? launch<false>(maps, args, smem, sms, stream) : launch<true>(maps, args, smem, sms, stream);
     if (e != cudaSuccess) {
         err = std::string("conv launch failed: ") + cudaGetErrorString(e);
         return -1;
