@@ -73,6 +73,23 @@ int conv_tc_path(const int16_t* x, int n, int ci, int h, int w, const int16_t* w
     return UFB_OK;
 }
 
+// Depthwise 3x3 (stride 1, padding 1): the split-layout depthwise kernel the
+// engine uses for DepthConvBlock dc.2, between two layout conversions.
+int conv_depthwise_path(const int16_t* x, int n, int c, int h, int w, const int16_t* weight, const void* bias,
+                        int16_t* out, cudaStream_t s) {
+    const int cp = round_up(c, 16);
+    StreamBuffer xs(static_cast<size_t>(n) * h * w * 2 * cp, s);
+    StreamBuffer os(static_cast<size_t>(n) * h * w * 2 * cp, s);
+    if (!xs.ok() || !os.ok()) return err(UFB_ECUDA, "cudaMallocAsync failed for convolution scratch");
+    const Act in = make_act(xs.get<uint8_t>(), n, h, w, c, cp);
+    const Act ov = make_act(os.get<uint8_t>(), n, h, w, c, cp);
+    if (!cuda_ok(nchw_to_split(x, n, c, h, w, 1, in, s), "input layout")) return last_code();
+    if (!cuda_ok(dwconv3x3(in, ov, weight, static_cast<const int16_t*>(bias), s), "depthwise convolution"))
+        return last_code();
+    if (!cuda_ok(split_to_nchw(ov, 1, out, s), "output layout")) return last_code();
+    return UFB_OK;
+}
+
 int conv_dispatch(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
                   const void* bias, int bias_bits, int sh, int sw, int ph, int pw, int groups, int16_t* out,
                   void* stream, bool allow_tc, bool allow_direct) {
@@ -82,6 +99,9 @@ int conv_dispatch(const int16_t* x, int n, int ci, int h, int w, const int16_t* 
     if (!check_conv(x, n, ci, h, w, weight, co, kh, kw, bias_bits, sh, sw, ph, pw, groups, out, oh, ow))
         return last_code();
     auto s = static_cast<cudaStream_t>(stream);
+    if (allow_tc && groups == ci && ci == co && ci % 4 == 0 && kh == 3 && kw == 3 && sh == 1 && sw == 1 && ph == 1 &&
+        pw == 1 && bias_bits != 32)
+        return conv_depthwise_path(x, n, ci, h, w, weight, bias_bits ? bias : nullptr, out, s);
     const bool tc_ok = allow_tc && groups == 1 && sh == 1 && sw == 1 && static_cast<long long>(ci) * kh * kw <= kTcMaxReduction;
     if (tc_ok) return conv_tc_path(x, n, ci, h, w, weight, co, kh, kw, bias, bias_bits, ph, pw, oh, ow, out, s);
     if (!allow_direct && !allow_tc) return err(UFB_EINVAL, "no convolution path");

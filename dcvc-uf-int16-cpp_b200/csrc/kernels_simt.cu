@@ -3,6 +3,7 @@
 // depthwise) convolution, the elementwise operators of the reference's CUDA
 // extension (src/cuda/elementwise.cu:16-46) and the fixed-point warp.
 #include "kernels.h"
+#include "conv_epi.cuh"
 #include "uf_common.cuh"
 
 #include <cuda_runtime.h>
@@ -94,83 +95,128 @@ __global__ void conv_direct_kernel(int16_t* __restrict__ out, const int16_t* __r
 
 // Depthwise 3x3, stride 1, zero padding 1 on split views (DepthConvBlock dc.2,
 // src/layers.cpp:96; the reference runs it through its scalar `general`
-// kernel, src/cuda/conv.cu:44-60).  A CTA stages an (8 + 2) x (32 + 2) pixel
-// tile of 64 channels (both byte planes) in shared memory once, then each
-// thread produces 8 channels of 8 output pixels.  Accumulation stays in int32
-// by keeping the planes apart: S_lo = sum lo * w and S_hi = sum hi * w
-// (|S| < 2^27 for 9 taps), and the exact rna(S_lo + 256 S_hi, 8192) is formed
-// without 64-bit arithmetic.
-constexpr int kDwTileW = 32, kDwTileH = 8, kDwC = 64, kDwThreads = 256;
-constexpr int kDwInW = kDwTileW + 2, kDwInH = kDwTileH + 2;
+// kernel, src/cuda/conv.cu:44-60).  A thread owns four channels (one 32-bit
+// word of each byte plane) of kDwCols adjacent output columns and slides down a
+// strip of rows: each input row is read once per thread (warp-coalesced
+// 128-byte rows; neighbouring columns meet again in L1), split into bytes and
+// multiplied into the three output rows it feeds, with the 36 weights held in
+// registers.  Accumulation stays in int32 by keeping the planes apart:
+// S_lo = sum lo * w and S_hi = sum hi * w (|S| < 2^27 for 9 taps), combined
+// exactly by the 32-bit rna recombination of the tensor-core epilogue.
+constexpr int kDwQuads = 32;     // channel quads per block (128 channels)
+constexpr int kDwColThreads = 8; // threads along x per block
+constexpr int kDwRows = 16;      // output rows per strip
+constexpr int kDwThreads = kDwQuads * kDwColThreads;  // 256
+constexpr int kDwCols = 2;       // output columns per thread (two blocks per SM: the best measured layout)
 
-__device__ __forceinline__ int32_t rna8192_split(int32_t s_lo, int32_t s_hi) {
-    const int32_t R = ((s_hi & 31) << 8) + (s_lo & 8191);
-    const int32_t T = (s_hi >> 5) + (s_lo >> 13) + (R >> 13);
-    const int32_t Rl = R & 8191;
-    return T + ((Rl > 4096) | ((Rl == 4096) & (T >= 0)));
+struct DwAcc {
+    int32_t lo[kDwCols][4], hi[kDwCols][4];  // [column][channel]
+};
+
+__device__ __forceinline__ void dw_zero(DwAcc& a) {
+#pragma unroll
+    for (int j = 0; j < kDwCols; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) a.lo[j][c] = a.hi[j][c] = 0;
 }
 
-__global__ void __launch_bounds__(kDwThreads) dwconv3x3_kernel(Act in, Act out, const int16_t* __restrict__ weight,
-                                                               const int16_t* __restrict__ bias) {
-    __shared__ __align__(16) uint8_t tile[kDwInH * kDwInW][2 * kDwC];  // [pixel][lo 64 | hi 64]
-    __shared__ int32_t wsm[9][kDwC];
-    __shared__ int32_t bsm[kDwC];
-    const int x0 = blockIdx.x * kDwTileW, y0 = blockIdx.y * kDwTileH;
-    const int cgroups = (in.c + kDwC - 1) / kDwC;
-    const int b = blockIdx.z / cgroups, c0 = (blockIdx.z - b * cgroups) * kDwC;
-    const int cn = in.c - c0 < kDwC ? in.c - c0 : kDwC;  // channels in this group (multiple of 8)
-    for (int i = threadIdx.x; i < 9 * kDwC; i += kDwThreads) {
-        const int t = i / kDwC, c = i - t * kDwC;
-        wsm[t][c] = c < cn ? weight[(c0 + c) * 9 + t] : 0;
-    }
-    for (int c = threadIdx.x; c < kDwC; c += kDwThreads) bsm[c] = (bias && c < cn) ? bias[c0 + c] : 0;
-    // stage the input tile: 16-byte chunks, 4 per plane per pixel
-    for (int i = threadIdx.x; i < kDwInH * kDwInW * 8; i += kDwThreads) {
-        const int chunk = i & 7, p = i >> 3;
-        const int ty = p / kDwInW, tx = p - ty * kDwInW;
-        const int iy = y0 + ty - 1, ix = x0 + tx - 1;
-        const int plane = chunk >> 2, cc = (chunk & 3) * 16;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (iy >= 0 && iy < in.h && ix >= 0 && ix < in.w && cc < cn) {
-            const long long px = in.pixel(b, iy, ix);
-            v = *reinterpret_cast<const uint4*>((plane ? in.hi(px) : in.lo(px)) + c0 + cc);
-        }
-        *reinterpret_cast<uint4*>(&tile[p][plane * kDwC + cc]) = v;
-    }
-    __syncthreads();
-    const int g = threadIdx.x & 7;  // channel group of 8
-    if (g * 8 >= cn) return;
-    for (int item = threadIdx.x >> 3; item < kDwTileH * kDwTileW; item += kDwThreads / 8) {
-        const int ty = item / kDwTileW, tx = item - ty * kDwTileW;
-        const int oy = y0 + ty, ox = x0 + tx;
-        if (oy >= in.h || ox >= in.w) continue;
-        int32_t slo[8] = {0, 0, 0, 0, 0, 0, 0, 0}, shi[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+// Adds one input row (pixels x0-1 .. x0+kDwCols as bytes l / h) into the
+// accumulator of an output row through weight row w[kx][channel].
+__device__ __forceinline__ void dw_add(DwAcc& a, const int32_t (&l)[kDwCols + 2][4],
+                                       const int32_t (&h)[kDwCols + 2][4], const int32_t (&w)[3][4]) {
 #pragma unroll
-        for (int ky = 0; ky < 3; ++ky)
+    for (int j = 0; j < kDwCols; ++j)
 #pragma unroll
-            for (int kx = 0; kx < 3; ++kx) {
-                const uint8_t* src = tile[(ty + ky) * kDwInW + tx + kx];
-                const uint2 lo = *reinterpret_cast<const uint2*>(src + g * 8);
-                const uint2 hi = *reinterpret_cast<const uint2*>(src + kDwC + g * 8);
-                const uint8_t* l = reinterpret_cast<const uint8_t*>(&lo);
-                const int8_t* h = reinterpret_cast<const int8_t*>(&hi);
+        for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int32_t wv = wsm[ky * 3 + kx][g * 8 + j];
-                    slo[j] += static_cast<int32_t>(l[j]) * wv;
-                    shi[j] += static_cast<int32_t>(h[j]) * wv;
-                }
+            for (int c = 0; c < 4; ++c) {
+                a.lo[j][c] += l[j + kx][c] * w[kx][c];
+                a.hi[j][c] += h[j + kx][c] * w[kx][c];
             }
-        uint8_t ol[8], oh8[8];
+}
+
+__device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], const Act& out, int img, int oy,
+                                         int x0, int c0) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int16_t v = sat16i(rna8192_split(slo[j], shi[j]) + bsm[g * 8 + j]);
-            ol[j] = static_cast<uint8_t>(v & 0xff);
-            oh8[j] = static_cast<uint8_t>((v >> 8) & 0xff);
+    for (int j = 0; j < kDwCols; ++j) {
+        if (x0 + j >= out.w) break;
+        int32_t r[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int32_t U = a.lo[j][c] + ((a.hi[j][c] & 31) << 8) + 4096;
+            const int32_t T = (a.hi[j][c] >> 5) + (U >> 13);
+            r[c] = T - static_cast<int32_t>(((U & 8191) == 0) & (T <= 0)) + b[c];
         }
-        const long long opx = out.pixel(b, oy, ox);
-        *reinterpret_cast<uint2*>(out.lo(opx) + c0 + g * 8) = *reinterpret_cast<const uint2*>(ol);
-        *reinterpret_cast<uint2*>(out.hi(opx) + c0 + g * 8) = *reinterpret_cast<const uint2*>(oh8);
+        const uint32_t p0 = pack2_sat(r[0], r[1]), p1 = pack2_sat(r[2], r[3]);
+        const long long px = out.pixel(img, oy, x0 + j);
+        *reinterpret_cast<uint32_t*>(out.lo(px) + c0) = __byte_perm(p0, p1, 0x6420);
+        *reinterpret_cast<uint32_t*>(out.hi(px) + c0) = __byte_perm(p0, p1, 0x7531);
+    }
+}
+
+// Input row iy, pixels x0-1 .. x0+kDwCols, four channels: low bytes (u8) and
+// high bytes (s8) as int32; zero outside the image.
+__device__ __forceinline__ void dw_load_row(const Act& in, int img, int iy, int x0, int c0,
+                                            int32_t (&l)[kDwCols + 2][4], int32_t (&h)[kDwCols + 2][4]) {
+    const bool row_ok = iy >= 0 && iy < in.h;
+#pragma unroll
+    for (int p = 0; p < kDwCols + 2; ++p) {
+        const int x = x0 - 1 + p;
+        uint32_t lw = 0, hw = 0;
+        if (row_ok && x >= 0 && x < in.w) {
+            const long long px = in.pixel(img, iy, x);
+            lw = __ldg(reinterpret_cast<const uint32_t*>(in.lo(px) + c0));
+            hw = __ldg(reinterpret_cast<const uint32_t*>(in.hi(px) + c0));
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            l[p][c] = static_cast<int32_t>((lw >> (8 * c)) & 0xffu);
+            h[p][c] = static_cast<int32_t>(static_cast<int8_t>(hw >> (8 * c)));
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kDwThreads, 2)
+dwconv3x3_kernel(Act in, Act out, const int16_t* __restrict__ weight, const int16_t* __restrict__ bias, int ch_blocks,
+                 int col_blocks, int strips) {
+    int bid = blockIdx.x;
+    const int cb = bid % ch_blocks;
+    bid /= ch_blocks;
+    const int xb = bid % col_blocks;
+    bid /= col_blocks;
+    const int sb = bid % strips;
+    const int img = bid / strips;
+    const int c0 = cb * 4 * kDwQuads + 4 * (threadIdx.x % kDwQuads);
+    const int x0 = kDwCols * (xb * kDwColThreads + static_cast<int>(threadIdx.x / kDwQuads));
+    if (c0 >= in.c || x0 >= in.w) return;
+    const int y0 = sb * kDwRows, y1 = y0 + kDwRows < in.h ? y0 + kDwRows : in.h;
+    int32_t w[3][3][4], b[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int t = 0; t < 9; ++t) w[t / 3][t % 3][c] = weight[(c0 + c) * 9 + t];
+        b[c] = bias ? bias[c0 + c] : 0;
+    }
+    // output rows iy + 1, iy, iy - 1 take input row iy through weight rows 0, 1, 2
+    DwAcc a0, a1, a2;
+    dw_zero(a0);
+    dw_zero(a1);
+    dw_zero(a2);
+    int32_t l[kDwCols + 2][4], h[kDwCols + 2][4];
+    auto step = [&](DwAcc& next, DwAcc& mid, DwAcc& done, int iy) {
+        dw_load_row(in, img, iy, x0, c0, l, h);
+        dw_add(next, l, h, w[0]);
+        dw_add(mid, l, h, w[1]);
+        dw_add(done, l, h, w[2]);
+        if (iy - 1 >= y0) dw_store(done, b, out, img, iy - 1, x0, c0);
+        dw_zero(done);
+    };
+    for (int iy = y0 - 1; iy <= y1; iy += 3) {
+        step(a0, a1, a2, iy);
+        if (iy + 1 > y1) break;
+        step(a2, a0, a1, iy + 1);
+        if (iy + 2 > y1) break;
+        step(a1, a2, a0, iy + 2);
     }
 }
 
@@ -289,13 +335,16 @@ cudaError_t conv_direct(int16_t* out, const int16_t* x, const int16_t* weight, c
 }
 
 cudaError_t dwconv3x3(const Act& in, const Act& out, const int16_t* weight, const int16_t* bias, cudaStream_t s) {
-    if (in.c % 8 || in.c != out.c || in.pitch % 16 || out.pitch % 16 ||
-        reinterpret_cast<uintptr_t>(in.base) % 16 || reinterpret_cast<uintptr_t>(out.base) % 16)
+    if (in.c % 4 || in.c != out.c || in.h != out.h || in.w != out.w || in.n != out.n || in.pitch % 16 ||
+        out.pitch % 16 || reinterpret_cast<uintptr_t>(in.base) % 16 || reinterpret_cast<uintptr_t>(out.base) % 16)
         return cudaErrorInvalidValue;
-    const int cgroups = (in.c + kDwC - 1) / kDwC;
-    const dim3 grid((in.w + kDwTileW - 1) / kDwTileW, (in.h + kDwTileH - 1) / kDwTileH, in.n * cgroups);
-    if (grid.z > 65535) return cudaErrorInvalidValue;
-    dwconv3x3_kernel<<<grid, kDwThreads, 0, s>>>(in, out, weight, bias);
+    const int ch_blocks = (in.c + 4 * kDwQuads - 1) / (4 * kDwQuads);
+    const int col_blocks = (in.w + kDwCols * kDwColThreads - 1) / (kDwCols * kDwColThreads);
+    const int strips = (in.h + kDwRows - 1) / kDwRows;
+    const long long blocks = static_cast<long long>(ch_blocks) * col_blocks * strips * in.n;
+    if (blocks > INT32_MAX) return cudaErrorInvalidValue;
+    dwconv3x3_kernel<<<static_cast<unsigned>(blocks), kDwThreads, 0, s>>>(in, out, weight, bias, ch_blocks,
+                                                                          col_blocks, strips);
     return cudaGetLastError();
 }
 

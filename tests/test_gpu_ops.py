@@ -171,6 +171,21 @@ def test_depthwise_and_stride2(ufb, ora, dev):
     assert np.array_equal(N(ufb.conv2d(T(x, dev), T(w2, dev), None, 2, 2, 1, 1)), ora.conv2d(x, w2, None, 2, 1))
 
 
+@pytest.mark.parametrize("n,c,h,w", [(1, 64, 10, 12), (2, 256, 37, 45), (1, 192, 16, 33), (1, 512, 35, 50),
+                                     (3, 4, 5, 7), (1, 132, 1, 1)])
+def test_depthwise_split_kernel(ufb, ora, dev, n, c, h, w):
+    """The engine's split-layout depthwise kernel (through conv2d's depthwise
+    route): strip, column-block and channel-block edges, odd sizes, 1x1 images."""
+    rng = np.random.default_rng(c * 31 + h)
+    x = rng.integers(-32768, 32768, (n, c, h, w)).astype(np.int16)
+    wd = rng.integers(-32768, 32768, (c, 1, 3, 3)).astype(np.int16)
+    b = rng.integers(-32768, 32768, (c,)).astype(np.int16)
+    for bias in (T(b, dev), None):
+        got = ufb.conv2d(T(x, dev), T(wd, dev), bias, 1, 1, 1, 1, c)
+        assert np.array_equal(N(got), ora.conv2d(x, wd, b if bias is not None else None, 1, 1, c))
+    _status_clean(ufb)
+
+
 def test_warp_matches_oracle(ufb, ora, dev):
     rng = np.random.default_rng(1)
     f = rng.integers(-4096, 4097, (1, 8, 44, 80)).astype(np.int16)
