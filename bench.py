@@ -146,9 +146,13 @@ def print_shapes(codecs, frames):
 
 
 def load_traffic(key):
-    path = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(path):
-        return json.load(open(path)).get(key)
+    """DRAM bytes per launch recorded in a profile summary (a line `key: N` in
+    profiles/*.md, written from an ncu capture of the same workload), or None."""
+    import glob
+    for path in sorted(glob.glob(os.path.join(ROOT, "profiles", "*.md"))):
+        for line in open(path):
+            if line.startswith(key + ":"):
+                return float(line.split(":", 1)[1].split()[0])
     return None
 
 

@@ -26,14 +26,16 @@
 // Persistent CTAs (one per SM) walk the output tiles.  Warp 0 issues TMA into a
 // 3 x 64 KB ring that runs ahead across tiles (about 1.4 us of L2 round trip
 // per stage needs that much in flight), warp 1 owns TMEM and issues the MMAs,
-// warps 4-19 run the epilogue (registers re-balanced towards them): they first
-// copy their 3 x 32 accumulator
-// columns into registers and release TMEM at once, so the next tile's MMAs
-// start while they recombine, add the bias, saturate, apply the fused
-// elementwise step and write the tile.  Output tiles leave through a 16 KB
-// shared-memory stage (128-byte swizzle, one byte plane at a time) and TMA
-// stores, which write whole lines; per-thread pixel-row stores reach only a
-// third of the bandwidth.
+// warps 2-9 run the epilogue, two per TMEM lane quarter, 64 output channels
+// each.  Consecutive tiles alternate between accumulator sets at TMEM columns
+// [0, 384) and [128, 512): the next tile's set overlaps only two of the three
+// slices of the current one, so the epilogue drains those two, releases TMEM
+// and reads the third while the next tile's MMAs already run.  Each epilogue
+// warp then recombines, adds the bias, saturates, applies the fused
+// elementwise step and stores its 32 pixels x 64 channels through its own
+// 2 KB shared-memory stage (64-byte swizzle, one byte plane at a time) with a
+// TMA store, which writes whole lines: per-thread pixel-row stores reach only
+// a third of the bandwidth.
 #include "umma.cuh"
 #include "conv_epi.cuh"
 #include "conv_tc.h"
@@ -61,7 +63,8 @@ constexpr uint32_t kABytes = kBM * kBK;                     // one activation pl
 constexpr uint32_t kBBytes = 2 * kBN * kBK;                 // stacked low / high weight rows
 constexpr uint32_t kStageBytes = 2 * kABytes + kBBytes;     // 64 KB
 constexpr int kStages = 3;
-constexpr uint32_t kStagingBytes = kBM * kBN;               // one byte plane of an output tile
+constexpr uint32_t kWarpStage = 2048;                        // per epilogue warp: 32 pixels x 64 channels, one plane
+constexpr uint32_t kStagingBytes = kWarpStage * kEpiWarps;
 constexpr uint32_t kTmemCols = 512;                         // two staggered accumulator sets
 constexpr size_t kSmemLimit = 225 * 1024;  // dynamic shared memory: 227 KB less static barriers and slack
 
@@ -186,24 +189,15 @@ __device__ __forceinline__ int32_t finish_rna(int32_t V, int32_t U) {
     return T - static_cast<int32_t>(((U & 8191) == 0) & (T <= 0));
 }
 
-// Bounded barrier among the epilogue warps (an mbarrier round, so a warp that
-// gave up on a pipeline wait cannot leave the others blocked forever).
-__device__ __forceinline__ bool epi_sync(uint64_t* bar, uint32_t& phase, int lane, int* status) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar);
-    const bool ok = mbar_wait(bar, phase, status, 6);
-    phase ^= 1;
-    __syncwarp();
-    return ok;
-}
-
+// TMA store of one epilogue warp's box: the 32 pixels of TMEM lane quarter q
+// (tile rows 32 q / tile_w ..) and channels c0 .. of one plane.
 template <bool SPATIAL>
-__device__ __forceinline__ void tma_store_tile(const CUtensorMap* map, const void* src, const TileCoord& tc, int c0,
-                                               int plane) {
+__device__ __forceinline__ void tma_store_quarter(const CUtensorMap* map, const void* src, const ConvTcArgs& a,
+                                                  const TileCoord& tc, int quarter, int c0, int plane) {
     if (SPATIAL)
-        tma_store_5d(map, src, c0, plane, tc.x0, tc.y0, tc.img);
+        tma_store_5d(map, src, c0, plane, tc.x0, tc.y0 + quarter * 32 / a.tile_w, tc.img);
     else
-        tma_store_3d(map, src, c0, plane, static_cast<int>(tc.p0));
+        tma_store_3d(map, src, c0, plane, static_cast<int>(tc.p0) + quarter * 32);
 }
 
 template <bool SPATIAL, int MODE, int SIGNED>
@@ -219,7 +213,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
     int16_t* lut_s = reinterpret_cast<int16_t*>(bias_s + args.n_tiles * kBN);          // LUT window
     __shared__ __align__(8) uint64_t full_bar[kStages];
     __shared__ __align__(8) uint64_t empty_bar[kStages];
-    __shared__ __align__(8) uint64_t tmem_full, tmem_empty, epi_bar;
+    __shared__ __align__(8) uint64_t tmem_full, tmem_empty;
     __shared__ uint32_t tmem_holder;
     __shared__ int consumed;
 
@@ -234,7 +228,6 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         }
         mbar_init(&tmem_full, 1);
         mbar_init(&tmem_empty, kEpiWarps);
-        mbar_init(&epi_bar, kEpiWarps);
         consumed = 0;
         fence_mbar_init();
     }
@@ -358,9 +351,9 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         const int cgroup = (warp - kFirstEpiWarp) >> 2;  // columns [kCols cgroup, kCols cgroup + kCols)
         const int row = quarter * 32 + lane;            // TMEM lane = pixel of the tile
         const uint32_t acc = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + cgroup * kCols;  // + set offset
-        const bool issuer = warp == kFirstEpiWarp && lane == 0;
+        const bool issuer = warp == kFirstEpiWarp && lane == 0;  // residual prefetches
+        uint8_t* stage = staging + (warp - kFirstEpiWarp) * kWarpStage;  // this warp's own stage
         const Act& out = args.out;
-        uint32_t sync_phase = 0;
         int ti = 0;
         if (MODE == kEpiRes && issuer && blockIdx.x < args.total_tiles)
             prefetch_residuals<SPATIAL>(&mapRes1, &mapRes2, args, blockIdx.x);
@@ -540,14 +533,12 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                 }
             }
             if (STORE == kStoreTma) {
-                // one byte plane at a time through the 128-byte-swizzled stage:
-                // row r holds the tile's 128 channels of pixel r, 16-byte chunk c
-                // at position c ^ (r & 7)
-                bool ok = true;
+                // each warp stores its own 32 pixels x 64 channels, one byte plane
+                // at a time, through its 2 KB stage in the 64-byte swizzle
+                // (16-byte chunk c of row r at position c ^ ((r >> 1) & 3)), so
+                // the eight lanes of a shared-memory phase hit distinct banks
 #pragma unroll
                 for (int plane = 0; plane < 2; ++plane) {
-                    ok = ok && epi_sync(&epi_bar, sync_phase, lane, args.status);  // stage is free
-                    if (!ok) break;
 #pragma unroll
                     for (int h = 0; h < kCols / 16; ++h) {
                         uint32_t p8[8];
@@ -555,47 +546,44 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         for (int i = 0; i < 8; ++i) p8[i] = p[8 * h + i];
                         uint4 lo, hi;
                         split_bytes(p8, lo, hi);
-                        const int chunk = cgroup * (kCols / 16) + h;
-                        *reinterpret_cast<uint4*>(staging + row * 128 + ((chunk ^ (row & 7)) << 4)) = plane ? hi : lo;
+                        *reinterpret_cast<uint4*>(stage + lane * 64 + ((h ^ ((lane >> 1) & 3)) << 4)) = plane ? hi : lo;
                     }
                     fence_proxy_async_smem();
-                    ok = epi_sync(&epi_bar, sync_phase, lane, args.status);
-                    if (!ok) break;
-                    if (issuer) {
-                        tma_store_tile<SPATIAL>(&mapOut, staging, tc, tc.co0, plane);
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_quarter<SPATIAL>(&mapOut, stage, args, tc, quarter, cbase, plane);
                         bulk_commit();
-                        bulk_wait_read();
+                        bulk_wait_read();  // the stage is reused by the next plane
                     }
+                    __syncwarp();
                 }
-                if (!ok) break;
             } else {
-                // wsilu4: kCols / 4 output channels per thread, both planes staged at
-                // once as [plane][pixel][32 channels] (unswizzled, 32-byte rows)
-                if (!epi_sync(&epi_bar, sync_phase, lane, args.status)) break;
+                // wsilu4: kCols / 4 output channels per thread, both planes staged
+                // at once as [plane][32 pixels][16 channels] (16-byte rows)
 #pragma unroll
                 for (int h = 0; h < kCols / 16; ++h) {
                     int32_t r[4];
 #pragma unroll
                     for (int g = 0; g < 4; ++g) {
                         const uint32_t a0 = p[8 * h + 2 * g], a1 = p[8 * h + 2 * g + 1];
-                        r[g] = clamp16(lut(lo16(a0)) + lut(hi16(a0)) + lut(lo16(a1)) + lut(hi16(a1)));
+                        r[g] = lut(lo16(a0)) + lut(hi16(a0)) + lut(lo16(a1)) + lut(hi16(a1));
                     }
-                    const uint32_t w0 = pack2(r[0], r[1]), w1 = pack2(r[2], r[3]);
-                    const int c4 = cgroup * (kCols / 4) + 4 * h;  // first wsilu4 channel of the group
-                    *reinterpret_cast<uint32_t*>(staging + row * 32 + c4) = __byte_perm(w0, w1, 0x6420);
-                    *reinterpret_cast<uint32_t*>(staging + kBM * 32 + row * 32 + c4) = __byte_perm(w0, w1, 0x7531);
+                    const uint32_t w0 = pack2_sat(r[0], r[1]), w1 = pack2_sat(r[2], r[3]);
+                    *reinterpret_cast<uint32_t*>(stage + lane * 16 + 4 * h) = __byte_perm(w0, w1, 0x6420);
+                    *reinterpret_cast<uint32_t*>(stage + 512 + lane * 16 + 4 * h) = __byte_perm(w0, w1, 0x7531);
                 }
                 fence_proxy_async_smem();
-                if (!epi_sync(&epi_bar, sync_phase, lane, args.status)) break;
-                if (issuer) {
-                    tma_store_tile<SPATIAL>(&mapOut, staging, tc, tc.co0 / 4, 0);
-                    tma_store_tile<SPATIAL>(&mapOut, staging + kBM * 32, tc, tc.co0 / 4, 1);
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_quarter<SPATIAL>(&mapOut, stage, args, tc, quarter, cbase / 4, 0);
+                    tma_store_quarter<SPATIAL>(&mapOut, stage + 512, args, tc, quarter, cbase / 4, 1);
                     bulk_commit();
                     bulk_wait_read();
                 }
+                __syncwarp();
             }
         }
-        if (issuer) bulk_wait_all();
+        if (lane == 0) bulk_wait_all();
     }
 
     tc_fence_before();
@@ -731,14 +719,15 @@ cudaError_t launch(const ConvMaps& m, const ConvTcArgs& args, size_t smem, int s
                              : launch_signed<SPATIAL, 0>(m, args, smem, sms, stream);
 }
 
-// Tensor map of a split-NHWC view in tile order: flat {c, plane, pixels} or
-// spatial {c, plane, w, h, n}, box of `box_c` channels of one plane.
+// Tensor map of a split-NHWC view in tile order: flat {c, plane, pixels} (box
+// of tw * th pixels) or spatial {c, plane, w, h, n} (box tw x th), box of
+// `box_c` channels of one plane.
 bool act_map(CUtensorMap* map, const Act& v, bool flat, int tw, int th, cuuint32_t box_c,
              CUtensorMapSwizzle swizzle, std::string& err) {
     if (flat) {
         const cuuint64_t dims[3] = {static_cast<cuuint64_t>(v.c), 2, static_cast<cuuint64_t>(v.pixels())};
         const cuuint64_t strides[2] = {static_cast<cuuint64_t>(v.pitch), static_cast<cuuint64_t>(2 * v.pitch)};
-        const cuuint32_t box[3] = {box_c, 1, kBM};
+        const cuuint32_t box[3] = {box_c, 1, static_cast<cuuint32_t>(tw * th)};
         return encode(map, v.base, 3, dims, strides, box, err, swizzle);
     }
     const cuuint64_t dims[5] = {static_cast<cuuint64_t>(v.c), 2, static_cast<cuuint64_t>(v.w),
@@ -892,12 +881,10 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     args.n_tiles = w.co_tiles;
     // output box: 128 channels of one plane (128-byte swizzle), or 32 channels
     // (wsilu4, unswizzled); the map's extent is the view's, so tails are clipped
-    const cuuint32_t out_box_c = epi.wsilu4 ? kBN / 4 : kBN;
-    const CUtensorMapSwizzle out_swizzle = epi.wsilu4 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B;
     ConvMaps maps{};
     maps.b = w.map;
     long long m_tiles;
-    int tw = 0, th = 0;
+    int tw = 16, th = kBM / 16;  // flat mode: only tw * th = 128 matters
     if (flat) {
         args.m_total = in.pixels();
         m_tiles = (in.pixels() + kBM - 1) / kBM;
@@ -912,8 +899,13 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     }
     // the activation box is the tile's input window (shifted per tap in spatial mode)
     if (!act_map(&maps.a, in, flat, tw, th, kBK, CU_TENSOR_MAP_SWIZZLE_128B, err)) return -1;
+    // output box: one epilogue warp's 32 pixels, 64 channels (64-byte swizzle) or,
+    // for wsilu4, 16 channels (unswizzled); the map's extent is the view's, so
+    // tails are clipped
     if (!epi.shuffle2) {
-        if (!act_map(&maps.out, out, flat, tw, th, out_box_c, out_swizzle, err)) return -1;
+        const cuuint32_t box_c = epi.wsilu4 ? 16 : 64;
+        const CUtensorMapSwizzle sw = epi.wsilu4 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_64B;
+        if (!act_map(&maps.out, out, flat, tw, 32 / tw, box_c, sw, err)) return -1;
     } else {
         maps.out = maps.a;  // unused: pixel-shuffled tiles are stored by the threads
     }
