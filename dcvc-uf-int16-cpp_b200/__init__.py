@@ -332,14 +332,25 @@ class Codec:
         f = _c(frames, _np.int16)
         _check(self.L.ufb_codec_add_ref_frames(self.h, f.ctypes.data, f.shape[-2], f.shape[-1]))
 
-    def decompress(self, payloads, width, height, qp, reset=False, frames=True, yuv=False):
+    def decompress(self, payloads, width, height, qp, reset=False, frames=True, yuv=False, yuv_out=None):
+        """Decode one packet per stream.  Returns (frames [B, F, 3, Hp, Wp] int16 or
+        None, yuv [B, F, W*H*3/2] uint8 or None).  yuv_out, when given, is a
+        C-contiguous uint8 array of that shape that receives the YUV bytes (for
+        example page-locked memory reused across packets, which the copy from
+        the GPU reaches at full bus speed); it is returned as the yuv result."""
         bufs = [_np.frombuffer(p, _np.uint8).copy() if len(p) else _np.zeros(1, _np.uint8) for p in payloads]
         ptrs = (C.c_void_p * self.batch)(*[b.ctypes.data for b in bufs])
         lens = (C.c_size_t * self.batch)(*[len(p) for p in payloads])
         F = 1 if self.model.variant == "image" else 8
         hp, wp = (height + 15) // 16 * 16, (width + 15) // 16 * 16
         fo = _np.empty((self.batch, F, 3, hp, wp), _np.int16) if frames else None
-        yo = _np.empty((self.batch, F, width * height * 3 // 2), _np.uint8) if yuv else None
+        yshape = (self.batch, F, width * height * 3 // 2)
+        if yuv_out is not None:
+            if (not isinstance(yuv_out, _np.ndarray) or yuv_out.dtype != _np.uint8 or yuv_out.shape != yshape or
+                    not yuv_out.flags.c_contiguous):
+                raise UfbError(-1, f"yuv_out must be a C-contiguous uint8 array of shape {yshape}")
+            yuv = True
+        yo = (yuv_out if yuv_out is not None else _np.empty(yshape, _np.uint8)) if yuv else None
         rc = self.L.ufb_codec_decompress(self.h, ptrs, lens, width, height, qp, 1, int(reset),
                                          fo.ctypes.data if frames else None, yo.ctypes.data if yuv else None)
         if rc < 0:
