@@ -44,6 +44,7 @@
 #include <atomic>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 namespace ufb {
@@ -63,10 +64,13 @@ constexpr uint32_t kABytes = kBM * kBK;                     // one activation pl
 constexpr uint32_t kBBytes = 2 * kBN * kBK;                 // stacked low / high weight rows
 constexpr uint32_t kStageBytes = 2 * kABytes + kBBytes;     // 64 KB
 constexpr int kStages = 3;
-constexpr uint32_t kWarpStage = 2048;                        // per epilogue warp: 32 pixels x 64 channels, one plane
-constexpr uint32_t kStagingBytes = kWarpStage * kEpiWarps;
+// Per epilogue warp: 32 pixels x 64 channels of one byte plane (2 KB), or of
+// both planes in the residual mode (4 KB: the warp's residual tile arrives by
+// TMA into the stage, which then holds both output planes).
+__host__ __device__ constexpr uint32_t warp_stage_bytes(int mode) { return mode == 2 ? 4096 : 2048; }
 constexpr uint32_t kTmemCols = 512;                         // two staggered accumulator sets
-constexpr size_t kSmemLimit = 225 * 1024;  // dynamic shared memory: 227 KB less static barriers and slack
+constexpr size_t kSmemOptin = 227 * 1024;  // shared memory per CTA on sm_100 (static + dynamic)
+constexpr size_t kSmemBudget = kSmemOptin - 256;  // host-side planning: static barriers stay below 256 B
 
 // How an output tile is written.
 enum StoreKind : int {
@@ -158,20 +162,17 @@ __device__ __forceinline__ void add_one_residual(const Act& res, uint32_t (&p)[8
     }
 }
 
-// L2 prefetch of both planes of a tile's residual rows.
+// L2 prefetch of both planes of a tile's second residual rows (the first
+// arrives by TMA into the epilogue stages).
 template <bool SPATIAL>
-__device__ __forceinline__ void prefetch_residuals(const CUtensorMap* m1, const CUtensorMap* m2, const ConvTcArgs& a,
-                                                   int tile) {
+__device__ __forceinline__ void prefetch_residuals(const CUtensorMap* m2, const ConvTcArgs& a, int tile) {
     const TileCoord tc = tile_coord<SPATIAL>(a, tile);
 #pragma unroll
     for (int plane = 0; plane < 2; ++plane) {
-        if (SPATIAL) {
-            tma_prefetch_5d(m1, tc.co0, plane, tc.x0, tc.y0, tc.img);
-            if (a.epi.res2.base) tma_prefetch_5d(m2, tc.co0, plane, tc.x0, tc.y0, tc.img);
-        } else {
-            tma_prefetch_3d(m1, tc.co0, plane, static_cast<int>(tc.p0));
-            if (a.epi.res2.base) tma_prefetch_3d(m2, tc.co0, plane, static_cast<int>(tc.p0));
-        }
+        if (SPATIAL)
+            tma_prefetch_5d(m2, tc.co0, plane, tc.x0, tc.y0, tc.img);
+        else
+            tma_prefetch_3d(m2, tc.co0, plane, static_cast<int>(tc.p0));
     }
 }
 
@@ -187,6 +188,22 @@ __device__ __forceinline__ void release_tmem(uint64_t* bar, int lane) {
 __device__ __forceinline__ int32_t finish_rna(int32_t V, int32_t U) {
     const int32_t T = V + (U >> 13);
     return T - static_cast<int32_t>(((U & 8191) == 0) & (T <= 0));
+}
+
+// TMA load of one epilogue warp's box (residual rows), completing on bar.
+template <bool SPATIAL>
+__device__ __forceinline__ void tma_load_quarter(const CUtensorMap* map, void* dst, uint64_t* bar, const ConvTcArgs& a,
+                                                 const TileCoord& tc, int quarter, int c0, int plane) {
+    if (SPATIAL)
+        tma_load_5d(dst, map, bar, c0, plane, tc.x0, tc.y0 + quarter * 32 / a.tile_w, tc.img);
+    else
+        tma_load_3d(dst, map, bar, c0, plane, static_cast<int>(tc.p0) + quarter * 32);
+}
+
+__device__ __forceinline__ int4 load_bias4(const int32_t* b) { return *reinterpret_cast<const int4*>(b); }
+__device__ __forceinline__ int4 load_bias4(const int16_t* b) {
+    const uint2 v = *reinterpret_cast<const uint2*>(b);
+    return make_int4(lo16(v.x), hi16(v.x), lo16(v.y), hi16(v.y));
 }
 
 // TMA store of one epilogue warp's box: the 32 pixels of TMEM lane quarter q
@@ -208,12 +225,16 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
     constexpr int STORE = MODE == kEpiShuffle2 ? kStoreThreads : (MODE == kEpiWsilu4 ? kStoreTmaQuarter : kStoreTma);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr uint32_t kStage = warp_stage_bytes(MODE);
+    // the residual mode stages its (int16) bias as int16 to fit the larger stages
+    using BiasT = typename std::conditional<MODE == kEpiRes, int16_t, int32_t>::type;
     uint8_t* staging = smem + size_t(kStages) * kStageBytes;                           // 1024-aligned
-    int32_t* bias_s = reinterpret_cast<int32_t*>(staging + kStagingBytes);             // [n_tiles * 128]
+    BiasT* bias_s = reinterpret_cast<BiasT*>(staging + kStage * kEpiWarps);             // [n_tiles * 128]
     int16_t* lut_s = reinterpret_cast<int16_t*>(bias_s + args.n_tiles * kBN);          // LUT window
     __shared__ __align__(8) uint64_t full_bar[kStages];
     __shared__ __align__(8) uint64_t empty_bar[kStages];
     __shared__ __align__(8) uint64_t tmem_full, tmem_empty;
+    __shared__ __align__(8) uint64_t res_bar[MODE == kEpiRes ? kEpiWarps : 1];
     __shared__ uint32_t tmem_holder;
     __shared__ int consumed;
 
@@ -228,6 +249,8 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         }
         mbar_init(&tmem_full, 1);
         mbar_init(&tmem_empty, kEpiWarps);
+        if (MODE == kEpiRes)
+            for (int i = 0; i < kEpiWarps; ++i) mbar_init(&res_bar[i], 1);
         consumed = 0;
         fence_mbar_init();
     }
@@ -241,7 +264,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         if (args.epi.bias && i < args.co)
             b = args.epi.bias32 ? static_cast<const int32_t*>(args.epi.bias)[i]
                                 : static_cast<const int16_t*>(args.epi.bias)[i];
-        bias_s[i] = stage_bias(b);
+        bias_s[i] = static_cast<BiasT>(MODE == kEpiRes ? b : stage_bias(b));
     }
     LutView lut{args.epi.lut, nullptr, 0, 0, 0};
     if ((MODE == kEpiLut || MODE == kEpiWsilu4) && args.epi.lut_n > 0) {
@@ -352,20 +375,30 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         const int row = quarter * 32 + lane;            // TMEM lane = pixel of the tile
         const uint32_t acc = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + cgroup * kCols;  // + set offset
         const bool issuer = warp == kFirstEpiWarp && lane == 0;  // residual prefetches
-        uint8_t* stage = staging + (warp - kFirstEpiWarp) * kWarpStage;  // this warp's own stage
+        const int ew = warp - kFirstEpiWarp;
+        uint8_t* stage = staging + ew * kStage;  // this warp's own stage
+        int res_issued = 0, res_seen = 0;
         const Act& out = args.out;
         int ti = 0;
-        if (MODE == kEpiRes && issuer && blockIdx.x < args.total_tiles)
-            prefetch_residuals<SPATIAL>(&mapRes1, &mapRes2, args, blockIdx.x);
+        if (MODE == kEpiRes && issuer && args.epi.res2.base && blockIdx.x < args.total_tiles)
+            prefetch_residuals<SPATIAL>(&mapRes2, args, blockIdx.x);
         for (int tile = blockIdx.x; tile < args.total_tiles; tile += gridDim.x, ++ti) {
             // residual rows of this CTA's next tile into L2 while this one finishes
-            if (MODE == kEpiRes && issuer && tile + static_cast<int>(gridDim.x) < args.total_tiles)
-                prefetch_residuals<SPATIAL>(&mapRes1, &mapRes2, args, tile + gridDim.x);
-            if (!mbar_wait(&tmem_full, ti & 1, args.status, 4)) break;
-            tc_fence_after();
+            if (MODE == kEpiRes && issuer && args.epi.res2.base && tile + static_cast<int>(gridDim.x) < args.total_tiles)
+                prefetch_residuals<SPATIAL>(&mapRes2, args, tile + gridDim.x);
             const TileCoord tc = tile_coord<SPATIAL>(args, tile);
             const int cbase = tc.co0 + cgroup * kCols;
-            const int4* bq = reinterpret_cast<const int4*>(bias_s + cbase);
+            if (MODE == kEpiRes && lane == 0) {
+                // this warp's 32 x 64 residual tile (both planes): in flight while the
+                // MMAs finish and the accumulators are recombined; the stage is free
+                // (the last TMA store out of it has been read)
+                mbar_arrive_expect_tx(&res_bar[ew], 2 * 2048);
+                tma_load_quarter<SPATIAL>(&mapRes1, stage, &res_bar[ew], args, tc, quarter, cbase, 0);
+                tma_load_quarter<SPATIAL>(&mapRes1, stage + 2048, &res_bar[ew], args, tc, quarter, cbase, 1);
+            }
+            if (MODE == kEpiRes) ++res_issued;
+            if (!mbar_wait(&tmem_full, ti & 1, args.status, 4)) break;
+            tc_fence_after();
             uint32_t p[kWords];
             if ((ti & 1) == 0) {
                 // set at [0, 384); the next tile's set [128, 512) overlaps X and HH.
@@ -396,7 +429,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     tmem_wait_ld();
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        const int4 b = bq[4 * h + q];
+                        const int4 b = load_bias4(bias_s + cbase + 16 * h + 4 * q);
                         const int bb[4] = {b.x, b.y, b.z, b.w};
                         int32_t r[4];
 #pragma unroll
@@ -439,7 +472,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     tmem_wait_ld();
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        const int4 b = bq[4 * h + q];
+                        const int4 b = load_bias4(bias_s + cbase + 16 * h + 4 * q);
                         const int bb[4] = {b.x, b.y, b.z, b.w};
                         int32_t r[4];
 #pragma unroll
@@ -489,50 +522,65 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
 #pragma unroll
                 for (int i = 0; i < kWords; ++i) p[i] = pack2(lut(lo16(p[i])), lut(hi16(p[i])));
             }
-            if (MODE == kEpiRes && valid) {
+            if (MODE == kEpiRes) {
+                // first residual from the stage (64-byte swizzle, like the output)
+                ++res_seen;
+                if (!mbar_wait(&res_bar[ew], ti & 1, args.status, 7)) break;
 #pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    const Act& res = r == 0 ? args.epi.res1 : args.epi.res2;
-                    if (r == 1 && !res.base) break;
-                    const long long rp = r == 0 ? rpx1 : rpx2;
-                    if (n_valid == kCols) {
-                        // all loads of the pixel's channels first, then the adds
-                        uint4 rl[kCols / 16], rh[kCols / 16];
+                for (int h = 0; h < kCols / 16; ++h) {
+                    const int off = lane * 64 + ((h ^ ((lane >> 1) & 3)) << 4);
+                    const uint4 rl = *reinterpret_cast<const uint4*>(stage + off);
+                    const uint4 rh = *reinterpret_cast<const uint4*>(stage + 2048 + off);
+                    const uint32_t lw[4] = {rl.x, rl.y, rl.z, rl.w}, hw[4] = {rh.x, rh.y, rh.z, rh.w};
 #pragma unroll
-                        for (int h = 0; h < kCols / 16; ++h) {
-                            rl[h] = reinterpret_cast<const uint4*>(res.lo(rp) + cbase)[h];
-                            rh[h] = reinterpret_cast<const uint4*>(res.hi(rp) + cbase)[h];
-                        }
+                    for (int k = 0; k < 4; ++k) {
+                        uint32_t q0, q1;
+                        join_bytes(lw[k], hw[k], q0, q1);
+                        uint32_t& a0 = p[8 * h + 2 * k];
+                        uint32_t& a1 = p[8 * h + 2 * k + 1];
+                        a0 = pack2_sat(lo16(a0) + lo16(q0), hi16(a0) + hi16(q0));
+                        a1 = pack2_sat(lo16(a1) + lo16(q1), hi16(a1) + hi16(q1));
+                    }
+                }
+                __syncwarp();  // every lane has read the stage before it takes the output
+                // second residual (the up / down blocks' shortcut): per-thread loads
+                if (args.epi.res2.base && valid) {
 #pragma unroll
-                        for (int h = 0; h < kCols / 16; ++h) {
-                            const uint32_t lw[4] = {rl[h].x, rl[h].y, rl[h].z, rl[h].w};
-                            const uint32_t hw[4] = {rh[h].x, rh[h].y, rh[h].z, rh[h].w};
+                    for (int h = 0; h < kCols / 16; ++h) {
+                        if (16 * h >= n_valid) break;
+                        uint32_t p8[8];
 #pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                uint32_t q0, q1;
-                                join_bytes(lw[k], hw[k], q0, q1);
-                                uint32_t& a0 = p[8 * h + 2 * k];
-                                uint32_t& a1 = p[8 * h + 2 * k + 1];
-                                a0 = pack2_sat(lo16(a0) + lo16(q0), hi16(a0) + hi16(q0));
-                                a1 = pack2_sat(lo16(a1) + lo16(q1), hi16(a1) + hi16(q1));
-                            }
-                        }
-                    } else {
+                        for (int i = 0; i < 8; ++i) p8[i] = p[8 * h + i];
+                        add_one_residual(args.epi.res2, p8, cbase + 16 * h,
+                                         n_valid - 16 * h < 16 ? n_valid - 16 * h : 16, rpx2);
 #pragma unroll
-                        for (int h = 0; h < kCols / 16; ++h) {
-                            if (16 * h >= n_valid) break;
-                            uint32_t p8[8];
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) p8[i] = p[8 * h + i];
-                            add_one_residual(res, p8, cbase + 16 * h, n_valid - 16 * h < 16 ? n_valid - 16 * h : 16,
-                                             rp);
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) p[8 * h + i] = p8[i];
-                        }
+                        for (int i = 0; i < 8; ++i) p[8 * h + i] = p8[i];
                     }
                 }
             }
-            if (STORE == kStoreTma) {
+            if (STORE == kStoreTma && MODE == kEpiRes) {
+                // both output planes into the 4 KB stage, one wait for the reads
+#pragma unroll
+                for (int h = 0; h < kCols / 16; ++h) {
+                    uint32_t p8[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) p8[i] = p[8 * h + i];
+                    uint4 lo, hi;
+                    split_bytes(p8, lo, hi);
+                    const int off = lane * 64 + ((h ^ ((lane >> 1) & 3)) << 4);
+                    *reinterpret_cast<uint4*>(stage + off) = lo;
+                    *reinterpret_cast<uint4*>(stage + 2048 + off) = hi;
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_quarter<SPATIAL>(&mapOut, stage, args, tc, quarter, cbase, 0);
+                    tma_store_quarter<SPATIAL>(&mapOut, stage + 2048, args, tc, quarter, cbase, 1);
+                    bulk_commit();
+                    bulk_wait_read();
+                }
+                __syncwarp();
+            } else if (STORE == kStoreTma) {
                 // each warp stores its own 32 pixels x 64 channels, one byte plane
                 // at a time, through its 2 KB stage in the 64-byte swizzle
                 // (16-byte chunk c of row r at position c ^ ((r >> 1) & 3)), so
@@ -583,6 +631,8 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                 __syncwarp();
             }
         }
+        // abort path only: a residual load issued for a tile that was not finished
+        if (MODE == kEpiRes && res_issued > res_seen) mbar_wait(&res_bar[ew], (res_issued - 1) & 1, args.status, 8);
         if (lane == 0) bulk_wait_all();
     }
 
@@ -693,8 +743,18 @@ struct ConvMaps {
 template <bool SPATIAL, int MODE, int SIGNED>
 cudaError_t launch_mode(const ConvMaps& m, const ConvTcArgs& args, size_t smem, int sms, cudaStream_t stream) {
     auto kernel = conv_i16_tc_kernel<SPATIAL, MODE, SIGNED>;
-    // the attribute is per function and device; setting it each launch is cheap
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    // The attribute is per function and device and shared by every thread that
+    // launches the kernel, so it is always the kernel's full allowance (a
+    // per-launch value could be lowered by another thread between its set and
+    // this launch).
+    static const int allowance = [&] {
+        cudaFuncAttributes attr{};
+        return cudaFuncGetAttributes(&attr, kernel) == cudaSuccess
+                   ? static_cast<int>(kSmemOptin) - static_cast<int>(attr.sharedSizeBytes)
+                   : 0;
+    }();
+    if (smem > static_cast<size_t>(allowance)) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, allowance);
     if (e != cudaSuccess) return e;
     int grid = args.total_tiles < sms ? args.total_tiles : sms;
     const int cap = g_max_ctas.load(std::memory_order_relaxed);
@@ -847,8 +907,15 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
         err = "wsilu4 output must have a quarter of the convolution's channels";
         return -1;
     }
-    const size_t base_smem = 1024 + size_t(kStages) * kStageBytes + kStagingBytes + size_t(w.co_tiles) * kBN * 4;
-    if (base_smem > kSmemLimit) {
+    const bool res_mode = epi.res1.base && !epi.shuffle2 && !epi.wsilu4 && !epi.lut;
+    if (res_mode && epi.bias && epi.bias32) {
+        err = "fused residual adds take an int16 bias";
+        return -1;
+    }
+    const int mode_id = res_mode ? 2 : 0;
+    const size_t base_smem = 1024 + size_t(kStages) * kStageBytes + size_t(warp_stage_bytes(mode_id)) * kEpiWarps +
+                             size_t(w.co_tiles) * kBN * (res_mode ? 2 : 4);
+    if (base_smem > kSmemBudget) {
         err = "too many output channels for the staged bias";
         return -1;
     }
@@ -865,7 +932,7 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     args.epi = epi;
     // the LUT window rides in shared memory after the bias when it fits
     const size_t lut_bytes = (static_cast<size_t>(epi.lut_n) * 2 + 15) / 16 * 16;
-    if (!epi.lut || epi.lut_n <= 0 || base_smem + lut_bytes > kSmemLimit) args.epi.lut_n = 0;
+    if (!epi.lut || epi.lut_n <= 0 || base_smem + lut_bytes > kSmemBudget) args.epi.lut_n = 0;
     const size_t smem = base_smem + (args.epi.lut_n > 0 ? lut_bytes : 0);
     args.co = w.co;
     args.ci = w.ci;
@@ -910,7 +977,8 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
         maps.out = maps.a;  // unused: pixel-shuffled tiles are stored by the threads
     }
     maps.res1 = maps.res2 = maps.a;  // unused unless residuals are fused
-    if (epi.res1.base && !act_map(&maps.res1, epi.res1, flat, tw, th, kBN, CU_TENSOR_MAP_SWIZZLE_NONE, err))
+    // first residual: loaded per epilogue warp like the output box; second: L2 prefetch per tile
+    if (epi.res1.base && !act_map(&maps.res1, epi.res1, flat, tw, 32 / tw, 64, CU_TENSOR_MAP_SWIZZLE_64B, err))
         return -1;
     if (epi.res2.base && !act_map(&maps.res2, epi.res2, flat, tw, th, kBN, CU_TENSOR_MAP_SWIZZLE_NONE, err))
         return -1;

@@ -180,6 +180,47 @@ def test_batched_streams_match_single(ufb, ora, ref, syn, models):
         assert np.array_equal(got[s], single[0])
 
 
+def test_concurrent_codecs_match(ufb, syn, models):
+    """Codecs decoding on their own CUDA streams from two host threads at once
+    (how the bench overlaps one group's host rANS with another group's kernels)
+    give the same frames as one after the other."""
+    import threading
+    import torch
+    mine, _ = models["htl"]
+    jobs = []
+    for s in range(2):
+        video = _frames(syn, 17, seed=70 + s)
+        enc = ufb.Codec(mine, 1)
+        enc.set_skip_threshold(0.2)
+        enc.add_ref_frames(np.zeros((1, 3, H, W), np.int16))
+        jobs.append([enc.compress(syn.frames_to_chunk(video[1 + 8 * k: 9 + 8 * k]), 20, k == 0)[0]
+                     for k in range(2)])
+
+    def decode(payloads, stream=None):
+        c = ufb.Codec(mine, 1)
+        c.set_skip_threshold(0.2)
+        if stream is not None:
+            c.set_stream(stream)
+        c.add_ref_frames(np.zeros((1, 3, H, W), np.int16))
+        return [c.decompress(p, W, H, 20, k == 0)[0] for k, p in enumerate(payloads)]
+
+    want = [decode(j) for j in jobs]
+    got = [None, None]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+
+    def run(i):
+        got[i] = decode(jobs[i], streams[i])
+
+    threads = [threading.Thread(target=run, args=(i,)) for i in range(2)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    for i in range(2):
+        for a, b in zip(got[i], want[i]):
+            assert np.array_equal(a, b)
+
+
 def test_odd_size_padding(ufb, ora, ref, syn, models):
     """Width/height not multiples of 16: replicate padding and raw-frame crop."""
     mine, _ = models["htl"]
@@ -213,6 +254,21 @@ def test_p_frame_without_reference_raises(ufb, models):
     with pytest.raises(ufb.UfbError) as e:
         c.decompress([b"\x00\x00\x80\x00"], W, H, 20, False)
     assert "no reference" in str(e.value)
+
+
+@pytest.mark.parametrize("table", ["random", "relu"])
+def test_lut_tables_beyond_wsilu(ufb, ref, syn, table):
+    """A WSiLU table with no narrow window (random: the kernels read the global
+    table) and one that is max(v, 0) everywhere (a one-entry window) through the
+    fused LUT and WSiLU4 epilogues."""
+    t = dict(syn.prepared("htl", 2))
+    rng = np.random.default_rng(5)
+    v = np.arange(-32768, 32768)
+    t["tables.wsilu"] = (rng.integers(-32768, 32768, 65536) if table == "random"
+                         else np.maximum(v, 0)).astype(np.int16)
+    mine, theirs = ufb.Model("htl", t), ref.model("htl", t)
+    x = rng.integers(-6000, 6000, (1, 512, 6, 9)).astype(np.int16)
+    assert np.array_equal(mine.run("feature_extractor", x), theirs.run("feature_extractor", x))
 
 
 @pytest.mark.parametrize("extreme", [32639, 32767])
