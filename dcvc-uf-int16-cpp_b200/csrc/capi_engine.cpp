@@ -105,6 +105,7 @@ int ufb_model_run(ufb_model* m, const char* module, int nargs, const int16_t* co
             throw std::invalid_argument("invalid module call");
         const std::string mod = module;
         const Model& model = *m->m;
+        DeviceGuard device(model.device());
         Runner r(model, m->pool, m->s, m->status);
         const bool image = model.variant() == "image";
         const bool unshuffle8 = (mod == "enc" && image) || mod == "encoder";

@@ -67,7 +67,18 @@ constexpr int kStages = 3;
 // Per epilogue warp: 32 pixels x 64 channels of one byte plane (2 KB), or of
 // both planes in the residual mode (4 KB: the warp's residual tile arrives by
 // TMA into the stage, which then holds both output planes).
-__host__ __device__ constexpr uint32_t warp_stage_bytes(int mode) { return mode == 2 ? 4096 : 2048; }
+constexpr int kWarpCols = kBN / (kEpiWarps / 4);              // output channels per epilogue warp
+constexpr uint32_t kPlaneStage = 32 * kWarpCols;             // 32 pixels x kWarpCols channels, one plane
+__host__ __device__ constexpr uint32_t warp_stage_bytes(int mode) { return mode == 2 ? 2 * kPlaneStage : kPlaneStage; }
+
+// Position of 16-byte chunk h of stage row r: the 64-byte swizzle for 64-byte
+// rows (chunk ^ ((r >> 1) & 3)) or the 32-byte swizzle for 32-byte rows
+// (chunk ^ ((r >> 2) & 1)), so the eight lanes of a shared-memory phase hit
+// distinct banks; the TMA maps use the matching swizzle mode.
+__device__ __forceinline__ int stage_off(int r, int h) {
+    return kWarpCols == 64 ? r * 64 + ((h ^ ((r >> 1) & 3)) << 4) : r * 32 + ((h ^ ((r >> 2) & 1)) << 4);
+}
+constexpr CUtensorMapSwizzle kStageSwizzle = kWarpCols == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
 constexpr uint32_t kTmemCols = 512;                         // two staggered accumulator sets
 constexpr size_t kSmemOptin = 227 * 1024;  // shared memory per CTA on sm_100 (static + dynamic)
 constexpr size_t kSmemBudget = kSmemOptin - 256;  // host-side planning: static barriers stay below 256 B
@@ -392,9 +403,9 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                 // this warp's 32 x 64 residual tile (both planes): in flight while the
                 // MMAs finish and the accumulators are recombined; the stage is free
                 // (the last TMA store out of it has been read)
-                mbar_arrive_expect_tx(&res_bar[ew], 2 * 2048);
+                mbar_arrive_expect_tx(&res_bar[ew], 2 * kPlaneStage);
                 tma_load_quarter<SPATIAL>(&mapRes1, stage, &res_bar[ew], args, tc, quarter, cbase, 0);
-                tma_load_quarter<SPATIAL>(&mapRes1, stage + 2048, &res_bar[ew], args, tc, quarter, cbase, 1);
+                tma_load_quarter<SPATIAL>(&mapRes1, stage + kPlaneStage, &res_bar[ew], args, tc, quarter, cbase, 1);
             }
             if (MODE == kEpiRes) ++res_issued;
             if (!mbar_wait(&tmem_full, ti & 1, args.status, 4)) break;
@@ -528,9 +539,9 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                 if (!mbar_wait(&res_bar[ew], ti & 1, args.status, 7)) break;
 #pragma unroll
                 for (int h = 0; h < kCols / 16; ++h) {
-                    const int off = lane * 64 + ((h ^ ((lane >> 1) & 3)) << 4);
+                    const int off = stage_off(lane, h);
                     const uint4 rl = *reinterpret_cast<const uint4*>(stage + off);
-                    const uint4 rh = *reinterpret_cast<const uint4*>(stage + 2048 + off);
+                    const uint4 rh = *reinterpret_cast<const uint4*>(stage + kPlaneStage + off);
                     const uint32_t lw[4] = {rl.x, rl.y, rl.z, rl.w}, hw[4] = {rh.x, rh.y, rh.z, rh.w};
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
@@ -567,15 +578,15 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     for (int i = 0; i < 8; ++i) p8[i] = p[8 * h + i];
                     uint4 lo, hi;
                     split_bytes(p8, lo, hi);
-                    const int off = lane * 64 + ((h ^ ((lane >> 1) & 3)) << 4);
+                    const int off = stage_off(lane, h);
                     *reinterpret_cast<uint4*>(stage + off) = lo;
-                    *reinterpret_cast<uint4*>(stage + 2048 + off) = hi;
+                    *reinterpret_cast<uint4*>(stage + kPlaneStage + off) = hi;
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
                     tma_store_quarter<SPATIAL>(&mapOut, stage, args, tc, quarter, cbase, 0);
-                    tma_store_quarter<SPATIAL>(&mapOut, stage + 2048, args, tc, quarter, cbase, 1);
+                    tma_store_quarter<SPATIAL>(&mapOut, stage + kPlaneStage, args, tc, quarter, cbase, 1);
                     bulk_commit();
                     bulk_wait_read();
                 }
@@ -594,7 +605,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         for (int i = 0; i < 8; ++i) p8[i] = p[8 * h + i];
                         uint4 lo, hi;
                         split_bytes(p8, lo, hi);
-                        *reinterpret_cast<uint4*>(stage + lane * 64 + ((h ^ ((lane >> 1) & 3)) << 4)) = plane ? hi : lo;
+                        *reinterpret_cast<uint4*>(stage + stage_off(lane, h)) = plane ? hi : lo;
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
@@ -617,14 +628,15 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         r[g] = lut(lo16(a0)) + lut(hi16(a0)) + lut(lo16(a1)) + lut(hi16(a1));
                     }
                     const uint32_t w0 = pack2_sat(r[0], r[1]), w1 = pack2_sat(r[2], r[3]);
-                    *reinterpret_cast<uint32_t*>(stage + lane * 16 + 4 * h) = __byte_perm(w0, w1, 0x6420);
-                    *reinterpret_cast<uint32_t*>(stage + 512 + lane * 16 + 4 * h) = __byte_perm(w0, w1, 0x7531);
+                    *reinterpret_cast<uint32_t*>(stage + lane * (kCols / 4) + 4 * h) = __byte_perm(w0, w1, 0x6420);
+                    *reinterpret_cast<uint32_t*>(stage + 8 * kCols + lane * (kCols / 4) + 4 * h) =
+                        __byte_perm(w0, w1, 0x7531);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
                     tma_store_quarter<SPATIAL>(&mapOut, stage, args, tc, quarter, cbase / 4, 0);
-                    tma_store_quarter<SPATIAL>(&mapOut, stage + 512, args, tc, quarter, cbase / 4, 1);
+                    tma_store_quarter<SPATIAL>(&mapOut, stage + 8 * kCols, args, tc, quarter, cbase / 4, 1);
                     bulk_commit();
                     bulk_wait_read();
                 }
@@ -970,15 +982,15 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     // for wsilu4, 16 channels (unswizzled); the map's extent is the view's, so
     // tails are clipped
     if (!epi.shuffle2) {
-        const cuuint32_t box_c = epi.wsilu4 ? 16 : 64;
-        const CUtensorMapSwizzle sw = epi.wsilu4 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_64B;
+        const cuuint32_t box_c = epi.wsilu4 ? kWarpCols / 4 : kWarpCols;
+        const CUtensorMapSwizzle sw = epi.wsilu4 ? CU_TENSOR_MAP_SWIZZLE_NONE : kStageSwizzle;
         if (!act_map(&maps.out, out, flat, tw, 32 / tw, box_c, sw, err)) return -1;
     } else {
         maps.out = maps.a;  // unused: pixel-shuffled tiles are stored by the threads
     }
     maps.res1 = maps.res2 = maps.a;  // unused unless residuals are fused
     // first residual: loaded per epilogue warp like the output box; second: L2 prefetch per tile
-    if (epi.res1.base && !act_map(&maps.res1, epi.res1, flat, tw, 32 / tw, 64, CU_TENSOR_MAP_SWIZZLE_64B, err))
+    if (epi.res1.base && !act_map(&maps.res1, epi.res1, flat, tw, 32 / tw, kWarpCols, kStageSwizzle, err))
         return -1;
     if (epi.res2.base && !act_map(&maps.res2, epi.res2, flat, tw, th, kBN, CU_TENSOR_MAP_SWIZZLE_NONE, err))
         return -1;

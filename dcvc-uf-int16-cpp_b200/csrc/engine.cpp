@@ -530,7 +530,10 @@ void Codec::set_skip_threshold(double threshold) {
     skip_threshold_ = static_cast<int>(rounded);
 }
 
-void Codec::clear_dpb() { reference_ = memory_ = context_ = Tensor(); }
+void Codec::clear_dpb() {
+    DeviceGuard device(m_.device());
+    reference_ = memory_ = context_ = Tensor();
+}
 
 void Codec::sync_and_check() {
     ck(cudaStreamSynchronize(s_), "codec stream");
@@ -569,6 +572,7 @@ void Codec::parallel_streams(F&& fn) {
 }
 
 void Codec::add_ref_frames(const int16_t* frames, int h, int w) {
+    DeviceGuard device(m_.device());
     // IntegerModel::add_ref_feature_from_frame: clear the DPB, reference =
     // pixel_unshuffle(frame, 8) (src/integer_model.cpp:107-114).
     if (h % 8 || w % 8) throw std::invalid_argument("reference frame extents must be multiples of 8");
@@ -585,6 +589,7 @@ void Codec::add_ref_frames(const int16_t* frames, int h, int w) {
 }
 
 void Codec::set_reference_from(const Codec& image) {
+    DeviceGuard device(m_.device());
     if (image.last_frames_.empty()) throw std::runtime_error("image codec has no reconstruction");
     const Tensor& f = image.last_frames_.back();
     if (f.a.n != batch_ || f.a.c != 192) throw std::invalid_argument("reference batch or channels differ");
@@ -799,6 +804,7 @@ void Codec::emit_frames(const std::vector<Tensor>& frames, uint32_t width, uint3
 // IntegerModel::decompress (src/integer_model.cpp:336-359).
 int Codec::decompress(const uint8_t* const* payloads, const size_t* lengths, uint32_t width, uint32_t height, int qp,
                       bool reset, int16_t* frames_out, uint8_t* yuv_out) {
+    DeviceGuard device(m_.device());
     if (qp < 0 || qp >= 64 || !width || !height) throw std::invalid_argument("Unsupported UF integer packet parameters");
     host_seconds_ = 0;
     Runner r(m_, pool_, s_, status_, &stats_);
@@ -831,6 +837,7 @@ int Codec::decompress(const uint8_t* const* payloads, const size_t* lengths, uin
 // IntegerModel::compress (src/integer_model.cpp:312-334).
 int Codec::compress(const uint8_t* frames, int channels, int h, int w, int qp, bool reset,
                     std::vector<std::vector<uint8_t>>& payloads, int16_t* frames_out) {
+    DeviceGuard device(m_.device());
     if (qp < 0 || qp >= 64) throw std::invalid_argument("UF QP must be between 0 and 63");
     host_seconds_ = 0;
     Runner r(m_, pool_, s_, status_, &stats_);
@@ -906,6 +913,7 @@ int Codec::compress(const uint8_t* frames, int channels, int h, int w, int qp, b
 }
 
 bool Codec::state(int which, int16_t* out, size_t capacity, int64_t* shape4) {
+    DeviceGuard device(m_.device());
     const Tensor& t = which == 0 ? reference_ : which == 1 ? memory_ : context_;
     if (!t.defined()) return false;
     const size_t n = static_cast<size_t>(t.a.n) * t.a.c * t.a.h * t.a.w;

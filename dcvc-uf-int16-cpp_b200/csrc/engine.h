@@ -118,6 +118,26 @@ private:
 
 // Launch accounting of one engine (all kernels) and, when profiling is on,
 // CUDA-event timing of the tensor-core convolution launches.
+// Makes `device` current in the calling thread for the guard's lifetime (the
+// engine's objects may be driven from any host thread, each of which starts
+// on device 0) and restores the previous device.
+class DeviceGuard {
+public:
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&prev_) != cudaSuccess) prev_ = -1;
+        if (prev_ != device) cudaSetDevice(device);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev_ >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev_) cudaSetDevice(prev_);
+    }
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+private:
+    int prev_ = -1;
+};
+
 struct EngineStats {
     long long launches = 0;        // kernels launched
     long long conv_launches = 0;   // tensor-core convolution launches
