@@ -98,11 +98,11 @@ __global__ void conv_direct_kernel(int16_t* __restrict__ out, const int16_t* __r
 // kernel, src/cuda/conv.cu:44-60).  A thread owns four channels (one 32-bit
 // word of each byte plane) of kDwCols adjacent output columns and slides down a
 // strip of rows: each input row is read once per thread (warp-coalesced
-// 128-byte rows; neighbouring columns meet again in L1), split into bytes and
-// multiplied into the three output rows it feeds, with the 36 weights held in
-// registers.  Accumulation stays in int32 by keeping the planes apart:
-// S_lo = sum lo * w and S_hi = sum hi * w (|S| < 2^27 for 9 taps), combined
-// exactly by the 32-bit rna recombination of the tensor-core epilogue.
+// 128-byte rows; neighbouring columns meet again in L1), its byte planes are
+// joined back into int16 values, and it is multiplied into the three output
+// rows it feeds with the 36 weights held in registers, one wide multiply-add
+// per tap into an exact int64 sum (|S| < 2^34).  Two blocks of 256 threads per
+// SM (128 registers) measured fastest: the kernel is latency-bound.
 constexpr int kDwQuads = 32;     // channel quads per block (128 channels)
 constexpr int kDwColThreads = 8; // threads along x per block
 constexpr int kDwRows = 16;      // output rows per strip
@@ -110,29 +110,26 @@ constexpr int kDwThreads = kDwQuads * kDwColThreads;  // 256
 constexpr int kDwCols = 2;       // output columns per thread (two blocks per SM: the best measured layout)
 
 struct DwAcc {
-    int32_t lo[kDwCols][4], hi[kDwCols][4];  // [column][channel]
+    int64_t s[kDwCols][4];  // [column][channel]: exact sum of x * w
 };
 
 __device__ __forceinline__ void dw_zero(DwAcc& a) {
 #pragma unroll
     for (int j = 0; j < kDwCols; ++j)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) a.lo[j][c] = a.hi[j][c] = 0;
+        for (int c = 0; c < 4; ++c) a.s[j][c] = 0;
 }
 
-// Adds one input row (pixels x0-1 .. x0+kDwCols as bytes l / h) into the
-// accumulator of an output row through weight row w[kx][channel].
-__device__ __forceinline__ void dw_add(DwAcc& a, const int32_t (&l)[kDwCols + 2][4],
-                                       const int32_t (&h)[kDwCols + 2][4], const int32_t (&w)[3][4]) {
+// Adds one input row (pixels x0-1 .. x0+kDwCols as int16 values x) into the
+// accumulator of an output row through weight row w[kx][channel]: one wide
+// multiply-add per tap (|x w| <= 2^30, nine taps need more than 32 bits).
+__device__ __forceinline__ void dw_add(DwAcc& a, const int32_t (&x)[kDwCols + 2][4], const int32_t (&w)[3][4]) {
 #pragma unroll
     for (int j = 0; j < kDwCols; ++j)
 #pragma unroll
         for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                a.lo[j][c] += l[j + kx][c] * w[kx][c];
-                a.hi[j][c] += h[j + kx][c] * w[kx][c];
-            }
+            for (int c = 0; c < 4; ++c) a.s[j][c] += static_cast<int64_t>(x[j + kx][c]) * w[kx][c];
 }
 
 __device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], const Act& out, int img, int oy,
@@ -143,9 +140,9 @@ __device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], 
         int32_t r[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            const int32_t U = a.lo[j][c] + ((a.hi[j][c] & 31) << 8) + 4096;
-            const int32_t T = (a.hi[j][c] >> 5) + (U >> 13);
-            r[c] = T - static_cast<int32_t>(((U & 8191) == 0) & (T <= 0)) + b[c];
+            // rna(S / 8192) = floor((S + 4096 - [S < 0]) / 8192); |S| < 2^34
+            const int64_t S = a.s[j][c];
+            r[c] = static_cast<int32_t>((S + 4096 + (S >> 63)) >> 13) + b[c];
         }
         const uint32_t p0 = pack2_sat(r[0], r[1]), p1 = pack2_sat(r[2], r[3]);
         const long long px = out.pixel(img, oy, x0 + j);
@@ -154,25 +151,26 @@ __device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], 
     }
 }
 
-// Input row iy, pixels x0-1 .. x0+kDwCols, four channels: low bytes (u8) and
-// high bytes (s8) as int32; zero outside the image.
+// Input row iy, pixels x0-1 .. x0+kDwCols, four channels, joined back into
+// int16 values; zero outside the image.
 __device__ __forceinline__ void dw_load_row(const Act& in, int img, int iy, int x0, int c0,
-                                            int32_t (&l)[kDwCols + 2][4], int32_t (&h)[kDwCols + 2][4]) {
+                                            int32_t (&x)[kDwCols + 2][4]) {
     const bool row_ok = iy >= 0 && iy < in.h;
 #pragma unroll
     for (int p = 0; p < kDwCols + 2; ++p) {
-        const int x = x0 - 1 + p;
+        const int xx = x0 - 1 + p;
         uint32_t lw = 0, hw = 0;
-        if (row_ok && x >= 0 && x < in.w) {
-            const long long px = in.pixel(img, iy, x);
+        if (row_ok && xx >= 0 && xx < in.w) {
+            const long long px = in.pixel(img, iy, xx);
             lw = __ldg(reinterpret_cast<const uint32_t*>(in.lo(px) + c0));
             hw = __ldg(reinterpret_cast<const uint32_t*>(in.hi(px) + c0));
         }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            l[p][c] = static_cast<int32_t>((lw >> (8 * c)) & 0xffu);
-            h[p][c] = static_cast<int32_t>(static_cast<int8_t>(hw >> (8 * c)));
-        }
+        uint32_t q0, q1;  // channels (0, 1) and (2, 3) as int16 pairs
+        join_bytes(lw, hw, q0, q1);
+        x[p][0] = lo16(q0);
+        x[p][1] = hi16(q0);
+        x[p][2] = lo16(q1);
+        x[p][3] = hi16(q1);
     }
 }
 
@@ -202,12 +200,12 @@ dwconv3x3_kernel(Act in, Act out, const int16_t* __restrict__ weight, const int1
     dw_zero(a0);
     dw_zero(a1);
     dw_zero(a2);
-    int32_t l[kDwCols + 2][4], h[kDwCols + 2][4];
+    int32_t xv[kDwCols + 2][4];
     auto step = [&](DwAcc& next, DwAcc& mid, DwAcc& done, int iy) {
-        dw_load_row(in, img, iy, x0, c0, l, h);
-        dw_add(next, l, h, w[0]);
-        dw_add(mid, l, h, w[1]);
-        dw_add(done, l, h, w[2]);
+        dw_load_row(in, img, iy, x0, c0, xv);
+        dw_add(next, xv, w[0]);
+        dw_add(mid, xv, w[1]);
+        dw_add(done, xv, w[2]);
         if (iy - 1 >= y0) dw_store(done, b, out, img, iy - 1, x0, c0);
         dw_zero(done);
     };
