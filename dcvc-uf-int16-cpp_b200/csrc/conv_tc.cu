@@ -211,10 +211,19 @@ __device__ __forceinline__ void tma_load_quarter(const CUtensorMap* map, void* d
         tma_load_3d(dst, map, bar, c0, plane, static_cast<int>(tc.p0) + quarter * 32);
 }
 
-__device__ __forceinline__ int4 load_bias4(const int32_t* b) { return *reinterpret_cast<const int4*>(b); }
+// Bias loads from shared memory stay where the epilogue uses them (volatile):
+// hoisted to the top of a tile they would hold 64 registers and cause spills.
+__device__ __forceinline__ int4 load_bias4(const int32_t* b) {
+    int4 v;
+    asm volatile("ld.shared.v4.s32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(smem_u32(b)));
+    return v;
+}
 __device__ __forceinline__ int4 load_bias4(const int16_t* b) {
-    const uint2 v = *reinterpret_cast<const uint2*>(b);
-    return make_int4(lo16(v.x), hi16(v.x), lo16(v.y), hi16(v.y));
+    uint32_t x, y;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(x), "=r"(y) : "r"(smem_u32(b)));
+    return make_int4(lo16(x), hi16(x), lo16(y), hi16(y));
 }
 
 // TMA store of one epilogue warp's box: the 32 pixels of TMEM lane quarter q
