@@ -337,6 +337,8 @@ def bench_decode_ours(args, rank, world, local):
                      "achieved": achieved, "peak": peak, "unit": "TOPS(int8)",
                      "frac": achieved / peak if achieved else None,
                      "traffic": load_traffic("decode_conv_per_launch"),
+                     "traffic_launch": "DRAM read + write of one 512->512 residual-epilogue launch over 32640 "
+                                       "pixels (profiles/conv_i16_tc_decode_full.md); algorithmic 100.3 MB",
                      "peak_source": "measured live: dense tcgen05 kind::i8 probe (ufb_probe_i8_peak)",
                      "algorithmic": "8 int8 ops per int16 MAC",
                      "measured_on": "one extra step with the codec groups in turn, every convolution "
