@@ -416,3 +416,244 @@ class Codec:
             shape, launches, macs, ms = line.split("\t")
             table[shape] = (int(launches), float(macs), float(ms))
         return table
+
+
+# ---------------------------------------------------------------------------
+# UF16 bitstream container, digests and whole-stream coding
+# (uf::read_* / write_* / scan_bitstream, src/bitstream.cpp:173-360;
+# uf::IntegerCodec::encode / decode_stream_impl, src/integer_codec.cpp:215-493).
+# ---------------------------------------------------------------------------
+
+NAL_SPS, NAL_INTRA, NAL_PREDICTED = 0, 1, 2
+PREPARED_FORMAT = "dcvc-uf-prepared-v1"
+ARITHMETIC = "uf-int16-q9-w13-acc64-rna-sat-v1"
+
+
+class Uf16Nal(C.Structure):
+    _fields_ = [("type", C.c_int), ("sps_id", C.c_int), ("width", C.c_uint32), ("height", C.c_uint32),
+                ("qp", C.c_int), ("entropy_parallel", C.c_int), ("reset", C.c_int),
+                ("payload_offset", C.c_uint64), ("payload_length", C.c_uint64)]
+
+
+class Uf16Summary(C.Structure):
+    _fields_ = [("integer", C.c_int), ("image_identity", C.c_uint8 * 32), ("video_identity", C.c_uint8 * 32),
+                ("width", C.c_uint32), ("height", C.c_uint32), ("packets", C.c_uint64),
+                ("intra_packets", C.c_uint64), ("predicted_packets", C.c_uint64), ("maximum_frames", C.c_uint64)]
+
+
+FRAME_SINK = C.CFUNCTYPE(None, C.c_void_p, C.c_int, C.c_uint64, C.POINTER(C.c_uint8), C.c_size_t)
+
+
+def _stream_lib():
+    L = _engine_lib()
+    if getattr(L, "_stream_ready", False):
+        return L
+    vp, ci, i64, sz, u32, u64 = C.c_void_p, C.c_int, C.c_int64, C.c_size_t, C.c_uint32, C.c_uint64
+    for name, args in (("ufb_uf16_write_preamble", [vp, vp, vp, sz]),
+                       ("ufb_uf16_write_sps", [ci, u32, u32, vp, sz]),
+                       ("ufb_uf16_write_packet", [ci, ci, ci, ci, ci, vp, sz, vp, sz]),
+                       ("ufb_uf16_write_uint", [u32, vp, sz])):
+        getattr(L, name).restype = i64
+        getattr(L, name).argtypes = args
+    L.ufb_uf16_read_uint.argtypes = [vp, sz, C.POINTER(sz), C.POINTER(u32)]
+    L.ufb_uf16_read_preamble.argtypes = [vp, sz, C.POINTER(sz), C.POINTER(ci), vp, vp]
+    L.ufb_uf16_next.argtypes = [vp, sz, C.POINTER(sz), C.POINTER(Uf16Nal)]
+    L.ufb_uf16_scan.argtypes = [vp, sz, C.c_char_p, i64, C.POINTER(Uf16Summary)]
+    L.ufb_sha256.argtypes = [vp, sz, vp]
+    L.ufb_prepared_identity.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, C.c_char_p, ci, C.POINTER(C.c_char_p),
+                                        C.POINTER(ci), C.POINTER(ci), C.POINTER(i64), C.POINTER(vp), C.c_char_p]
+    L.ufb_stream_codec_create.restype = vp
+    L.ufb_stream_codec_create.argtypes = [vp, vp, vp, vp]
+    L.ufb_stream_codec_destroy.argtypes = [vp]
+    L.ufb_stream_encode.argtypes = [vp, vp, u64, u32, u32, ci, ci, ci, ci, vp, sz, C.POINTER(sz), C.POINTER(u64)]
+    L.ufb_stream_decode.argtypes = [vp, C.POINTER(vp), C.POINTER(sz), u64, u64, u32, u32, FRAME_SINK, vp, vp,
+                                    C.POINTER(u64), C.POINTER(u64)]
+    L._stream_ready = True
+    return L
+
+
+def _buf(data: bytes):
+    """A ctypes view of bytes (kept alive by the caller's reference)."""
+    a = _np.frombuffer(bytes(data), _np.uint8)
+    return a, (a.ctypes.data if a.size else None)
+
+
+def _written(n: int, out) -> bytes:
+    if n < 0:
+        _check(int(n))
+    return bytes(out[:n])
+
+
+def write_preamble(image_identity: bytes, video_identity: bytes = bytes(32)) -> bytes:
+    """write_preamble of an integer (UF16) stream: 72 bytes."""
+    L = _stream_lib()
+    if len(image_identity) != 32 or len(video_identity) != 32:
+        raise UfbError(-1, "identities are 32 bytes")
+    out = (C.c_uint8 * 72)()
+    return _written(L.ufb_uf16_write_preamble(bytes(image_identity), bytes(video_identity), out, 72), out)
+
+
+def write_sps(sps_id: int, width: int, height: int) -> bytes:
+    L = _stream_lib()
+    out = (C.c_uint8 * 16)()
+    return _written(L.ufb_uf16_write_sps(sps_id, width, height, out, 16), out)
+
+
+def write_packet(nal_type: int, sps_id: int, qp: int, entropy_parallel: int, reset: bool, payload: bytes) -> bytes:
+    L = _stream_lib()
+    keep, p = _buf(payload)
+    cap = len(payload) + 16
+    out = (C.c_uint8 * cap)()
+    return _written(L.ufb_uf16_write_packet(nal_type, sps_id, qp, entropy_parallel, int(bool(reset)), p,
+                                            len(payload), out, cap), out)
+
+
+def write_uint(value: int) -> bytes:
+    L = _stream_lib()
+    out = (C.c_uint8 * 8)()
+    return _written(L.ufb_uf16_write_uint(value, out, 8), out)
+
+
+def read_uint(data: bytes, pos: int = 0):
+    """read_uint_adaptive: (value, next position)."""
+    L = _stream_lib()
+    keep, p = _buf(data)
+    at, v = C.c_size_t(pos), C.c_uint32()
+    _check(L.ufb_uf16_read_uint(p, len(data), C.byref(at), C.byref(v)))
+    return v.value, at.value
+
+
+def read_preamble(data: bytes, pos: int = 0):
+    """read_preamble: ({"integer", "image_identity", "video_identity"}, next position)."""
+    L = _stream_lib()
+    keep, p = _buf(data)
+    at, integer = C.c_size_t(pos), C.c_int()
+    img, vid = (C.c_uint8 * 32)(), (C.c_uint8 * 32)()
+    _check(L.ufb_uf16_read_preamble(p, len(data), C.byref(at), C.byref(integer), img, vid))
+    out = {"integer": bool(integer.value), "image_identity": bytes(32), "video_identity": bytes(32)}
+    if integer.value:
+        out["image_identity"], out["video_identity"] = bytes(img), bytes(vid)
+    return out, at.value
+
+
+def iter_nals(data: bytes, pos: int = 0):
+    """The NAL units from pos on, as dicts (packets carry their payload bytes)."""
+    L = _stream_lib()
+    keep, p = _buf(data)
+    at, nal = C.c_size_t(pos), Uf16Nal()
+    while True:
+        rc = L.ufb_uf16_next(p, len(data), C.byref(at), C.byref(nal))
+        if rc < 0:
+            _check(rc)
+        if rc == 0:
+            return
+        if nal.type == NAL_SPS:
+            yield {"type": NAL_SPS, "sps_id": nal.sps_id, "width": nal.width, "height": nal.height}
+        else:
+            o, n = nal.payload_offset, nal.payload_length
+            yield {"type": nal.type, "sps_id": nal.sps_id, "qp": nal.qp, "entropy_parallel": nal.entropy_parallel,
+                   "reset": bool(nal.reset), "payload": bytes(data[o:o + n])}
+
+
+def scan_bitstream(data: bytes, variant: str, expected_frames=None) -> dict:
+    """scan_bitstream (src/bitstream.cpp:315-358) over a whole stream in memory."""
+    L = _stream_lib()
+    keep, p = _buf(data)
+    s = Uf16Summary()
+    _check(L.ufb_uf16_scan(p, len(data), variant.encode(), -1 if expected_frames is None else int(expected_frames),
+                           C.byref(s)))
+    return {"integer": bool(s.integer), "image_identity": bytes(s.image_identity),
+            "video_identity": bytes(s.video_identity), "width": s.width, "height": s.height,
+            "packets": s.packets, "intra_packets": s.intra_packets, "predicted_packets": s.predicted_packets,
+            "maximum_frames": s.maximum_frames}
+
+
+def sha256(data) -> bytes:
+    L = _stream_lib()
+    a = _np.ascontiguousarray(_np.frombuffer(bytes(data), _np.uint8) if isinstance(data, (bytes, bytearray))
+                              else data).view(_np.uint8)
+    out = (C.c_uint8 * 32)()
+    _check(L.ufb_sha256(a.ctypes.data if a.size else None, a.nbytes, out))
+    return bytes(out)
+
+
+def prepared_identity(tensors: dict, variant: str, source_sha256: str = "", format: str = PREPARED_FORMAT,
+                      arithmetic: str = ARITHMETIC) -> str:
+    """uf::prepared_identity (src/prepared.cpp:64-105): 64 hex digits."""
+    L = _stream_lib()
+    names = sorted(tensors)
+    arrays = [_np.ascontiguousarray(tensors[n]) for n in names]
+    c_names = (C.c_char_p * max(len(names), 1))(*[n.encode() for n in names])
+    dtypes = (C.c_int * max(len(names), 1))(*[_DTYPE_CODES[a.dtype] for a in arrays])
+    ndims = (C.c_int * max(len(names), 1))(*[a.ndim for a in arrays])
+    flat = [int(s) for a in arrays for s in a.shape]
+    shapes = (C.c_int64 * max(len(flat), 1))(*flat)
+    data = (C.c_void_p * max(len(names), 1))(*[a.ctypes.data for a in arrays])
+    out = C.create_string_buffer(65)
+    _check(L.ufb_prepared_identity(format.encode(), arithmetic.encode(), variant.encode(), source_sha256.encode(),
+                                   len(names), c_names, dtypes, ndims, shapes, data, out))
+    return out.value.decode()
+
+
+class StreamCodec:
+    """uf::IntegerCodec over an image codec and an optional video codec of the
+    same batch: B independent UF16 streams coded in lock step."""
+
+    def __init__(self, image: Codec, video: "Codec | None", image_identity: bytes, video_identity: bytes = bytes(32)):
+        L = self.L = _stream_lib()
+        if video is not None and video.batch != image.batch:
+            raise UfbError(-1, "image and video codec batches differ")
+        self.image, self.video, self.batch = image, video, image.batch
+        self._ids = (bytes(image_identity), bytes(video_identity))
+        self.h = L.ufb_stream_codec_create(image.h, video.h if video is not None else None, self._ids[0],
+                                           self._ids[1])
+        if not self.h:
+            raise UfbError(-1, L.ufb_last_error().decode())
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.L.ufb_stream_codec_destroy(self.h)
+            self.h = None
+
+    def encode(self, frames_u8, width, height, qp_i, qp_p, reset_interval=0, intra_period=-1):
+        """frames_u8: uint8 YUV444 [B, T, 3, height, width].  Returns (list of B
+        bitstreams, packet count)."""
+        x = _c(frames_u8, _np.uint8)
+        if x.ndim != 5 or x.shape[0] != self.batch or x.shape[2:] != (3, height, width):
+            raise UfbError(-1, f"frames must be [{self.batch}, T, 3, {height}, {width}] uint8")
+        cap = 4096 + 4 * x[0].size
+        out = _np.empty(self.batch * cap, _np.uint8)
+        lens = (C.c_size_t * self.batch)()
+        packets = C.c_uint64()
+        _check(self.L.ufb_stream_encode(self.h, x.ctypes.data, x.shape[1], width, height, qp_i, qp_p,
+                                        reset_interval, intra_period, out.ctypes.data, cap, lens,
+                                        C.byref(packets)))
+        return [out[i * cap: i * cap + lens[i]].tobytes() for i in range(self.batch)], packets.value
+
+    def decode(self, streams, total_frames, total_packets, width=0, height=0, sink=None):
+        """Decode B streams; sink(stream, frame, yuv_bytes) receives every frame.
+        Returns {"frames", "packets", "sha256": [hex digest per stream]}."""
+        if len(streams) != self.batch:
+            raise UfbError(-1, f"{self.batch} streams required")
+        bufs = [_buf(s) for s in streams]
+        ptrs = (C.c_void_p * self.batch)(*[p for _, p in bufs])
+        lens = (C.c_size_t * self.batch)(*[len(s) for s in streams])
+        digest = (C.c_uint8 * (32 * self.batch))()
+        frames, packets = C.c_uint64(), C.c_uint64()
+        errors = []
+
+        def forward(_user, stream, frame, yuv, n):
+            try:
+                sink(stream, frame, C.string_at(yuv, n))
+            except Exception as e:  # noqa: BLE001 -- re-raised after the C call returns
+                errors.append(e)
+
+        cb = FRAME_SINK(forward) if sink is not None else FRAME_SINK()
+        rc = self.L.ufb_stream_decode(self.h, ptrs, lens, total_frames, total_packets, width, height, cb, None,
+                                      digest, C.byref(frames), C.byref(packets))
+        if errors:
+            raise errors[0]
+        _check(rc)
+        d = bytes(digest)
+        return {"frames": frames.value, "packets": packets.value,
+                "sha256": [d[32 * b: 32 * b + 32].hex() for b in range(self.batch)]}

@@ -2,6 +2,7 @@
 // (uf::Layers::run) and per-stream codec state (uf::IntegerModel).
 #include "uf_b200.h"
 
+#include "capi_engine.h"
 #include "capi_util.h"
 #include "engine.h"
 #include "engine_kernels.h"
@@ -15,48 +16,6 @@
 #include <stdexcept>
 
 using namespace ufb;
-
-struct ufb_model {
-    std::unique_ptr<Model> m;
-    DevicePool pool;
-    cudaStream_t s = nullptr;
-    int* status = nullptr;
-    explicit ufb_model(int device) : pool(device) {}
-};
-
-struct ufb_codec {
-    std::unique_ptr<Codec> c;
-};
-
-namespace {
-
-template <class F>
-int guarded(F&& fn) {
-    clear_error();
-    try {
-        return fn();
-    } catch (const StreamError& e) {
-        return err(UFB_ESTREAM, e.what());
-    } catch (const CudaFailure& e) {
-        return err(UFB_ECUDA, e.what());
-    } catch (const std::invalid_argument& e) {
-        return err(UFB_EINVAL, e.what());
-    } catch (const std::length_error& e) {
-        return err(UFB_ERANGE, e.what());
-    } catch (const std::overflow_error& e) {
-        return err(UFB_ERANGE, e.what());
-    } catch (const std::bad_alloc&) {
-        return err(UFB_ECUDA, "host allocation failed");
-    } catch (const std::exception& e) {
-        return err(UFB_ESTATE, e.what());
-    }
-}
-
-void ck(cudaError_t e, const char* what) {
-    if (e != cudaSuccess) throw CudaFailure(std::string(what) + ": " + cudaGetErrorString(e));
-}
-
-}  // namespace
 
 extern "C" {
 

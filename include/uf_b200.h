@@ -255,6 +255,120 @@ int ufb_codec_stats(ufb_codec* c, int reset, int64_t* launches, int64_t* conv_la
 int ufb_codec_shape_table(ufb_codec* c, char* text, int64_t capacity, int64_t* length);
 
 /* ---------------------------------------------------------------------------
+ * UF16 bitstream container (include/uf/bitstream.hpp:20-107,
+ * src/bitstream.cpp:173-360): host-only, no GPU needed.
+ *
+ *   preamble  "UF16" 01 00 00 00 + image identity (32 B) + video identity (32 B)
+ *   NAL unit  header byte type << 4 | sps_id (type 0 SPS, 1 I packet, 2 P packet)
+ *   SPS       adaptive height, adaptive width
+ *   packet    qp, entropy_parallel << 1 | reset, adaptive payload length, payload
+ *   adaptive  1, 2 or 4 bytes for values below 2^7, 2^14, 2^30
+ *
+ * Writers append at out (capacity bytes) and return the bytes written, or a
+ * negative UFB_E* code (UFB_ERANGE when capacity is too small or a value
+ * exceeds 30 bits, UFB_EINVAL for an invalid SPS or packet).  Readers start at
+ * *pos and advance it; a truncated or malformed stream gives UFB_ESTREAM with
+ * the reference's message ("Truncated UF bitstream", "Unsupported UF NAL
+ * type", ...).
+ * ------------------------------------------------------------------------- */
+#define UFB_NAL_SPS 0
+#define UFB_NAL_INTRA 1
+#define UFB_NAL_PREDICTED 2
+
+typedef struct ufb_uf16_nal {
+    int type;                  /* UFB_NAL_* */
+    int sps_id;                /* 0..15 */
+    uint32_t width, height;    /* SPS */
+    int qp;                    /* packets: 0..255 on the wire */
+    int entropy_parallel;      /* packets: flags >> 1 */
+    int reset;                 /* packets: flags & 1 (reset_feature_memory) */
+    uint64_t payload_offset;   /* packets: payload position in the stream */
+    uint64_t payload_length;
+} ufb_uf16_nal;
+
+typedef struct ufb_uf16_summary {
+    int integer;               /* 1: UF16 preamble present */
+    uint8_t image_identity[32];
+    uint8_t video_identity[32];
+    uint32_t width, height;    /* dimensions of the coded packets */
+    uint64_t packets, intra_packets, predicted_packets;
+    uint64_t maximum_frames;   /* I packets count 1, P packets 8 ("ld": 1) */
+} ufb_uf16_summary;
+
+/* write_preamble of an integer stream (72 bytes). */
+int64_t ufb_uf16_write_preamble(const uint8_t* image_identity, const uint8_t* video_identity, uint8_t* out,
+                                size_t capacity);
+/* write_sps: id < 16, width and height nonzero. */
+int64_t ufb_uf16_write_sps(int id, uint32_t width, uint32_t height, uint8_t* out, size_t capacity);
+/* write_packet: type UFB_NAL_INTRA or UFB_NAL_PREDICTED, sps_id < 16,
+ * 0 <= qp < 256, 0 <= entropy_parallel < 128, length < 2^30. */
+int64_t ufb_uf16_write_packet(int type, int sps_id, int qp, int entropy_parallel, int reset, const uint8_t* payload,
+                              size_t length, uint8_t* out, size_t capacity);
+/* write_uint_adaptive / read_uint_adaptive. */
+int64_t ufb_uf16_write_uint(uint32_t value, uint8_t* out, size_t capacity);
+int ufb_uf16_read_uint(const uint8_t* data, size_t size, size_t* pos, uint32_t* value);
+/* read_preamble: *integer = 0 (nothing consumed) when the stream does not
+ * start with 'U'; identities are written only for an integer stream. */
+int ufb_uf16_read_preamble(const uint8_t* data, size_t size, size_t* pos, int* integer, uint8_t* image_identity,
+                           uint8_t* video_identity);
+/* Next NAL unit (read_optional_header + read_sps / read_packet): returns 1
+ * and fills *nal, or 0 at the clean end of the stream. */
+int ufb_uf16_next(const uint8_t* data, size_t size, size_t* pos, ufb_uf16_nal* nal);
+/* scan_bitstream: variant "ld", "hts" or "htl"; expected_frames < 0 for none. */
+int ufb_uf16_scan(const uint8_t* data, size_t size, const char* variant, int64_t expected_frames,
+                  ufb_uf16_summary* out);
+
+/* SHA-256 of size bytes (OpenSSL EVP, as the reference). */
+int ufb_sha256(const void* data, size_t size, uint8_t* digest32);
+
+/* prepared_identity (src/prepared.cpp:64-105): the content hash of a prepared
+ * model, 64 lowercase hex digits and a terminating zero written to hex65.
+ * The tensor table is the one ufb_model_create takes; format is normally
+ * "dcvc-uf-prepared-v1" and arithmetic "uf-int16-q9-w13-acc64-rna-sat-v1". */
+int ufb_prepared_identity(const char* format, const char* arithmetic, const char* variant, const char* source_sha256,
+                          int count, const char* const* names, const int* dtypes, const int* ndims,
+                          const int64_t* shapes, const void* const* data, char* hex65);
+
+/* ---------------------------------------------------------------------------
+ * Whole streams (uf::IntegerCodec::encode / decode_stream_impl,
+ * src/integer_codec.cpp:215-292, 405-493): an image codec and an optional
+ * video codec of the same batch B code B independent UF16 streams in lock
+ * step.  The stream codec borrows both codecs (destroy it first).
+ * ------------------------------------------------------------------------- */
+typedef struct ufb_stream_codec ufb_stream_codec;
+
+/* Identities: the 32-byte prepared-model identities written to (and required
+ * in) the preamble; video_identity is ignored (zeros) without a video codec. */
+ufb_stream_codec* ufb_stream_codec_create(ufb_codec* image, ufb_codec* video, const uint8_t* image_identity,
+                                          const uint8_t* video_identity);
+void ufb_stream_codec_destroy(ufb_stream_codec* s);
+
+/* IntegerCodec::encode of count frames per stream: frames host uint8 YUV444
+ * [B][count][3][height][width].  Packet structure as the reference: an I packet
+ * first and wherever frame % intra_period == 1 (intra_period 1: all intra;
+ * <= 0: only the first), P packets of 8 frames (the last padded by repeating
+ * its last frame), reset when (frame + 8) % reset_interval == 1.  Stream b is
+ * written at out + b * capacity, its length to lengths[b]; *packets receives
+ * the packet count.  Returns 0 or a UFB_E* code. */
+int ufb_stream_encode(ufb_stream_codec* s, const uint8_t* frames, uint64_t count, uint32_t width, uint32_t height,
+                      int qp_i, int qp_p, int reset_interval, int intra_period, uint8_t* out, size_t capacity,
+                      size_t* lengths, uint64_t* packets);
+
+/* Decoded-frame callback: raw YUV420 frame `frame` of stream `stream`. */
+typedef void (*ufb_frame_sink)(void* user, int stream, uint64_t frame, const uint8_t* yuv, size_t bytes);
+
+/* IntegerCodec::decode_stream_impl of B streams (data[b], sizes[b]): checks
+ * the preamble identities, decodes every packet, hands each frame to sink
+ * (may be NULL) and returns in sha256_out [B][32] the SHA-256 of each
+ * stream's raw YUV420 frames (the archive's decoded_yuv_sha256).  The frame
+ * and packet counts must equal total_frames / total_packets ("Incomplete UF
+ * integer bitstream" otherwise); expected_width / expected_height (0: any)
+ * are the archive metadata's dimensions. */
+int ufb_stream_decode(ufb_stream_codec* s, const uint8_t* const* data, const size_t* sizes, uint64_t total_frames,
+                      uint64_t total_packets, uint32_t expected_width, uint32_t expected_height, ufb_frame_sink sink,
+                      void* user, uint8_t* sha256_out, uint64_t* frames, uint64_t* packets);
+
+/* ---------------------------------------------------------------------------
  * No-allocation convolution (no counterpart in the reference: its uf_conv
  * always allocates its output and temporaries through the caller's allocator).
  * ------------------------------------------------------------------------- */

@@ -4,8 +4,11 @@
   the reference INT16 arithmetic (``uf_oracle.c``).
 * ``Ref`` -- ``_ref/libufref.so``: the reference's own CPU INT16 path
   (``src/int16_ops.cpp``, ``src/layers.cpp``, ``src/integer_model.cpp``,
-  ``src/entropy.cpp``) compiled from its sources by ``Makefile`` target ``ref``,
-  wrapped by ``ref_shim.cpp``.
+  ``src/entropy.cpp``) and UF16 container (``src/bitstream.cpp``) compiled from
+  its sources by ``Makefile`` target ``ref``, wrapped by ``ref_shim.cpp``.
+* ``stream`` -- restatements in Python of the stream-level loops over the
+  compiled reference models (``uf::IntegerCodec``) and of the prepared-model
+  identity.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU arm may
 import this package; the product library never links or calls it.
@@ -237,6 +240,15 @@ class RefOracle:
         L.ufref_rans_set_stream.argtypes = [C.c_void_p, C.c_void_p, C.c_int64]
         L.ufref_rans_decode_z.argtypes = [C.c_void_p, C.c_int64, C.c_int, C.c_int, C.c_void_p]
         L.ufref_rans_decode_y.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]
+        for name, args in (("ufref_bs_write_uint", [C.c_uint32, C.c_void_p, C.c_int64]),
+                           ("ufref_bs_write_preamble", [C.c_char_p, C.c_char_p, C.c_void_p, C.c_int64]),
+                           ("ufref_bs_write_sps", [C.c_int, C.c_uint32, C.c_uint32, C.c_void_p, C.c_int64]),
+                           ("ufref_bs_write_packet", [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_char_p,
+                                                      C.c_int64, C.c_void_p, C.c_int64])):
+            getattr(L, name).restype = C.c_int64
+            getattr(L, name).argtypes = args
+        L.ufref_bs_scan.argtypes = [C.c_char_p, C.c_int64, C.c_char_p, C.c_int64, _i64p, _u8p]
+        L.ufref_bs_parse.argtypes = [C.c_char_p, C.c_int64, _i64p, _i64p, C.c_int64, _i64p, _u8p, C.c_int64]
 
     def _check(self, rc):
         if rc < 0:
@@ -319,6 +331,59 @@ class RefOracle:
 
     def model(self, variant, tensors):
         return RefModel(self, variant, tensors)
+
+    # ---- UF16 container: uf::write_* / read_* / scan_bitstream (src/bitstream.cpp) ----
+
+    def _written(self, n, out):
+        self._check(n)
+        return bytes(out[:n])
+
+    def bs_write_uint(self, v):
+        out = (C.c_uint8 * 8)()
+        return self._written(self.lib.ufref_bs_write_uint(v, out, 8), out)
+
+    def bs_write_preamble(self, image_identity, video_identity):
+        out = (C.c_uint8 * 72)()
+        return self._written(self.lib.ufref_bs_write_preamble(bytes(image_identity), bytes(video_identity), out, 72),
+                             out)
+
+    def bs_write_sps(self, sps_id, width, height):
+        out = (C.c_uint8 * 16)()
+        return self._written(self.lib.ufref_bs_write_sps(sps_id, width, height, out, 16), out)
+
+    def bs_write_packet(self, nal_type, sps_id, qp, entropy_parallel, reset, payload):
+        cap = len(payload) + 16
+        out = (C.c_uint8 * cap)()
+        return self._written(self.lib.ufref_bs_write_packet(nal_type, sps_id, qp, entropy_parallel, int(bool(reset)),
+                                                            bytes(payload), len(payload), out, cap), out)
+
+    def bs_scan(self, data, variant, expected_frames=None):
+        summary, ids = np.zeros(7, np.int64), np.zeros(64, np.uint8)
+        self._check(self.lib.ufref_bs_scan(bytes(data), len(data), variant.encode(),
+                                           -1 if expected_frames is None else int(expected_frames), summary, ids))
+        keys = ("integer", "width", "height", "packets", "intra_packets", "predicted_packets", "maximum_frames")
+        out = {k: int(v) for k, v in zip(keys, summary)}
+        out["integer"] = bool(out["integer"])
+        out["image_identity"], out["video_identity"] = ids[:32].tobytes(), ids[32:].tobytes()
+        return out
+
+    def bs_parse(self, data, max_units=4096):
+        """read_preamble, then every NAL unit: (integer, [unit dicts])."""
+        integer, units = np.zeros(1, np.int64), np.zeros(1, np.int64)
+        records = np.zeros(7 * max_units, np.int64)
+        payloads = np.zeros(max(len(data), 1), np.uint8)
+        self._check(self.lib.ufref_bs_parse(bytes(data), len(data), integer, records, max_units, units, payloads,
+                                            payloads.size))
+        out, used = [], 0
+        for r in records[: 7 * int(units[0])].reshape(-1, 7):
+            t, sid, w, h, qp, flags, n = (int(v) for v in r)
+            if t == 0:
+                out.append({"type": 0, "sps_id": sid, "width": w, "height": h})
+            else:
+                out.append({"type": t, "sps_id": sid, "qp": qp, "entropy_parallel": flags >> 1,
+                            "reset": bool(flags & 1), "payload": payloads[used: used + n].tobytes()})
+                used += n
+        return bool(integer[0]), out
 
     def rans(self, tables):
         return RefRans(self, tables)

@@ -2,30 +2,38 @@
 //
 // C-ABI shim around the reference's own CPU INT16 path, so tests and the
 // bench's CPU arm can run the UNMODIFIED reference sources
-//   src/int16_ops.cpp, src/layers.cpp, src/integer_model.cpp, src/entropy.cpp
+//   src/int16_ops.cpp, src/layers.cpp, src/integer_model.cpp, src/entropy.cpp,
+//   src/bitstream.cpp
 // (compiled in place from the reference checkout by oracle/Makefile) on the
-// same seeded inputs the CUDA engine receives.  Only two symbols the reference
-// declares but whose defining files drag in unrelated subsystems are supplied
-// here: uf::ProcessInterrupt::check() (include/uf/process.hpp:68-79; a no-op,
-// nothing here installs signal handlers) and uf::PreparedModel::tensor()
-// (include/uf/prepared.hpp:19-20; a plain map lookup).
+// same seeded inputs the CUDA engine receives.  Only three symbols the
+// reference declares but whose defining files drag in unrelated subsystems are
+// supplied here: uf::ProcessInterrupt::check() (include/uf/process.hpp:68-79;
+// a no-op, nothing here installs signal handlers), uf::PreparedModel::tensor()
+// (include/uf/prepared.hpp:19-20; a plain map lookup) and
+// uf::python_path_normalize (include/uf/python_path.hpp:25; the identity,
+// reached only by uf::filesize, which nothing here calls).
 //
 // Every entry point returns 0 on success and -1 on a thrown exception, whose
 // message is kept in a thread-local string (ufref_last_error()).
+#include "uf/bitstream.hpp"
 #include "uf/entropy.hpp"
 #include "uf/int16_ops.hpp"
 #include "uf/integer_model.hpp"
 #include "uf/layers.hpp"
 #include "uf/prepared.hpp"
 #include "uf/process.hpp"
+#include "uf/python_path.hpp"
 
 #include <ATen/Parallel.h>
 #include <torch/torch.h>
 
+#include <array>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
+#include <optional>
+#include <sstream>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -37,6 +45,7 @@ const torch::Tensor& PreparedModel::tensor(const std::string& name) const {
     if (it == tensors.end()) throw std::runtime_error("Missing prepared UF tensor: " + name);
     return it->second;
 }
+std::filesystem::path python_path_normalize(const std::filesystem::path& path) { return path; }
 }  // namespace uf
 
 namespace {
@@ -366,6 +375,128 @@ int ufref_rans_decode_y(void* h, const uint8_t* indexes, int64_t n, int8_t* out)
     return guarded([&] {
         const auto v = static_cast<RefRans*>(h)->decoder.decode_y(std::vector<uint8_t>(indexes, indexes + n));
         if (!v.empty()) std::memcpy(out, v.data(), v.size());
+    });
+}
+
+}  // extern "C"
+
+// ---- UF16 container (src/bitstream.cpp) over std::stringstream ----
+
+namespace {
+
+// Copies a writer's output to out; returns the byte count the writer reported.
+template <class F>
+int64_t ref_write(uint8_t* out, int64_t capacity, F&& fn) {
+    int64_t n = -1;
+    std::string bytes;
+    const int rc = guarded([&] {
+        std::ostringstream s(std::ios::binary);
+        n = static_cast<int64_t>(fn(s));
+        bytes = s.str();
+        if (static_cast<int64_t>(bytes.size()) != n) throw std::runtime_error("writer count differs from bytes");
+        if (n > capacity) throw std::length_error("output buffer too small");
+    });
+    if (rc) return -1;
+    if (n) std::memcpy(out, bytes.data(), static_cast<size_t>(n));
+    return n;
+}
+
+std::array<std::uint8_t, 32> id32(const uint8_t* p) {
+    std::array<std::uint8_t, 32> a{};
+    std::memcpy(a.data(), p, 32);
+    return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t ufref_bs_write_uint(uint32_t value, uint8_t* out, int64_t capacity) {
+    return ref_write(out, capacity, [&](std::ostream& s) { return uf::write_uint_adaptive(s, value); });
+}
+
+int64_t ufref_bs_write_preamble(const uint8_t* image_id, const uint8_t* video_id, uint8_t* out, int64_t capacity) {
+    return ref_write(out, capacity, [&](std::ostream& s) {
+        uf::Preamble p;
+        p.integer = true;
+        p.image_identity = id32(image_id);
+        p.video_identity = id32(video_id);
+        const auto before = s.tellp();
+        uf::write_preamble(s, p);
+        return static_cast<size_t>(s.tellp() - before);
+    });
+}
+
+int64_t ufref_bs_write_sps(int id, uint32_t width, uint32_t height, uint8_t* out, int64_t capacity) {
+    return ref_write(out, capacity, [&](std::ostream& s) {
+        return uf::write_sps(s, uf::Sps{static_cast<std::uint8_t>(id), width, height});
+    });
+}
+
+int64_t ufref_bs_write_packet(int type, int sps_id, int qp, int entropy_parallel, int reset, const uint8_t* payload,
+                              int64_t length, uint8_t* out, int64_t capacity) {
+    return ref_write(out, capacity, [&](std::ostream& s) {
+        uf::Packet p{static_cast<uf::NalType>(type), static_cast<std::uint8_t>(sps_id), static_cast<std::uint8_t>(qp),
+                     static_cast<std::uint8_t>(entropy_parallel), reset != 0,
+                     std::vector<std::uint8_t>(payload, payload + length)};
+        return uf::write_packet(s, p);
+    });
+}
+
+// scan_bitstream; summary[0..6] = integer, width, height, packets,
+// intra_packets, predicted_packets, maximum_frames; identities to ids[64].
+int ufref_bs_scan(const uint8_t* data, int64_t size, const char* variant, int64_t expected_frames, int64_t* summary,
+                  uint8_t* ids) {
+    return guarded([&] {
+        std::istringstream s(std::string(reinterpret_cast<const char*>(data), static_cast<size_t>(size)),
+                             std::ios::binary);
+        std::optional<std::uint64_t> expected;
+        if (expected_frames >= 0) expected = static_cast<std::uint64_t>(expected_frames);
+        const auto r = uf::scan_bitstream(s, variant, expected);
+        summary[0] = r.preamble.integer;
+        summary[1] = r.dimensions.width;
+        summary[2] = r.dimensions.height;
+        summary[3] = static_cast<int64_t>(r.packets);
+        summary[4] = static_cast<int64_t>(r.intra_packets);
+        summary[5] = static_cast<int64_t>(r.predicted_packets);
+        summary[6] = static_cast<int64_t>(r.maximum_frames);
+        std::memcpy(ids, r.preamble.image_identity.data(), 32);
+        std::memcpy(ids + 32, r.preamble.video_identity.data(), 32);
+    });
+}
+
+// read_preamble then every NAL unit: per unit 7 values (type, sps_id, width,
+// height, qp, entropy_parallel << 1 | reset, payload length) and the payloads
+// concatenated; returns the unit count in *units.
+int ufref_bs_parse(const uint8_t* data, int64_t size, int64_t* integer, int64_t* records, int64_t max_units,
+                   int64_t* units, uint8_t* payloads, int64_t payload_capacity) {
+    return guarded([&] {
+        std::istringstream s(std::string(reinterpret_cast<const char*>(data), static_cast<size_t>(size)),
+                             std::ios::binary);
+        *integer = uf::read_preamble(s).integer;
+        int64_t n = 0, used = 0;
+        while (const auto h = uf::read_optional_header(s)) {
+            if (n >= max_units) throw std::length_error("too many units");
+            int64_t* r = records + 7 * n;
+            r[0] = static_cast<int64_t>(h->type);
+            r[1] = h->sps_id;
+            r[2] = r[3] = r[4] = r[5] = r[6] = 0;
+            if (h->type == uf::NalType::sps) {
+                const auto sps = uf::read_sps(s, h->sps_id);
+                r[2] = sps.width;
+                r[3] = sps.height;
+            } else {
+                const auto p = uf::read_packet(s, h->type, h->sps_id);
+                r[4] = p.qp;
+                r[5] = p.entropy_parallel << 1 | p.reset_feature_memory;
+                r[6] = static_cast<int64_t>(p.payload.size());
+                if (used + r[6] > payload_capacity) throw std::length_error("payload buffer too small");
+                if (!p.payload.empty()) std::memcpy(payloads + used, p.payload.data(), p.payload.size());
+                used += r[6];
+            }
+            ++n;
+        }
+        *units = n;
     });
 }
 
