@@ -84,7 +84,11 @@ int conv_depthwise_path(const int16_t* x, int n, int c, int h, int w, const int1
     const Act in = make_act(xs.get<uint8_t>(), n, h, w, c, cp);
     const Act ov = make_act(os.get<uint8_t>(), n, h, w, c, cp);
     if (!cuda_ok(nchw_to_split(x, n, c, h, w, 1, in, s), "input layout")) return last_code();
-    if (!cuda_ok(dwconv3x3(in, ov, weight, static_cast<const int16_t*>(bias), s), "depthwise convolution"))
+    int device = 0;
+    if (!cuda_ok(cudaGetDevice(&device), "current device")) return last_code();
+    int* status = device_status(device);
+    if (!status) return last_code();
+    if (!cuda_ok(dwconv3x3(in, ov, weight, static_cast<const int16_t*>(bias), status, s), "depthwise convolution"))
         return last_code();
     if (!cuda_ok(split_to_nchw(ov, 1, out, s), "output layout")) return last_code();
     return UFB_OK;

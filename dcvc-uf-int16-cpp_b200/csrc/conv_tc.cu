@@ -825,8 +825,8 @@ bool act_map(CUtensorMap* map, const Act& v, bool flat, int tw, int th, cuuint32
 void tc_set_max_ctas(int n) { g_max_ctas.store(n > 0 ? n : 0, std::memory_order_relaxed); }
 
 bool tc_encode_map(CUtensorMap* map, void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
-                   const cuuint32_t* box, std::string& err) {
-    return encode(map, base, rank, dims, strides, box, err);
+                   const cuuint32_t* box, std::string& err, CUtensorMapSwizzle swizzle) {
+    return encode(map, base, rank, dims, strides, box, err, swizzle);
 }
 
 size_t tc_weight_bytes(int co, int ci, int kh, int kw, int bn) {

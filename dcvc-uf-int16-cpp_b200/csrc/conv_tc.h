@@ -53,9 +53,10 @@ void tc_lut_window(const int16_t* table, int& start, int& n, int& hi);
 // True when every weight allows the signed split (host data).
 bool tc_signed_split_ok(const int16_t* weight_host, size_t count);
 
-// cuTensorMapEncodeTiled for a byte tensor with the 128-byte swizzle.
+// cuTensorMapEncodeTiled for a byte tensor (128-byte swizzle unless given).
 bool tc_encode_map(CUtensorMap* map, void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
-                   const cuuint32_t* box, std::string& err);
+                   const cuuint32_t* box, std::string& err,
+                   CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // Caps the persistent grid at n CTAs (0: one per SM).  A testing aid: with few
 // CTAs every CTA walks many tiles, which exercises both TMEM accumulator sets.

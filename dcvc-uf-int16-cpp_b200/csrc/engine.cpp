@@ -280,7 +280,7 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
             ev0 = stats_->take_event();
             ck(cudaEventRecord(ev0, s_), "event");
         }
-        ck(dwconv3x3(in.a, out.a, L->weights16, L->bias, s_), "depthwise conv");
+        ck(dwconv3x3(in.a, out.a, L->weights16, L->bias, status_, s_), "depthwise conv");
         if (ev0) {
             cudaEvent_t ev1 = stats_->take_event();
             ck(cudaEventRecord(ev1, s_), "event");

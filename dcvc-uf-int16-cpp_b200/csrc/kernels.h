@@ -13,7 +13,10 @@ cudaError_t split_to_nchw(const Act& in, int f, int16_t* out, cudaStream_t s);
 cudaError_t conv_direct(int16_t* out, const int16_t* x, const int16_t* weight, const void* bias, int bias32, int n,
                         int ci, int co, int h, int w, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw,
                         int groups, cudaStream_t s);
-cudaError_t dwconv3x3(const Act& in, const Act& out, const int16_t* weight, const int16_t* bias, cudaStream_t s);
+// Depthwise 3x3, stride 1, padding 1 on split views (dwconv.cu); a bounded
+// wait that gives up records code 9 in *status.
+cudaError_t dwconv3x3(const Act& in, const Act& out, const int16_t* weight, const int16_t* bias, int* status,
+                      cudaStream_t s);
 cudaError_t ew_add(int16_t* out, const int16_t* a, const int16_t* b, const int16_t* c, const int16_t* d, long long n,
                    cudaStream_t s);
 cudaError_t ew_mul(int16_t* out, const int16_t* x, const int16_t* scale, const long long* xs, const long long* ss,

@@ -93,131 +93,6 @@ __global__ void conv_direct_kernel(int16_t* __restrict__ out, const int16_t* __r
     }
 }
 
-// Depthwise 3x3, stride 1, zero padding 1 on split views (DepthConvBlock dc.2,
-// src/layers.cpp:96; the reference runs it through its scalar `general`
-// kernel, src/cuda/conv.cu:44-60).  A thread owns four channels (one 32-bit
-// word of each byte plane) of kDwCols adjacent output columns and slides down a
-// strip of rows: each input row is read once per thread (warp-coalesced
-// 128-byte rows; neighbouring columns meet again in L1), its byte planes are
-// joined back into int16 values, and it is multiplied into the three output
-// rows it feeds with the 36 weights held in registers, one wide multiply-add
-// per tap into an exact int64 sum (|S| < 2^34).  Two blocks of 256 threads per
-// SM (128 registers) measured fastest: the kernel is latency-bound.
-constexpr int kDwQuads = 32;     // channel quads per block (128 channels)
-constexpr int kDwColThreads = 8; // threads along x per block
-constexpr int kDwRows = 16;      // output rows per strip
-constexpr int kDwThreads = kDwQuads * kDwColThreads;  // 256
-constexpr int kDwCols = 2;       // output columns per thread (two blocks per SM: the best measured layout)
-
-struct DwAcc {
-    int64_t s[kDwCols][4];  // [column][channel]: exact sum of x * w
-};
-
-__device__ __forceinline__ void dw_zero(DwAcc& a) {
-#pragma unroll
-    for (int j = 0; j < kDwCols; ++j)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) a.s[j][c] = 0;
-}
-
-// Adds one input row (pixels x0-1 .. x0+kDwCols as int16 values x) into the
-// accumulator of an output row through weight row w[kx][channel]: one wide
-// multiply-add per tap (|x w| <= 2^30, nine taps need more than 32 bits).
-__device__ __forceinline__ void dw_add(DwAcc& a, const int32_t (&x)[kDwCols + 2][4], const int32_t (&w)[3][4]) {
-#pragma unroll
-    for (int j = 0; j < kDwCols; ++j)
-#pragma unroll
-        for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) a.s[j][c] += static_cast<int64_t>(x[j + kx][c]) * w[kx][c];
-}
-
-__device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], const Act& out, int img, int oy,
-                                         int x0, int c0) {
-#pragma unroll
-    for (int j = 0; j < kDwCols; ++j) {
-        if (x0 + j >= out.w) break;
-        int32_t r[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            // rna(S / 8192) = floor((S + 4096 - [S < 0]) / 8192); |S| < 2^34
-            const int64_t S = a.s[j][c];
-            r[c] = static_cast<int32_t>((S + 4096 + (S >> 63)) >> 13) + b[c];
-        }
-        const uint32_t p0 = pack2_sat(r[0], r[1]), p1 = pack2_sat(r[2], r[3]);
-        const long long px = out.pixel(img, oy, x0 + j);
-        *reinterpret_cast<uint32_t*>(out.lo(px) + c0) = __byte_perm(p0, p1, 0x6420);
-        *reinterpret_cast<uint32_t*>(out.hi(px) + c0) = __byte_perm(p0, p1, 0x7531);
-    }
-}
-
-// Input row iy, pixels x0-1 .. x0+kDwCols, four channels, joined back into
-// int16 values; zero outside the image.
-__device__ __forceinline__ void dw_load_row(const Act& in, int img, int iy, int x0, int c0,
-                                            int32_t (&x)[kDwCols + 2][4]) {
-    const bool row_ok = iy >= 0 && iy < in.h;
-#pragma unroll
-    for (int p = 0; p < kDwCols + 2; ++p) {
-        const int xx = x0 - 1 + p;
-        uint32_t lw = 0, hw = 0;
-        if (row_ok && xx >= 0 && xx < in.w) {
-            const long long px = in.pixel(img, iy, xx);
-            lw = __ldg(reinterpret_cast<const uint32_t*>(in.lo(px) + c0));
-            hw = __ldg(reinterpret_cast<const uint32_t*>(in.hi(px) + c0));
-        }
-        uint32_t q0, q1;  // channels (0, 1) and (2, 3) as int16 pairs
-        join_bytes(lw, hw, q0, q1);
-        x[p][0] = lo16(q0);
-        x[p][1] = hi16(q0);
-        x[p][2] = lo16(q1);
-        x[p][3] = hi16(q1);
-    }
-}
-
-__global__ void __launch_bounds__(kDwThreads, 2)
-dwconv3x3_kernel(Act in, Act out, const int16_t* __restrict__ weight, const int16_t* __restrict__ bias, int ch_blocks,
-                 int col_blocks, int strips) {
-    int bid = blockIdx.x;
-    const int cb = bid % ch_blocks;
-    bid /= ch_blocks;
-    const int xb = bid % col_blocks;
-    bid /= col_blocks;
-    const int sb = bid % strips;
-    const int img = bid / strips;
-    const int c0 = cb * 4 * kDwQuads + 4 * (threadIdx.x % kDwQuads);
-    const int x0 = kDwCols * (xb * kDwColThreads + static_cast<int>(threadIdx.x / kDwQuads));
-    if (c0 >= in.c || x0 >= in.w) return;
-    const int y0 = sb * kDwRows, y1 = y0 + kDwRows < in.h ? y0 + kDwRows : in.h;
-    int32_t w[3][3][4], b[4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-#pragma unroll
-        for (int t = 0; t < 9; ++t) w[t / 3][t % 3][c] = weight[(c0 + c) * 9 + t];
-        b[c] = bias ? bias[c0 + c] : 0;
-    }
-    // output rows iy + 1, iy, iy - 1 take input row iy through weight rows 0, 1, 2
-    DwAcc a0, a1, a2;
-    dw_zero(a0);
-    dw_zero(a1);
-    dw_zero(a2);
-    int32_t xv[kDwCols + 2][4];
-    auto step = [&](DwAcc& next, DwAcc& mid, DwAcc& done, int iy) {
-        dw_load_row(in, img, iy, x0, c0, xv);
-        dw_add(next, xv, w[0]);
-        dw_add(mid, xv, w[1]);
-        dw_add(done, xv, w[2]);
-        if (iy - 1 >= y0) dw_store(done, b, out, img, iy - 1, x0, c0);
-        dw_zero(done);
-    };
-    for (int iy = y0 - 1; iy <= y1; iy += 3) {
-        step(a0, a1, a2, iy);
-        if (iy + 1 > y1) break;
-        step(a2, a0, a1, iy + 1);
-        if (iy + 2 > y1) break;
-        step(a1, a2, a0, iy + 2);
-    }
-}
-
 // ---- elementwise on dense int16 tensors (reference src/cuda/elementwise.cu) ----
 
 __global__ void add_kernel(int16_t* out, const int16_t* a, const int16_t* b, const int16_t* c, const int16_t* d,
@@ -329,20 +204,6 @@ cudaError_t conv_direct(int16_t* out, const int16_t* x, const int16_t* weight, c
     const long long count = static_cast<long long>(n) * co * oh * ow;
     conv_direct_kernel<<<grid_for(count), kBlock, 0, s>>>(out, x, weight, bias, bias32, count, ci, co, h, w, oh, ow, kh,
                                                           kw, sh, sw, ph, pw, groups);
-    return cudaGetLastError();
-}
-
-cudaError_t dwconv3x3(const Act& in, const Act& out, const int16_t* weight, const int16_t* bias, cudaStream_t s) {
-    if (in.c % 4 || in.c != out.c || in.h != out.h || in.w != out.w || in.n != out.n || in.pitch % 16 ||
-        out.pitch % 16 || reinterpret_cast<uintptr_t>(in.base) % 16 || reinterpret_cast<uintptr_t>(out.base) % 16)
-        return cudaErrorInvalidValue;
-    const int ch_blocks = (in.c + 4 * kDwQuads - 1) / (4 * kDwQuads);
-    const int col_blocks = (in.w + kDwCols * kDwColThreads - 1) / (kDwCols * kDwColThreads);
-    const int strips = (in.h + kDwRows - 1) / kDwRows;
-    const long long blocks = static_cast<long long>(ch_blocks) * col_blocks * strips * in.n;
-    if (blocks > INT32_MAX) return cudaErrorInvalidValue;
-    dwconv3x3_kernel<<<static_cast<unsigned>(blocks), kDwThreads, 0, s>>>(in, out, weight, bias, ch_blocks,
-                                                                          col_blocks, strips);
     return cudaGetLastError();
 }
 
