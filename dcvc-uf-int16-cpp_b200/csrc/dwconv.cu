@@ -2,18 +2,20 @@
 // src/layers.cpp:96; the reference runs it through its scalar `general`
 // kernel, src/cuda/conv.cu:44-60).
 //
-// The kernel is bound by HBM: every input and output byte moves once, and the
-// nine multiply-adds per value are cheap next to that.  Persistent CTAs walk
-// output tiles of 128 channels x 16 columns x 8 rows.  Each tile's input window
-// (18 x 10 pixels with the halo, both byte planes, 45 KB) arrives by TMA into
-// one of two shared-memory buffers while the previous tile is computed from
-// the other, so every SM keeps tens of KB of loads in flight; the halo outside
-// the image is the TMA's zero fill, which is exactly the convolution's
-// padding.  A thread owns four channels (one 32-bit word of each plane) of two
-// adjacent output columns and slides down the tile's rows: each input row is
-// read once from shared memory (a warp reads one 128-byte pixel line), joined
-// back into int16 values and multiplied into the three output rows it feeds,
-// one wide multiply-add per tap into an exact int64 sum (|S| < 2^34).
+// Persistent CTAs walk output tiles of 128 channels x 16 columns x 8 rows.
+// Each tile's input window (18 x 10 pixels with the halo, both byte planes,
+// 45 KB) arrives by TMA into one of two shared-memory buffers while the
+// previous tile is computed from the other; the halo outside the image is the
+// TMA's zero fill, which is exactly the convolution's padding.  A thread owns
+// four channels (one 32-bit word of each plane) of two adjacent output columns
+// and slides down the tile's rows, reading each input row once from shared
+// memory (a warp reads one 128-byte pixel line).  The arithmetic stays on the
+// byte planes as they are stored: with x = 256 h + l (l unsigned, h signed
+// bytes), S = 256 sum(h w) + sum(l w), and each partial sum of nine taps fits
+// in 32 bits (|sum(l w)| <= 9 * 255 * 2^15).  Two-way dot-product instructions
+// (16-bit weight pair times two bytes) take taps (0, 1) of a weight row in one
+// instruction and tap 2 in another, and the output is rna(S / 8192) recombined
+// exactly in 32-bit arithmetic, as the tensor-core epilogue does.
 #include "kernels.h"
 
 #include "conv_epi.cuh"
@@ -40,30 +42,79 @@ constexpr uint32_t kBuffer = 2 * kPlane;          // both planes
 constexpr int kThreads = kQuads * kColThreads;    // 256
 constexpr size_t kSmem = 2 * size_t(kBuffer) + 128;  // two buffers, 128-byte alignment slack
 
+// Exact sums of one output row: S = 256 h + l over the two byte planes of the
+// input (l: unsigned low bytes, h: signed high bytes) for [column][channel].
 struct DwAcc {
-    int64_t s[kCols][4];  // [column][channel]: exact sum of x * w
+    int32_t l[kCols][4], h[kCols][4];
 };
 
 __device__ __forceinline__ void dw_zero(DwAcc& a) {
 #pragma unroll
     for (int j = 0; j < kCols; ++j)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) a.s[j][c] = 0;
+        for (int c = 0; c < 4; ++c) a.l[j][c] = a.h[j][c] = 0;
 }
 
-// Adds one input row (window columns 2t .. 2t + 3 as int16 values x) into the
-// accumulator of an output row through weight row w[kx][channel].
-__device__ __forceinline__ void dw_add(DwAcc& a, const int32_t (&x)[kCols + 2][4], const int32_t (&w)[3][4]) {
-#pragma unroll
-    for (int j = 0; j < kCols; ++j)
-#pragma unroll
-        for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) a.s[j][c] += static_cast<int64_t>(x[j + kx][c]) * w[kx][c];
+// Two-way dot products: signed 16-bit pair a times two bytes of b (unsigned
+// or signed) plus c; .lo takes bytes 0 and 1 of b, .hi bytes 2 and 3.
+__device__ __forceinline__ int32_t dp2_lo_u(uint32_t a, uint32_t b, int32_t c) {
+    int32_t d;
+    asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int32_t dp2_hi_u(uint32_t a, uint32_t b, int32_t c) {
+    int32_t d;
+    asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int32_t dp2_lo_s(uint32_t a, uint32_t b, int32_t c) {
+    int32_t d;
+    asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int32_t dp2_hi_s(uint32_t a, uint32_t b, int32_t c) {
+    int32_t d;
+    asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
-// sat(rna(S / 8192) + bias) of two output columns, stored as one 32-bit word
-// per plane (columns outside the image are skipped).
+// One input row in the forms the dot products take: for output column j,
+// pair[j][g] interleaves the bytes of pixels j and j + 1 for channels 2g and
+// 2g + 1 (taps kx = 0, 1), one[j][s] holds pixel j + 2 shifted by 8 s bits
+// (tap kx = 2: channel s in byte 0 and channel s + 2 in byte 2).
+struct DwRow {
+    uint32_t pair[kCols][2], one[kCols][2];
+};
+
+__device__ __forceinline__ void dw_prep(const uint32_t (&v)[kCols + 2], DwRow& r) {
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) {
+        r.pair[j][0] = __byte_perm(v[j], v[j + 1], 0x5140);
+        r.pair[j][1] = __byte_perm(v[j], v[j + 1], 0x7362);
+        r.one[j][0] = v[j + 2];
+        r.one[j][1] = v[j + 2] >> 8;
+    }
+}
+
+// Adds one input row into an output row through weight row ky: wp[c] packs
+// taps (0, 1) of channel c as int16 halves, ws[c] tap 2 with a zero high half.
+__device__ __forceinline__ void dw_add(DwAcc& a, const DwRow& lo, const DwRow& hi, const uint32_t (&wp)[4],
+                                       const uint32_t (&ws)[4]) {
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) {
+        a.l[j][0] = dp2_lo_u(ws[0], lo.one[j][0], dp2_lo_u(wp[0], lo.pair[j][0], a.l[j][0]));
+        a.l[j][1] = dp2_lo_u(ws[1], lo.one[j][1], dp2_hi_u(wp[1], lo.pair[j][0], a.l[j][1]));
+        a.l[j][2] = dp2_hi_u(ws[2], lo.one[j][0], dp2_lo_u(wp[2], lo.pair[j][1], a.l[j][2]));
+        a.l[j][3] = dp2_hi_u(ws[3], lo.one[j][1], dp2_hi_u(wp[3], lo.pair[j][1], a.l[j][3]));
+        a.h[j][0] = dp2_lo_s(ws[0], hi.one[j][0], dp2_lo_s(wp[0], hi.pair[j][0], a.h[j][0]));
+        a.h[j][1] = dp2_lo_s(ws[1], hi.one[j][1], dp2_hi_s(wp[1], hi.pair[j][0], a.h[j][1]));
+        a.h[j][2] = dp2_hi_s(ws[2], hi.one[j][0], dp2_lo_s(wp[2], hi.pair[j][1], a.h[j][2]));
+        a.h[j][3] = dp2_hi_s(ws[3], hi.one[j][1], dp2_hi_s(wp[3], hi.pair[j][1], a.h[j][3]));
+    }
+}
+
+// sat(rna(S / 8192) + bias) of two output columns, S = 256 h + l recombined
+// exactly in 32 bits, stored as one 32-bit word per plane.
 __device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], const Act& out, int img, int oy,
                                          int ox, int c0) {
 #pragma unroll
@@ -71,11 +122,7 @@ __device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], 
         if (ox + j >= out.w) break;
         int32_t r[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            // rna(S / 8192) = floor((S + 4096 - [S < 0]) / 8192)
-            const int64_t S = a.s[j][c];
-            r[c] = static_cast<int32_t>((S + 4096 + (S >> 63)) >> 13) + b[c];
-        }
+        for (int c = 0; c < 4; ++c) r[c] = recombine32(a.l[j][c], a.h[j][c], 0) + b[c];
         const uint32_t p0 = pack2_sat(r[0], r[1]), p1 = pack2_sat(r[2], r[3]);
         const long long px = out.pixel(img, oy, ox + j);
         *reinterpret_cast<uint32_t*>(out.lo(px) + c0) = __byte_perm(p0, p1, 0x6420);
@@ -83,24 +130,21 @@ __device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], 
     }
 }
 
-// Window row r, columns 2t .. 2t + 3, channels 4q .. 4q + 3 from the buffer.
-__device__ __forceinline__ void dw_row(const uint8_t* buf, int r, int t, int q, int32_t (&x)[kCols + 2][4]) {
+// Window row r, columns 2t .. 2t + 3, channels 4q .. 4q + 3 of both planes.
+__device__ __forceinline__ void dw_row(const uint8_t* buf, int r, int t, int q, DwRow& lo, DwRow& hi) {
+    uint32_t lw[kCols + 2], hw[kCols + 2];
 #pragma unroll
     for (int p = 0; p < kCols + 2; ++p) {
         const uint32_t off = (static_cast<uint32_t>(r) * kInW + kCols * t + p) * kLine + 4 * q;
-        const uint32_t lw = *reinterpret_cast<const uint32_t*>(buf + off);
-        const uint32_t hw = *reinterpret_cast<const uint32_t*>(buf + kPlane + off);
-        uint32_t q0, q1;  // channels (0, 1) and (2, 3) as int16 pairs
-        join_bytes(lw, hw, q0, q1);
-        x[p][0] = lo16(q0);
-        x[p][1] = hi16(q0);
-        x[p][2] = lo16(q1);
-        x[p][3] = hi16(q1);
+        lw[p] = *reinterpret_cast<const uint32_t*>(buf + off);
+        hw[p] = *reinterpret_cast<const uint32_t*>(buf + kPlane + off);
     }
+    dw_prep(lw, lo);
+    dw_prep(hw, hi);
 }
 
 __global__ void __launch_bounds__(kThreads, 2)
-dwconv3x3_tma_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t* __restrict__ weight,
+dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t* __restrict__ weight,
                      const int16_t* __restrict__ bias, int channels, int tiles_x, int tiles_y, int images,
                      int total_tiles, int* status) {
     extern __shared__ uint8_t smem_raw[];
@@ -131,7 +175,8 @@ dwconv3x3_tma_kernel(const __grid_constant__ CUtensorMap map, Act out, const int
     __syncthreads();
     if (threadIdx.x == 0 && blockIdx.x < total_tiles) issue(blockIdx.x, 0);
 
-    int32_t w[3][3][4], bv[4];
+    uint32_t wp[3][4], ws[3][4];
+    int32_t bv[4];
     int loaded_cb = -1;
     int i = 0;
     bool next_issued = false;
@@ -152,7 +197,13 @@ dwconv3x3_tma_kernel(const __grid_constant__ CUtensorMap map, Act out, const int
             for (int c = 0; c < 4; ++c) {
                 const bool ok = c0 + c < channels;
 #pragma unroll
-                for (int k = 0; k < 9; ++k) w[k / 3][k % 3][c] = ok ? weight[(c0 + c) * 9 + k] : 0;
+                for (int ky = 0; ky < 3; ++ky) {
+                    const uint32_t w0 = ok ? static_cast<uint16_t>(weight[(c0 + c) * 9 + 3 * ky]) : 0;
+                    const uint32_t w1 = ok ? static_cast<uint16_t>(weight[(c0 + c) * 9 + 3 * ky + 1]) : 0;
+                    const uint32_t w2 = ok ? static_cast<uint16_t>(weight[(c0 + c) * 9 + 3 * ky + 2]) : 0;
+                    wp[ky][c] = w0 | (w1 << 16);
+                    ws[ky][c] = w2;
+                }
                 bv[c] = ok && bias ? bias[c0 + c] : 0;
             }
             loaded_cb = cb;
@@ -172,12 +223,12 @@ dwconv3x3_tma_kernel(const __grid_constant__ CUtensorMap map, Act out, const int
             dw_zero(a0);
             dw_zero(a1);
             dw_zero(a2);
-            int32_t xv[kCols + 2][4];
+            DwRow lo, hi;
             auto step = [&](DwAcc& next, DwAcc& mid, DwAcc& done, int wr) {
-                dw_row(buf, wr, t, q, xv);
-                dw_add(next, xv, w[0]);
-                dw_add(mid, xv, w[1]);
-                dw_add(done, xv, w[2]);
+                dw_row(buf, wr, t, q, lo, hi);
+                dw_add(next, lo, hi, wp[0], ws[0]);
+                dw_add(mid, lo, hi, wp[1], ws[1]);
+                dw_add(done, lo, hi, wp[2], ws[2]);
                 if (wr >= 2 && oy0 + wr - 2 < out.h) dw_store(done, bv, out, img, oy0 + wr - 2, ox, c0);
                 dw_zero(done);
             };
@@ -220,12 +271,12 @@ cudaError_t dwconv3x3(const Act& in, const Act& out, const int16_t* weight, cons
     if (total > INT32_MAX) return cudaErrorInvalidValue;
     // per device; always the same value, so concurrent callers cannot disagree
     const cudaError_t attr =
-        cudaFuncSetAttribute(dwconv3x3_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem));
+        cudaFuncSetAttribute(dwconv3x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem));
     if (attr != cudaSuccess) return attr;
     int device = 0, sms = 148;
     if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     const long long grid = total < 2ll * sms ? total : 2ll * sms;
-    dwconv3x3_tma_kernel<<<static_cast<unsigned>(grid), kThreads, kSmem, s>>>(
+    dwconv3x3_kernel<<<static_cast<unsigned>(grid), kThreads, kSmem, s>>>(
         map, out, weight, bias, in.c, tiles_x, tiles_y, in.n, static_cast<int>(total), status);
     return cudaGetLastError();
 }

@@ -186,6 +186,23 @@ def test_depthwise_split_kernel(ufb, ora, dev, n, c, h, w):
     _status_clean(ufb)
 
 
+@pytest.mark.parametrize("xv,wv", [(-32768, -32768), (32767, -32768), (-32768, 32767), (-1, 4096), (3, 4096),
+                                   (-3, 4096), (255, 32767), (-256, -32768)])
+def test_depthwise_extremes_and_ties(ufb, ora, dev, xv, wv):
+    """Constant inputs and weights at the int16 extremes (the largest partial
+    sums of the byte-plane dot products) and exact half-way cases (S = +-4096
+    mod 8192, rounded away from zero), with and without a saturating bias."""
+    c = 136
+    x = np.full((2, c, 9, 19), xv, np.int16)
+    wd = np.full((c, 1, 3, 3), wv, np.int16)
+    wd[1::3, 0, 0, :] = 0  # some channels see fewer taps
+    wd[2::5, 0, :, 1] = -wd[2::5, 0, :, 1]
+    for b in (np.zeros(c, np.int16), np.full(c, -32768, np.int16), np.arange(c, dtype=np.int16) * 241):
+        got = ufb.conv2d(T(x, dev), T(wd, dev), T(b, dev), 1, 1, 1, 1, c)
+        assert np.array_equal(N(got), ora.conv2d(x, wd, b, 1, 1, c))
+    _status_clean(ufb)
+
+
 def test_warp_matches_oracle(ufb, ora, dev):
     rng = np.random.default_rng(1)
     f = rng.integers(-4096, 4097, (1, 8, 44, 80)).astype(np.int16)
