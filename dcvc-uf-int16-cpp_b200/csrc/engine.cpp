@@ -638,14 +638,14 @@ Tensor Codec::prior(Runner& r, const Tensor* y, const Tensor& params, int qp, bo
         yenc = r.alloc(n, h, w, C);
         if (image) {
             ck(mul_channels(y->a, qrow, yenc.a, r.stream()), "encode multiply");
-    stats_.launches += 1;
+            stats_.launches += 1;
         } else {
             // q_enc = reciprocal(max(q_raw, 256)); encoded_y = multiply(y, q_enc)
             Tensor qenc = r.alloc(n, h, w, C);
             ck(reciprocal_q(qraw.a, qenc.a, r.stream()), "reciprocal");
-    stats_.launches += 1;
+            stats_.launches += 1;
             ck(mul_elementwise(y->a, qenc.a, yenc.a, r.stream()), "encode multiply");
-    stats_.launches += 1;
+            stats_.launches += 1;
         }
     }
     // cat(restored, reduction) lives in one buffer so the adaptors read it in place
@@ -680,7 +680,7 @@ Tensor Codec::prior(Runner& r, const Tensor* y, const Tensor& params, int qp, bo
             ck(prior_indexes(C, h, w, n, part, scales.a, skip_threshold_, d_counts, m_.scale_index(),
                              static_cast<uint8_t*>(d_buf), cap, r.stream()),
                "prior indexes");
-    stats_.launches += 1;
+            stats_.launches += 1;
             sync_and_check();
             for (int b = 0; b < n; ++b)
                 if (h_totals[b])
@@ -701,14 +701,14 @@ Tensor Codec::prior(Runner& r, const Tensor* y, const Tensor& params, int qp, bo
             ck(prior_restore(C, h, w, n, part, scales.a, means.a, skip_threshold_, d_counts, d_sym, cap, restored.a,
                              r.stream()),
                "prior restore");
-    stats_.launches += 1;
+            stats_.launches += 1;
             // the host buffers are reused by the next part: wait for the uploads
             ck(cudaStreamSynchronize(r.stream()), "symbols");
         } else {
             ck(prior_encode(C, h, w, n, part, scales.a, means.a, yenc.a, skip_threshold_, d_counts, m_.scale_index(),
                             static_cast<int16_t*>(d_buf), cap, restored.a, r.stream()),
                "prior encode");
-    stats_.launches += 1;
+            stats_.launches += 1;
             sync_and_check();
             int16_t* hp = reinterpret_cast<int16_t*>(h_buf);
             for (int b = 0; b < n; ++b)
@@ -727,10 +727,10 @@ Tensor Codec::prior(Runner& r, const Tensor* y, const Tensor& params, int qp, bo
     if (image) {
         const ParamTable* q = m_.param("q_scale_y_dec");
         ck(mul_channels(restored.a, q->data + static_cast<size_t>(qp) * q->cols, yhat_t.a, r.stream()), "y_hat");
-    stats_.launches += 1;
+        stats_.launches += 1;
     } else {
         ck(yhat(restored.a, qraw.a, yhat_t.a, r.stream()), "y_hat");
-    stats_.launches += 1;
+        stats_.launches += 1;
     }
     return yhat_t;
 }
@@ -774,7 +774,7 @@ void Codec::emit_frames(const std::vector<Tensor>& frames, uint32_t width, uint3
                 one.base = frames[f].a.base + static_cast<long long>(b) * frames[f].a.img_px * 2 * frames[f].a.pitch;
                 one.n = 1;
                 ck(split_to_nchw(one, 8, d + (static_cast<size_t>(b) * F + f) * per_frame, s_), "frame shuffle");
-    stats_.launches += 1;
+                stats_.launches += 1;
             }
         }
         ck(cudaMemcpyAsync(frames_out, d, bytes, cudaMemcpyDeviceToHost, s_), "frames download");
@@ -792,7 +792,7 @@ void Codec::emit_frames(const std::vector<Tensor>& frames, uint32_t width, uint3
                 ck(raw_frame(one, static_cast<int>(height), static_cast<int>(width),
                              d + (static_cast<size_t>(b) * F + f) * yuv_frame, static_cast<long long>(yuv_frame), s_),
                    "raw frame");
-    stats_.launches += 1;
+                stats_.launches += 1;
             }
         }
         ck(cudaMemcpyAsync(yuv_out, d, bytes, cudaMemcpyDeviceToHost, s_), "yuv download");
@@ -851,7 +851,7 @@ int Codec::compress(const uint8_t* frames, int channels, int h, int w, int qp, b
         if (channels != 3) throw std::invalid_argument("image model takes one frame");
         Tensor x = r.alloc(batch_, hp / 8, wp / 8, 192);
         ck(bytes_to_split_padded(d_in, batch_, channels, h, w, hp, wp, 8, x.a, s_), "frame unshuffle");
-    stats_.launches += 1;
+        stats_.launches += 1;
         const ParamTable* q = m_.param("q_scale_enc");
         y = r.run("enc", {x}, q->data + static_cast<size_t>(qp) * q->cols);
     } else {
@@ -860,10 +860,10 @@ int Codec::compress(const uint8_t* frames, int channels, int h, int w, int qp, b
         Tensor xin = r.alloc(batch_, hp / 8, wp / 8, channels * 64 + context_.a.c);
         Tensor xv = xin.channels(0, channels * 64);
         ck(bytes_to_split_padded(d_in, batch_, channels, h, w, hp, wp, 8, xv.a, s_), "frame unshuffle");
-    stats_.launches += 1;
+        stats_.launches += 1;
         Tensor cv = xin.channels(channels * 64, context_.a.c);
         ck(copy_channels(context_.a, cv.a, s_), "context cat");
-    stats_.launches += 1;
+        stats_.launches += 1;
         const ParamTable* q = m_.param("q_encoder");
         Tensor out = r.simple("encoder.conv1", xin);
         if (m_.has_child("encoder.conv2")) out = r.simple("encoder.conv2", out);
