@@ -384,6 +384,17 @@ class Codec:
             return None
         return out[: int(_np.prod(list(shape)))].reshape(tuple(shape)).copy()
 
+    def state_hash(self, which):
+        """SHA-256 hex of a DPB state as NCHW int16 little-endian bytes (the
+        reference's check-int16 tensor_hash), or None when undefined."""
+        L = _stream_lib()
+        idx = {"reference": 0, "memory": 1, "context": 2}[which]
+        out = (C.c_uint8 * 32)()
+        rc = L.ufb_codec_state_hash(self.h, idx, out)
+        if rc < 0:
+            _check(rc)
+        return None if rc == 1 else bytes(out).hex()
+
     def host_seconds(self):
         return self.L.ufb_codec_host_seconds(self.h)
 
@@ -462,6 +473,10 @@ def _stream_lib():
     L.ufb_sha256.argtypes = [vp, sz, vp]
     L.ufb_prepared_identity.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, C.c_char_p, ci, C.POINTER(C.c_char_p),
                                         C.POINTER(ci), C.POINTER(ci), C.POINTER(i64), C.POINTER(vp), C.c_char_p]
+    L.ufb_codec_state_hash.argtypes = [vp, ci, vp]
+    L.ufb_set_interrupt.argtypes = [ci]
+    L.ufb_set_interrupt.restype = None
+    L.ufb_interrupt_requested.restype = ci
     L.ufb_stream_codec_create.restype = vp
     L.ufb_stream_codec_create.argtypes = [vp, vp, vp, vp]
     L.ufb_stream_codec_destroy.argtypes = [vp]
@@ -566,6 +581,15 @@ def scan_bitstream(data: bytes, variant: str, expected_frames=None) -> dict:
             "video_identity": bytes(s.video_identity), "width": s.width, "height": s.height,
             "packets": s.packets, "intra_packets": s.intra_packets, "predicted_packets": s.predicted_packets,
             "maximum_frames": s.maximum_frames}
+
+
+def set_interrupt(on: bool = True) -> None:
+    """uf::ProcessInterrupt: while set, codec calls stop with UfbError code -6."""
+    _stream_lib().ufb_set_interrupt(int(bool(on)))
+
+
+def interrupt_requested() -> bool:
+    return bool(_stream_lib().ufb_interrupt_requested())
 
 
 def sha256(data) -> bytes:

@@ -6,6 +6,7 @@
 
 #include "capi_util.h"
 #include "engine.h"
+#include "interrupt.h"
 #include "rans.h"
 
 #include <memory>
@@ -33,6 +34,8 @@ inline int guarded(F&& fn) {
     clear_error();
     try {
         return fn();
+    } catch (const Interrupted& e) {
+        return err(UFB_EINTR, e.what());
     } catch (const StreamError& e) {
         return err(UFB_ESTREAM, e.what());
     } catch (const CudaFailure& e) {

@@ -4,6 +4,7 @@
 
 #include "capi_engine.h"
 #include "digest.h"
+#include "interrupt.h"
 #include "stream_codec.h"
 #include "uf16_stream.h"
 
@@ -205,6 +206,25 @@ int ufb_prepared_identity(const char* format, const char* arithmetic, const char
         return 0;
     });
 }
+
+int ufb_codec_state_hash(ufb_codec* c, int which, uint8_t* sha256_32) {
+    return guarded([&] {
+        if (!c || !sha256_32 || which < 0 || which > 2) throw std::invalid_argument("invalid state request");
+        int64_t shape[4];
+        if (!c->c->state_shape(which, shape)) return 1;
+        std::vector<int16_t> host(static_cast<size_t>(shape[0] * shape[1] * shape[2] * shape[3]));
+        c->c->state(which, host.data(), host.size(), shape);
+        Sha256 h;
+        h.update(host.data(), host.size() * sizeof(int16_t));  // little-endian host
+        const auto d = h.finish();
+        std::memcpy(sha256_32, d.data(), d.size());
+        return 0;
+    });
+}
+
+void ufb_set_interrupt(int on) { set_interrupt(on != 0); }
+
+int ufb_interrupt_requested(void) { return interrupt_requested() ? 1 : 0; }
 
 ufb_stream_codec* ufb_stream_codec_create(ufb_codec* image, ufb_codec* video, const uint8_t* image_identity,
                                           const uint8_t* video_identity) {

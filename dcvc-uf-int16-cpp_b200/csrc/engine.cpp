@@ -1,4 +1,5 @@
 #include "engine.h"
+#include "interrupt.h"
 
 #include <cstdio>
 
@@ -804,6 +805,7 @@ void Codec::emit_frames(const std::vector<Tensor>& frames, uint32_t width, uint3
 // IntegerModel::decompress (src/integer_model.cpp:336-359).
 int Codec::decompress(const uint8_t* const* payloads, const size_t* lengths, uint32_t width, uint32_t height, int qp,
                       bool reset, int16_t* frames_out, uint8_t* yuv_out) {
+    check_interrupt();
     DeviceGuard device(m_.device());
     if (qp < 0 || qp >= 64 || !width || !height) throw std::invalid_argument("Unsupported UF integer packet parameters");
     host_seconds_ = 0;
@@ -837,6 +839,7 @@ int Codec::decompress(const uint8_t* const* payloads, const size_t* lengths, uin
 // IntegerModel::compress (src/integer_model.cpp:312-334).
 int Codec::compress(const uint8_t* frames, int channels, int h, int w, int qp, bool reset,
                     std::vector<std::vector<uint8_t>>& payloads, int16_t* frames_out) {
+    check_interrupt();
     DeviceGuard device(m_.device());
     if (qp < 0 || qp >= 64) throw std::invalid_argument("UF QP must be between 0 and 63");
     host_seconds_ = 0;
@@ -910,6 +913,16 @@ int Codec::compress(const uint8_t* frames, int channels, int h, int w, int qp, b
     }
     sync_and_check();
     return static_cast<int>(rec.size());
+}
+
+bool Codec::state_shape(int which, int64_t* shape4) const {
+    const Tensor& t = which == 0 ? reference_ : which == 1 ? memory_ : context_;
+    if (!t.defined()) return false;
+    shape4[0] = t.a.n;
+    shape4[1] = t.a.c;
+    shape4[2] = t.a.h;
+    shape4[3] = t.a.w;
+    return true;
 }
 
 bool Codec::state(int which, int16_t* out, size_t capacity, int64_t* shape4) {

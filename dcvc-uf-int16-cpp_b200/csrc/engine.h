@@ -243,6 +243,8 @@ public:
     // state: 0 reference, 1 memory, 2 context; copies NCHW int16 to host.
     // Returns false when the state is undefined.
     bool state(int which, int16_t* out, size_t capacity, int64_t* shape4);
+    // NCHW shape of a state (false when undefined)
+    bool state_shape(int which, int64_t* shape4) const;
     int frames_per_packet() const { return m_.variant() == "image" ? 1 : 8; }
     double last_host_seconds() const { return host_seconds_; }
     // reference = another codec's last reconstruction (device to device): the

@@ -2,6 +2,7 @@
 #include "stream_codec.h"
 
 #include "digest.h"
+#include "interrupt.h"
 #include "rans.h"  // StreamError
 
 #include <algorithm>
@@ -50,6 +51,7 @@ std::vector<std::vector<uint8_t>> StreamCodec::encode(const uint8_t* frames, uin
     std::vector<std::vector<uint8_t>> payloads;
     uint64_t done = 0, packets = 0;
     while (done < count) {
+        check_interrupt();
         const bool intra = done == 0 || s.intra_period == 1 ||
                            (s.intra_period > 1 && done != 1 && done % static_cast<uint64_t>(s.intra_period) == 1);
         const uint64_t valid = std::min<uint64_t>(intra ? 1 : kChunk, count - done);
@@ -117,6 +119,7 @@ StreamStats StreamCodec::decode(const uint8_t* const* data, const size_t* sizes,
     std::vector<uint8_t> yuv;
     const auto differ = [] { return StreamError("UF streams of one batch differ in packet structure"); };
     for (;;) {
+        check_interrupt();
         uf16::Nal type;
         uint8_t id;
         const bool more = in[0].header(type, id);
@@ -176,8 +179,10 @@ StreamStats StreamCodec::decode(const uint8_t* const* data, const size_t* sizes,
         for (auto& j : jobs) j.get();
         if (sink)
             for (int b = 0; b < B; ++b)
-                for (int f = 0; f < valid; ++f)
+                for (int f = 0; f < valid; ++f) {
+                    check_interrupt();
                     sink(b, stats.frames + f, yuv.data() + (static_cast<size_t>(b) * F + f) * yuv_frame, yuv_frame);
+                }
         stats.frames += valid;
         ++stats.packets;
     }

@@ -34,6 +34,7 @@ extern "C" {
 #define UFB_ECUDA -3    /* CUDA runtime error */
 #define UFB_ESTREAM -4  /* corrupt or truncated entropy-coded stream (std::runtime_error) */
 #define UFB_ESTATE -5   /* call not valid in the current codec state (std::runtime_error) */
+#define UFB_EINTR -6    /* "UF operation interrupted" (ufb_set_interrupt; uf::ProcessInterrupt::check) */
 
 /* Library version (major * 10000 + minor * 100 + patch). */
 int ufb_version(void);
@@ -226,6 +227,19 @@ int ufb_codec_compress(ufb_codec* c, const uint8_t* frames, int channels, int he
 /* DPB state views (IntegerModel::reference/memory/context): which 0, 1, 2.
  * Writes NCHW int16 and its shape; returns 1 when the state is undefined. */
 int ufb_codec_state(ufb_codec* c, int which, int16_t* out, int64_t capacity, int64_t* shape4);
+
+/* SHA-256 of a DPB state tensor (which 0, 1, 2) as NCHW int16 little-endian
+ * bytes -- the tensor_hash of the reference's check-int16 state records
+ * (src/int16_validation.cpp:110-144).  Returns 0, or 1 (digest untouched) when
+ * the state is undefined. */
+int ufb_codec_state_hash(ufb_codec* c, int which, uint8_t* sha256_32);
+
+/* Process-wide cancellation (uf::ProcessInterrupt, include/uf/process.hpp:66-79):
+ * while set, codec compress/decompress calls and the stream encoder / decoder
+ * (between packets and frames) stop with UFB_EINTR "UF operation interrupted".
+ * Lock-free, so a signal handler may call it. */
+void ufb_set_interrupt(int on);
+int ufb_interrupt_requested(void);
 
 /* Seconds the last decompress/compress spent in host entropy coding. */
 double ufb_codec_host_seconds(ufb_codec* c);

@@ -132,3 +132,36 @@ def test_invalid_encode_settings(ufb, syn, setup):
         with pytest.raises(ufb.UfbError) as e:
             sc.encode(video, *args)
         assert "Invalid UF encode settings" in str(e.value)
+
+
+def test_interrupt_stops_coding(ufb, syn, setup):
+    video = syn.synthetic_video(W, H, 9, 51)
+    sc, _ = _engine(ufb, setup)
+    streams, packets = sc.encode(video[None], W, H, 0, 20, 0, -1)
+    dec, _ = _engine(ufb, setup)
+    ufb.set_interrupt(True)
+    try:
+        for call in (lambda: dec.decode(streams, 9, packets), lambda: sc.encode(video[None], W, H, 0, 20, 0, -1)):
+            with pytest.raises(ufb.UfbError) as e:
+                call()
+            assert e.value.code == -6 and str(e.value) == "UF operation interrupted"
+    finally:
+        ufb.set_interrupt(False)
+    assert dec.decode(streams, 9, packets)["frames"] == 9
+
+
+def test_state_hashes_match_reference(ufb, ref, ora, syn, setup):
+    """check-int16 state records: SHA-256 of each DPB tensor's NCHW int16 bytes."""
+    import oracle.stream as st
+    video = syn.synthetic_video(W, H, 9, 61)
+    r = st.RefStreamCodec(ref, ora, setup["img_t"], setup["vid_t"], *setup["ids"], skip_threshold=SKIP)
+    data, packets = r.encode(video, W, H, 0, 20, 0, -1)
+    r.decode(data, 9, packets)
+    sc, (ic, vc) = _engine(ufb, setup)
+    sc.decode([data], 9, packets)
+    for k in ("reference", "memory", "context"):
+        mine, want = vc.state_hash(k), r.video.state(k)
+        assert (mine is None) == (want is None), k
+        if want is not None:
+            assert mine == hashlib.sha256(np.ascontiguousarray(want, "<i2").tobytes()).hexdigest(), k
+            assert mine == hashlib.sha256(vc.state(k).astype("<i2").tobytes()).hexdigest(), k

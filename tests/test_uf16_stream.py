@@ -205,3 +205,13 @@ def test_prepared_identity_names_and_dtypes(ufb):
     }
     assert ufb.prepared_identity(t, "htl", "x") == st.prepared_identity(t, "htl", "x")
     assert ufb.prepared_identity({}, "image") == st.prepared_identity({}, "image")
+
+
+def test_interrupt_flag(ufb):
+    assert not ufb.interrupt_requested()
+    ufb.set_interrupt(True)
+    try:
+        assert ufb.interrupt_requested()
+    finally:
+        ufb.set_interrupt(False)
+    assert not ufb.interrupt_requested()
