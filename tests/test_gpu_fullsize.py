@@ -1,0 +1,72 @@
+"""GPU: size-independent properties at the benchmark's full frame size
+(1920x1088), where the CPU reference is too slow to compare
+against (about 29 minutes per P packet).
+
+* Encode -> decode round trip: the decoder, from the payload bytes alone,
+  reproduces the encoder's reconstruction and decoded-picture buffer exactly
+  (the encoder runs the same reconstruction the decoder does).
+* The YUV420 output equals the C oracle's raw_frame conversion of the decoded
+  int16 frames, and a whole UF16 stream's decoded-YUV SHA-256 equals the hash
+  of the frames handed to the sink.
+"""
+import hashlib
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+W, H = 1920, 1088
+SKIP = 0.2
+
+
+@pytest.fixture(scope="module")
+def full(ufb, syn, dev):
+    img_t, vid_t = syn.prepared("image", 1), syn.prepared("htl", 2)
+    return {"image": ufb.Model("image", img_t), "htl": ufb.Model("htl", vid_t), "img_t": img_t, "vid_t": vid_t,
+            "video": syn.synthetic_video(W, H, 10, 100)}
+
+
+def _codec(ufb, model):
+    c = ufb.Codec(model, 1)
+    c.set_skip_threshold(SKIP)
+    return c
+
+
+@pytest.mark.parametrize("reset", [True, False])
+def test_fullsize_round_trip(ufb, ora, syn, full, reset):
+    video = full["video"]
+    ie, ve = _codec(ufb, full["image"]), _codec(ufb, full["htl"])
+    ip, irec = ie.compress(syn.frames_to_chunk(video[:1]), 0, frames=True)
+    ve.set_reference_from(ie)
+    pp, prec = ve.compress(syn.frames_to_chunk(video[1:9]), 20, reset, frames=True)
+    assert irec.shape == (1, 1, 3, H, W) and prec.shape == (1, 8, 3, H, W)
+
+    idc, vdc = _codec(ufb, full["image"]), _codec(ufb, full["htl"])
+    ifr, iyuv = idc.decompress(ip, W, H, 0, frames=True, yuv=True)
+    assert np.array_equal(ifr, irec)
+    vdc.set_reference_from(idc)
+    pfr, pyuv = vdc.decompress(pp, W, H, 20, reset, frames=True, yuv=True)
+    assert np.array_equal(pfr, prec)
+    for k in ("reference", "memory", "context"):
+        assert vdc.state_hash(k) == ve.state_hash(k), k
+    assert np.array_equal(iyuv[0, 0], ora.raw_frame(ifr[0, 0], H, W))
+    for f in (0, 3, 7):
+        assert np.array_equal(pyuv[0, f], ora.raw_frame(pfr[0, f], H, W)), f
+
+
+def test_fullsize_stream_digest(ufb, full):
+    video = full["video"]
+    ids = (bytes.fromhex(ufb.prepared_identity(full["img_t"], "image")),
+           bytes.fromhex(ufb.prepared_identity(full["vid_t"], "htl")))
+    enc = ufb.StreamCodec(_codec(ufb, full["image"]), _codec(ufb, full["htl"]), *ids)
+    streams, packets = enc.encode(video[None], W, H, 0, 20, 8, -1)
+    assert packets == 3  # I, P of 8, P of 1 padded to 8
+    info = ufb.scan_bitstream(streams[0], "htl", 10)
+    assert (info["width"], info["height"], info["intra_packets"], info["predicted_packets"]) == (W, H, 1, 2)
+    dec = ufb.StreamCodec(_codec(ufb, full["image"]), _codec(ufb, full["htl"]), *ids)
+    seen = []
+    res = dec.decode(streams, 10, packets, W, H, sink=lambda b, f, y: seen.append(y))
+    assert res["frames"] == 10 and len(seen) == 10
+    assert all(len(y) == W * H * 3 // 2 for y in seen)
+    assert res["sha256"][0] == hashlib.sha256(b"".join(seen)).hexdigest()
