@@ -98,23 +98,36 @@ __device__ __forceinline__ void dw_prep(const uint32_t (&v)[kCols + 2], DwRow& r
 
 // Adds one input row into an output row through weight row ky: wp[c] packs
 // taps (0, 1) of channel c as int16 halves, ws[c] tap 2 with a zero high half.
+// The sums start (FRESH: the row's first input row) from l = 4096, the
+// rounding half of rna(S / 8192), and h = 32 bias, which adds the bias to
+// h >> 5 without touching h & 31, so the store needs neither.
+template <bool FRESH>
 __device__ __forceinline__ void dw_add(DwAcc& a, const DwRow& lo, const DwRow& hi, const uint32_t (&wp)[4],
-                                       const uint32_t (&ws)[4]) {
+                                       const uint32_t (&ws)[4], const int32_t (&h0)[4]) {
 #pragma unroll
     for (int j = 0; j < kCols; ++j) {
-        a.l[j][0] = dp2_lo_u(ws[0], lo.one[j][0], dp2_lo_u(wp[0], lo.pair[j][0], a.l[j][0]));
-        a.l[j][1] = dp2_lo_u(ws[1], lo.one[j][1], dp2_hi_u(wp[1], lo.pair[j][0], a.l[j][1]));
-        a.l[j][2] = dp2_hi_u(ws[2], lo.one[j][0], dp2_lo_u(wp[2], lo.pair[j][1], a.l[j][2]));
-        a.l[j][3] = dp2_hi_u(ws[3], lo.one[j][1], dp2_hi_u(wp[3], lo.pair[j][1], a.l[j][3]));
-        a.h[j][0] = dp2_lo_s(ws[0], hi.one[j][0], dp2_lo_s(wp[0], hi.pair[j][0], a.h[j][0]));
-        a.h[j][1] = dp2_lo_s(ws[1], hi.one[j][1], dp2_hi_s(wp[1], hi.pair[j][0], a.h[j][1]));
-        a.h[j][2] = dp2_hi_s(ws[2], hi.one[j][0], dp2_lo_s(wp[2], hi.pair[j][1], a.h[j][2]));
-        a.h[j][3] = dp2_hi_s(ws[3], hi.one[j][1], dp2_hi_s(wp[3], hi.pair[j][1], a.h[j][3]));
+        int32_t l[4], h[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            l[c] = FRESH ? 4096 : a.l[j][c];
+            h[c] = FRESH ? h0[c] : a.h[j][c];
+        }
+        a.l[j][0] = dp2_lo_u(ws[0], lo.one[j][0], dp2_lo_u(wp[0], lo.pair[j][0], l[0]));
+        a.l[j][1] = dp2_lo_u(ws[1], lo.one[j][1], dp2_hi_u(wp[1], lo.pair[j][0], l[1]));
+        a.l[j][2] = dp2_hi_u(ws[2], lo.one[j][0], dp2_lo_u(wp[2], lo.pair[j][1], l[2]));
+        a.l[j][3] = dp2_hi_u(ws[3], lo.one[j][1], dp2_hi_u(wp[3], lo.pair[j][1], l[3]));
+        a.h[j][0] = dp2_lo_s(ws[0], hi.one[j][0], dp2_lo_s(wp[0], hi.pair[j][0], h[0]));
+        a.h[j][1] = dp2_lo_s(ws[1], hi.one[j][1], dp2_hi_s(wp[1], hi.pair[j][0], h[1]));
+        a.h[j][2] = dp2_hi_s(ws[2], hi.one[j][0], dp2_lo_s(wp[2], hi.pair[j][1], h[2]));
+        a.h[j][3] = dp2_hi_s(ws[3], hi.one[j][1], dp2_hi_s(wp[3], hi.pair[j][1], h[3]));
     }
 }
 
-// sat(rna(S / 8192) + bias) of two output columns, S = 256 h + l recombined
-// exactly in 32 bits, stored as one 32-bit word per plane.
+// sat(rna(S / 8192) + bias) of two output columns, stored as one 32-bit word
+// per plane.  With l = 4096 + sum(l w) and h = 32 bias + sum(h w):
+// U = l + 256 (h & 31) and T = (h >> 5) + (U >> 13) = floor((S + 4096) / 8192)
+// + bias, and an exact tie (U % 8192 == 0) with S < 0, i.e. T <= bias, rounds
+// away from zero to T - 1 (the recombination of conv_epi.cuh, recombine32).
 __device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], const Act& out, int img, int oy,
                                          int ox, int c0) {
 #pragma unroll
@@ -122,7 +135,11 @@ __device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], 
         if (ox + j >= out.w) break;
         int32_t r[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) r[c] = recombine32(a.l[j][c], a.h[j][c], 0) + b[c];
+        for (int c = 0; c < 4; ++c) {
+            const int32_t U = a.l[j][c] + ((a.h[j][c] & 31) << 8);
+            const int32_t T = (a.h[j][c] >> 5) + (U >> 13);
+            r[c] = T - static_cast<int32_t>(((U & 8191) == 0) & (T <= b[c]));
+        }
         const uint32_t p0 = pack2_sat(r[0], r[1]), p1 = pack2_sat(r[2], r[3]);
         const long long px = out.pixel(img, oy, ox + j);
         *reinterpret_cast<uint32_t*>(out.lo(px) + c0) = __byte_perm(p0, p1, 0x6420);
@@ -218,19 +235,20 @@ dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t
         const int oy0 = ty * kTileH, ox = tx * kTileW + kCols * t;
         const bool active = c0 < channels && ox < out.w;
         if (active) {
-            // output rows r - 2, r - 1, r take window row r through weight rows 2, 1, 0
+            // output rows r - 2, r - 1, r take window row r through weight rows
+            // 2, 1, 0; row r starts there (the rows -1 and -2 of the first two
+            // steps are never stored)
+            const int32_t h0[4] = {32 * bv[0], 32 * bv[1], 32 * bv[2], 32 * bv[3]};
             DwAcc a0, a1, a2;
-            dw_zero(a0);
             dw_zero(a1);
             dw_zero(a2);
             DwRow lo, hi;
             auto step = [&](DwAcc& next, DwAcc& mid, DwAcc& done, int wr) {
                 dw_row(buf, wr, t, q, lo, hi);
-                dw_add(next, lo, hi, wp[0], ws[0]);
-                dw_add(mid, lo, hi, wp[1], ws[1]);
-                dw_add(done, lo, hi, wp[2], ws[2]);
+                dw_add<true>(next, lo, hi, wp[0], ws[0], h0);
+                dw_add<false>(mid, lo, hi, wp[1], ws[1], h0);
+                dw_add<false>(done, lo, hi, wp[2], ws[2], h0);
                 if (wr >= 2 && oy0 + wr - 2 < out.h) dw_store(done, bv, out, img, oy0 + wr - 2, ox, c0);
-                dw_zero(done);
             };
 #pragma unroll 1
             for (int wr = 0; wr < kInH; wr += 3) {
