@@ -165,3 +165,42 @@ def test_state_hashes_match_reference(ufb, ref, ora, syn, setup):
         if want is not None:
             assert mine == hashlib.sha256(np.ascontiguousarray(want, "<i2").tobytes()).hexdigest(), k
             assert mine == hashlib.sha256(vc.state(k).astype("<i2").tobytes()).hexdigest(), k
+
+
+def test_cli_encode_decode_verify(ufb, syn, setup, tmp_path, capsys):
+    """The command line (encode / decode / verify) over a raw YUV420 file."""
+    import importlib.util
+    import json
+    import os
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("ufb200_cli", os.path.join(root, "dcvc-uf-int16-cpp_b200", "cli.py"))
+    cli = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(cli)
+    img, vid = str(tmp_path / "image.npz"), str(tmp_path / "video.npz")
+    cli.save_model_npz(img, setup["img_t"], "image", "src-image")
+    cli.save_model_npz(vid, setup["vid_t"], "htl", "src-htl")
+    video = syn.synthetic_video(W, H, 10, 81)
+    yuv = tmp_path / "in.yuv"
+    with open(yuv, "wb") as f:
+        for fr in video:
+            f.write(fr[0].tobytes() + fr[1, ::2, ::2].tobytes() + fr[2, ::2, ::2].tobytes())
+    bits, out = str(tmp_path / "video.bin"), str(tmp_path / "out.yuv")
+
+    def run(*argv):
+        rc = cli.main(list(argv))
+        return rc, json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+
+    rc, ev = run("encode", "--image", img, "--video", vid, "--input", str(yuv), "--width", str(W), "--height",
+                 str(H), "--output", bits)
+    assert rc == 0 and ev["frames"] == 10 and ev["packets"] == 3
+    info = ufb.scan_bitstream(open(bits, "rb").read(), "htl", 10)
+    assert info["image_identity"] == setup["ids"][0] and info["video_identity"] == setup["ids"][1]
+    common = ("--image", img, "--video", vid, "--input", bits, "--frames", "10", "--packets", "3")
+    rc, ev = run("decode", *common, "--output", out)
+    assert rc == 0 and ev["decoded_frames"] == 10
+    assert ev["decoded_yuv_sha256"] == hashlib.sha256(open(out, "rb").read()).hexdigest()
+    assert os.path.getsize(out) == 10 * W * H * 3 // 2
+    rc, ev2 = run("verify", *common, "--expect-sha256", ev["decoded_yuv_sha256"])
+    assert rc == 0 and ev2["event"] == "verification_completed"
+    rc, ev3 = run("verify", *common, "--expect-sha256", "0" * 64)
+    assert rc == 1 and ev3["message"] == "Decoded UF pixels differ from archive validation"
