@@ -248,6 +248,17 @@ class RefOracle:
             getattr(L, name).restype = C.c_int64
             getattr(L, name).argtypes = args
         L.ufref_bs_scan.argtypes = [C.c_char_p, C.c_int64, C.c_char_p, C.c_int64, _i64p, _u8p]
+        table = [C.c_char_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_int), C.POINTER(C.c_int),
+                 C.POINTER(C.c_int64), C.POINTER(C.c_void_p)]
+        L.ufref_codec_new.restype = C.c_void_p
+        L.ufref_codec_new.argtypes = [C.c_char_p, C.c_double, C.c_int] + table + table
+        L.ufref_codec_free.argtypes = [C.c_void_p]
+        L.ufref_codec_encode.argtypes = [C.c_void_p, _u8p, C.c_int64, C.c_uint32, C.c_uint32, C.c_int, C.c_int,
+                                         C.c_int, C.c_int, C.c_char_p, _i64p]
+        L.ufref_codec_decode.argtypes = [C.c_void_p, C.c_char_p, C.c_int64, C.c_int64, C.c_int64, C.c_char_p,
+                                         C.c_void_p, C.c_int64, _i64p]
+        L.ufref_raw_frame.restype = C.c_int64
+        L.ufref_raw_frame.argtypes = [_i16p, _i64p, C.c_int64, C.c_int64, _u8p, C.c_int64]
         L.ufref_bs_parse.argtypes = [C.c_char_p, C.c_int64, _i64p, _i64p, C.c_int64, _i64p, _u8p, C.c_int64]
 
     def _check(self, rc):
@@ -388,6 +399,22 @@ class RefOracle:
     def rans(self, tables):
         return RefRans(self, tables)
 
+    def codec(self, image_tensors, image_identity_hex, video_tensors=None, video_identity_hex="",
+              variant="htl", skip_threshold=0.0, threads=0):
+        return RefCodec(self, image_tensors, image_identity_hex, video_tensors, video_identity_hex, variant,
+                        skip_threshold, threads)
+
+    def raw_frame(self, frame, height, width):
+        """uf::IntegerCodec::raw_frame (src/integer_codec.cpp:294-323): int16
+        [1, 3, fh, fw] (or [3, fh, fw]) -> YUV420 bytes of width x height."""
+        frame = _c(frame, np.int16)
+        if frame.ndim == 3:
+            frame = frame[None]
+        cap = width * height + 2 * ((height + 1) // 2) * ((width + 1) // 2)
+        out = np.empty(max(cap, 1), np.uint8)
+        n = self._check(self.lib.ufref_raw_frame(frame, _c(frame.shape, np.int64), width, height, out, out.size))
+        return out[:n].copy()
+
 
 class RefModel:
     """uf::IntegerModel + uf::Layers on torch::kCPU."""
@@ -474,6 +501,69 @@ class RefModel:
         shape = np.zeros(4, np.int64)
         self._check(self.ref.lib.ufref_layers_parameter(self.h, name.encode(), qp, buf, buf.size, shape))
         return buf[: int(np.prod(shape))].reshape(tuple(int(s) for s in shape)).copy()
+
+
+def _tensor_table(tensors: dict):
+    names = sorted(tensors)
+    arrays = [np.ascontiguousarray(tensors[n]) for n in names]
+    flat = [int(s) for a in arrays for s in a.shape]
+    return (arrays,
+            (C.c_char_p * len(names))(*[n.encode() for n in names]),
+            (C.c_int * len(names))(*[DTYPE_CODES[a.dtype] for a in arrays]),
+            (C.c_int * len(names))(*[a.ndim for a in arrays]),
+            (C.c_int64 * max(len(flat), 1))(*flat),
+            (C.c_void_p * len(names))(*[a.ctypes.data for a in arrays]))
+
+
+class RefCodec:
+    """uf::IntegerCodec on torch::kCPU (src/integer_codec.cpp): the reference's
+    own stream encode loop and decode loop (decoded-YUV SHA-256, raw frames)."""
+
+    def __init__(self, ref: RefOracle, image_tensors, image_identity_hex, video_tensors, video_identity_hex,
+                 variant, skip_threshold, threads):
+        self.ref, L = ref, ref.lib
+        img = _tensor_table(image_tensors)
+        if video_tensors is not None:
+            vid = _tensor_table(video_tensors)
+            vargs = [video_identity_hex.encode(), len(vid[0])] + list(vid[1:])
+        else:
+            vargs = [b"", -1, None, None, None, None, None]
+        self.h = L.ufref_codec_new(variant.encode(), float(skip_threshold), int(threads),
+                                   image_identity_hex.encode(), len(img[0]), *img[1:], *vargs)
+        if not self.h:
+            raise RefError(L.ufref_last_error().decode())
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.ref.lib.ufref_codec_free(self.h)
+            self.h = None
+
+    def encode(self, frames_u8, width, height, qp_i, qp_p, reset_interval=32, intra_period=-1):
+        """frames_u8: [T, 3, height, width] uint8 YUV444 -> (archive bytes, frames, packets)."""
+        import tempfile
+        frames_u8 = _c(frames_u8, np.uint8)
+        stats = np.zeros(2, np.int64)
+        with tempfile.TemporaryDirectory() as d:
+            path = os.path.join(d, "video.bin")
+            self.ref._check(self.ref.lib.ufref_codec_encode(self.h, frames_u8, frames_u8.shape[0], width, height,
+                                                            qp_i, qp_p, reset_interval, intra_period,
+                                                            path.encode(), stats))
+            with open(path, "rb") as f:
+                data = f.read()
+        return data, int(stats[0]), int(stats[1])
+
+    def decode(self, data: bytes, total_frames, total_packets, width=None, height=None):
+        """-> (decoded-YUV SHA-256 hex, [raw YUV420 frames] or None, packets)."""
+        digest = C.create_string_buffer(65)
+        stats = np.zeros(3, np.int64)
+        keep = width is not None and height is not None
+        frame_bytes = width * height + 2 * (height // 2) * (width // 2) if keep else 0
+        yuv = np.empty(max(frame_bytes * total_frames, 1), np.uint8) if keep else None
+        self.ref._check(self.ref.lib.ufref_codec_decode(self.h, bytes(data), len(data), total_frames, total_packets,
+                                                        digest, yuv.ctypes.data if keep else None,
+                                                        yuv.size if keep else 0, stats))
+        frames = [yuv[i * frame_bytes:(i + 1) * frame_bytes].copy() for i in range(int(stats[0]))] if keep else None
+        return digest.value.decode(), frames, int(stats[1])
 
 
 class RefRans:

@@ -3,21 +3,26 @@
 // C-ABI shim around the reference's own CPU INT16 path, so tests and the
 // bench's CPU arm can run the UNMODIFIED reference sources
 //   src/int16_ops.cpp, src/layers.cpp, src/integer_model.cpp, src/entropy.cpp,
-//   src/bitstream.cpp
+//   src/bitstream.cpp, src/integer_codec.cpp, src/bitstream_output.cpp,
+//   src/inference_environment.cpp
 // (compiled in place from the reference checkout by oracle/Makefile) on the
-// same seeded inputs the CUDA engine receives.  Only three symbols the
+// same seeded inputs the CUDA engine receives.  Only a few symbols the
 // reference declares but whose defining files drag in unrelated subsystems are
 // supplied here: uf::ProcessInterrupt::check() (include/uf/process.hpp:68-79;
 // a no-op, nothing here installs signal handlers), uf::PreparedModel::tensor()
-// (include/uf/prepared.hpp:19-20; a plain map lookup) and
+// (include/uf/prepared.hpp:19-20; a plain map lookup),
 // uf::python_path_normalize (include/uf/python_path.hpp:25; the identity,
-// reached only by uf::filesize, which nothing here calls).
+// reached only by uf::filesize, which nothing here calls) and the owning
+// descriptor uf::FileDescriptor's destructor, reset and checked close
+// (include/uf/process.hpp:16-32; POSIX close(2) on the owned descriptor), which
+// the bitstream file writer of src/bitstream_output.cpp uses.
 //
 // Every entry point returns 0 on success and -1 on a thrown exception, whose
 // message is kept in a thread-local string (ufref_last_error()).
 #include "uf/bitstream.hpp"
 #include "uf/entropy.hpp"
 #include "uf/int16_ops.hpp"
+#include "uf/integer_codec.hpp"
 #include "uf/integer_model.hpp"
 #include "uf/layers.hpp"
 #include "uf/prepared.hpp"
@@ -36,7 +41,11 @@
 #include <sstream>
 #include <stdexcept>
 #include <string>
+#include <system_error>
 #include <vector>
+
+#include <cerrno>
+#include <unistd.h>
 
 namespace uf {
 void ProcessInterrupt::check() {}
@@ -46,6 +55,17 @@ const torch::Tensor& PreparedModel::tensor(const std::string& name) const {
     return it->second;
 }
 std::filesystem::path python_path_normalize(const std::filesystem::path& path) { return path; }
+FileDescriptor::~FileDescriptor() { reset(); }
+void FileDescriptor::reset(int value) {
+    const int old = value_;
+    value_ = value;
+    if (old >= 0 && old != value) ::close(old);
+}
+void FileDescriptor::close_checked(const std::string& context) {
+    const int fd = value_;
+    value_ = -1;
+    if (fd >= 0 && ::close(fd) != 0) throw std::system_error(errno, std::generic_category(), context);
+}
 }  // namespace uf
 
 namespace {
@@ -498,6 +518,127 @@ int ufref_bs_parse(const uint8_t* data, int64_t size, int64_t* integer, int64_t*
         }
         *units = n;
     });
+}
+
+}  // extern "C"
+
+// ---- uf::IntegerCodec (src/integer_codec.cpp): the reference's own stream
+// encode / decode loops and raw_frame, over in-memory frames ----
+
+namespace {
+
+struct RefCodec {
+    std::unique_ptr<uf::IntegerCodec> codec;
+};
+
+void fill_prepared(uf::PreparedModel& p, const char* variant, const char* identity_hex, int count,
+                   const char* const* names, const int* dtypes, const int* ndims, const int64_t* shapes,
+                   const void* const* data) {
+    p.format = "dcvc-uf-prepared-v1";
+    p.arithmetic = uf::int16::arithmetic_id;
+    p.variant = variant;
+    p.identity = identity_hex;
+    const int64_t* cursor = shapes;
+    for (int i = 0; i < count; ++i) {
+        std::vector<int64_t> shape(cursor, cursor + ndims[i]);
+        cursor += ndims[i];
+        p.tensors[names[i]] = wrap(data[i], shape, dtype_of(dtypes[i]));
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+// IntegerCodec(image, video, variant, kCPU, skip_threshold).  The constructor
+// applies the reference's inference environment (which sets one intra-op
+// thread); `threads` > 0 is applied afterwards.  video_count < 0: no video model.
+void* ufref_codec_new(const char* variant, double skip_threshold, int threads,
+                      const char* image_identity, int image_count, const char* const* image_names,
+                      const int* image_dtypes, const int* image_ndims, const int64_t* image_shapes,
+                      const void* const* image_data,
+                      const char* video_identity, int video_count, const char* const* video_names,
+                      const int* video_dtypes, const int* video_ndims, const int64_t* video_shapes,
+                      const void* const* video_data) {
+    auto handle = std::make_unique<RefCodec>();
+    const int rc = guarded([&] {
+        uf::PreparedModel image, video;
+        fill_prepared(image, "image", image_identity, image_count, image_names, image_dtypes, image_ndims,
+                      image_shapes, image_data);
+        if (video_count >= 0)
+            fill_prepared(video, variant, video_identity, video_count, video_names, video_dtypes, video_ndims,
+                          video_shapes, video_data);
+        handle->codec = std::make_unique<uf::IntegerCodec>(image, video_count >= 0 ? &video : nullptr, variant,
+                                                           torch::kCPU, skip_threshold);
+        if (threads > 0) torch::set_num_threads(threads);
+    });
+    return rc == 0 ? handle.release() : nullptr;
+}
+
+void ufref_codec_free(void* h) { delete static_cast<RefCodec*>(h); }
+
+// IntegerCodec::encode over `frames` ([count, 3, height, width] uint8 YUV444,
+// the FrameSource contract of include/uf/integer_codec.hpp:25-27), written to
+// `output` (a path that must not exist yet).  stats[0..1] = frames, packets.
+int ufref_codec_encode(void* h, const uint8_t* frames, int64_t count, uint32_t width, uint32_t height, int qp_i,
+                       int qp_p, int reset_interval, int intra_period, const char* output, int64_t* stats) {
+    return guarded([&] {
+        const size_t frame_bytes = static_cast<size_t>(width) * height * 3;
+        int64_t next = 0;
+        uf::FrameSource source = [&]() -> std::optional<std::vector<std::uint8_t>> {
+            if (next >= count) return std::nullopt;
+            const uint8_t* f = frames + static_cast<size_t>(next++) * frame_bytes;
+            return std::vector<std::uint8_t>(f, f + frame_bytes);
+        };
+        const auto s = static_cast<RefCodec*>(h)->codec->encode(source, output, width, height, qp_i, qp_p,
+                                                                reset_interval, intra_period);
+        stats[0] = static_cast<int64_t>(s.frames);
+        stats[1] = static_cast<int64_t>(s.packets);
+    });
+}
+
+// IntegerCodec::decode_stream over an in-memory archive.  digest_hex receives
+// the decoded-YUV SHA-256 (65 bytes incl. NUL); when yuv_out is non-null each
+// raw YUV420 frame the FrameSink receives is appended there (capacity bytes).
+int ufref_codec_decode(void* h, const uint8_t* data, int64_t size, int64_t total_frames, int64_t total_packets,
+                       char* digest_hex, uint8_t* yuv_out, int64_t capacity, int64_t* stats) {
+    return guarded([&] {
+        std::istringstream s(std::string(reinterpret_cast<const char*>(data), static_cast<size_t>(size)),
+                             std::ios::binary);
+        int64_t used = 0;
+        uf::FrameSink sink;
+        if (yuv_out) {
+            sink = [&](const std::vector<std::uint8_t>& raw) {
+                if (used + static_cast<int64_t>(raw.size()) > capacity) throw std::length_error("yuv buffer too small");
+                std::memcpy(yuv_out + used, raw.data(), raw.size());
+                used += static_cast<int64_t>(raw.size());
+            };
+        }
+        const auto r = static_cast<RefCodec*>(h)->codec->decode_stream(s, static_cast<std::uint64_t>(total_frames),
+                                                                        static_cast<std::uint64_t>(total_packets),
+                                                                        sink);
+        if (r.decoded_yuv_sha256.size() != 64) throw std::runtime_error("unexpected digest length");
+        std::memcpy(digest_hex, r.decoded_yuv_sha256.c_str(), 65);
+        stats[0] = static_cast<int64_t>(r.frames);
+        stats[1] = static_cast<int64_t>(r.packets);
+        stats[2] = used;
+    });
+}
+
+// IntegerCodec::raw_frame (src/integer_codec.cpp:294-323): an int16 frame
+// tensor [1, 3, fh, fw] -> YUV420 bytes of width x height (Y then U then V).
+int64_t ufref_raw_frame(const int16_t* frame, const int64_t* fs, int64_t width, int64_t height, uint8_t* out,
+                        int64_t capacity) {
+    int64_t n = -1;
+    std::vector<std::uint8_t> raw;
+    const int rc = guarded([&] {
+        raw = uf::IntegerCodec::raw_frame(wrap(frame, {fs[0], fs[1], fs[2], fs[3]}, torch::kInt16), width, height);
+        if (static_cast<int64_t>(raw.size()) > capacity) throw std::length_error("output buffer too small");
+        n = static_cast<int64_t>(raw.size());
+    });
+    if (rc) return -1;
+    if (n) std::memcpy(out, raw.data(), static_cast<size_t>(n));
+    return n;
 }
 
 }  // extern "C"
