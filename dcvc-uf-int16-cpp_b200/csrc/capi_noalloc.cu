@@ -13,7 +13,6 @@
 #include "conv_tc.h"
 #include "kernels.h"
 
-#include <climits>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -55,19 +54,10 @@ extern "C" int ufb_conv2d_noalloc(const int16_t* x, int n, int ci, int h, int w,
                                   int groups, int16_t* out, void* stream) {
     clear_error();
     if (!bias) bias_bits = 0;
-    if (!x || !weight || !out) return err(UFB_EINVAL, "convolution tensors must be non-null");
-    if (sh <= 0 || sw <= 0 || ph < 0 || pw < 0 || groups <= 0) return err(UFB_EINVAL, "invalid convolution geometry");
-    if (ci <= 0 || co <= 0 || kh <= 0 || kw <= 0 || n <= 0 || h <= 0 || w <= 0) return err(UFB_EINVAL, "empty convolution");
-    if (ci % groups || co % groups) return err(UFB_EINVAL, "invalid groups");
-    if (bias_bits != 0 && bias_bits != 16 && bias_bits != 32) return err(UFB_EINVAL, "bias_bits must be 16 or 32");
-    const long long padded_h = static_cast<long long>(h) + 2ll * ph, padded_w = static_cast<long long>(w) + 2ll * pw;
-    if (padded_h < kh || padded_w < kw) return err(UFB_EINVAL, "kernel exceeds input");
-    const long long ohl = (padded_h - kh) / sh + 1, owl = (padded_w - kw) / sw + 1;
-    const long long planes = static_cast<long long>(n) * co;
-    if (planes > INT32_MAX || ohl > INT32_MAX / planes || owl > INT32_MAX / (planes * ohl) ||
-        static_cast<long long>(n) * ci * h * w > INT32_MAX)
-        return err(UFB_ERANGE, "convolution output exceeds indexing bounds");
-    const int oh = static_cast<int>(ohl), ow = static_cast<int>(owl);
+    int oh = 0, ow = 0;
+    // the same argument checks as ufb_conv2d
+    if (!check_conv(x, n, ci, h, w, weight, co, kh, kw, bias_bits, sh, sw, ph, pw, groups, out, oh, ow))
+        return last_code();
     auto s = static_cast<cudaStream_t>(stream);
     // first call on this device: resolve the scratch array's device address
     uint8_t* base = scratch_for_current_device();
@@ -92,6 +82,9 @@ extern "C" int ufb_conv2d_noalloc(const int16_t* x, int n, int ci, int h, int w,
                                    std::to_string(kNoAllocScratchBytes) + " (UFB_NOALLOC_SCRATCH_BYTES)");
     int device = 0;
     if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return last_code();
+    // the pipeline-timeout status word is a device variable too (no allocation)
+    int* status = device_status(device);
+    if (!status) return last_code();
     // Nothing in the scratch must start at zero: the layout conversion and the
     // weight preparation overwrite every byte the convolution reads (channels
     // past ci are outside the TMA tensor extent and read as zero), and the
@@ -106,7 +99,7 @@ extern "C" int ufb_conv2d_noalloc(const int16_t* x, int n, int ci, int h, int w,
     Epilogue epi{};
     epi.bias = bias_bits ? bias : nullptr;
     epi.bias32 = bias_bits == 32;
-    if (conv_tc_run(tw, in, ov, epi, ph, pw, s, device_status(device), msg) != 0) return err(UFB_ECUDA, msg);
+    if (conv_tc_run(tw, in, ov, epi, ph, pw, s, status, msg) != 0) return err(UFB_ECUDA, msg);
     if (!cuda_ok(split_to_nchw(ov, 1, out, s), "output layout")) return last_code();
     return UFB_OK;
 }

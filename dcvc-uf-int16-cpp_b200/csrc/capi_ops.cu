@@ -17,28 +17,6 @@ using namespace ufb;
 
 namespace {
 
-bool check_conv(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
-                int bias_bits, int sh, int sw, int ph, int pw, int groups, int16_t* out, int& oh, int& ow) {
-    if (!x || !weight || !out) return fail(UFB_EINVAL, "convolution tensors must be non-null");
-    if (sh <= 0 || sw <= 0 || ph < 0 || pw < 0 || groups <= 0) return fail(UFB_EINVAL, "invalid convolution geometry");
-    if (ci <= 0 || co <= 0 || kh <= 0 || kw <= 0 || n <= 0 || h <= 0 || w <= 0)
-        return fail(UFB_EINVAL, "empty convolution");
-    if (ci % groups || co % groups) return fail(UFB_EINVAL, "invalid groups");
-    if (bias_bits != 16 && bias_bits != 32 && bias_bits != 0) return fail(UFB_EINVAL, "bias_bits must be 16 or 32");
-    const long long padded_h = static_cast<long long>(h) + 2ll * ph, padded_w = static_cast<long long>(w) + 2ll * pw;
-    if (padded_h < kh || padded_w < kw) return fail(UFB_EINVAL, "kernel exceeds input");
-    if (static_cast<long long>(ci / groups) * kh * kw >= (INT64_MAX / 1073741824LL) - 1)
-        return fail(UFB_ERANGE, "dot product overflow");
-    const long long ohl = (padded_h - kh) / sh + 1, owl = (padded_w - kw) / sw + 1;
-    const long long planes = static_cast<long long>(n) * co;
-    if (planes > INT32_MAX || ohl > INT32_MAX / planes || owl > INT32_MAX / (planes * ohl) ||
-        static_cast<long long>(n) * ci * h * w > INT32_MAX)
-        return fail(UFB_ERANGE, "convolution output exceeds indexing bounds");
-    oh = static_cast<int>(ohl);
-    ow = static_cast<int>(owl);
-    return true;
-}
-
 int conv_direct_path(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
                      const void* bias, int bias_bits, int sh, int sw, int ph, int pw, int groups, int oh, int ow,
                      int16_t* out, cudaStream_t s) {
@@ -58,6 +36,8 @@ int conv_tc_path(const int16_t* x, int n, int ci, int h, int w, const int16_t* w
     StreamBuffer wp(tc_weight_bytes(co, ci, kh, kw, 128), s);
     StreamBuffer os(static_cast<size_t>(n) * oh * ow * 2 * cop, s);
     if (!xs.ok() || !wp.ok() || !os.ok()) return err(UFB_ECUDA, "cudaMallocAsync failed for convolution scratch");
+    int* status = device_status(device);
+    if (!status) return last_code();
     TcWeights tw;
     std::string msg;
     // unsigned byte split: valid for any weights, needs no host inspection
@@ -68,7 +48,7 @@ int conv_tc_path(const int16_t* x, int n, int ci, int h, int w, const int16_t* w
     Epilogue epi{};
     epi.bias = bias_bits ? bias : nullptr;
     epi.bias32 = bias_bits == 32;
-    if (conv_tc_run(tw, in, ov, epi, ph, pw, s, device_status(device), msg) != 0) return err(UFB_ECUDA, msg);
+    if (conv_tc_run(tw, in, ov, epi, ph, pw, s, status, msg) != 0) return err(UFB_ECUDA, msg);
     if (!cuda_ok(split_to_nchw(ov, 1, out, s), "output layout")) return last_code();
     return UFB_OK;
 }
@@ -288,6 +268,8 @@ int ufb_conv2d_split(const uint8_t* x, int n, int ci, int h, int w, int x_pitch,
     if (static_cast<long long>(ci) * kh * kw > kTcMaxReduction) return err(UFB_ERANGE, "reduction exceeds 8192");
     int device = 0;
     if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return last_code();
+    int* status = device_status(device);
+    if (!status) return last_code();
     TcWeights tw;
     std::string msg;
     if (!tc_describe(tw, co, ci, kh, kw, false, 128, const_cast<uint8_t*>(planes), msg)) return err(UFB_ECUDA, msg);
@@ -296,7 +278,7 @@ int ufb_conv2d_split(const uint8_t* x, int n, int ci, int h, int w, int x_pitch,
     Epilogue epi{};
     epi.bias = bias_bits ? bias : nullptr;
     epi.bias32 = bias_bits == 32;
-    if (conv_tc_run(tw, in, ov, epi, pad_h, pad_w, static_cast<cudaStream_t>(stream), device_status(device), msg))
+    if (conv_tc_run(tw, in, ov, epi, pad_h, pad_w, static_cast<cudaStream_t>(stream), status, msg))
         return err(UFB_EINVAL, msg);
     return UFB_OK;
 }

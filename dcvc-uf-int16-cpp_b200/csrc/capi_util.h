@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <cstdint>
 #include <string>
 
 namespace ufb {
@@ -17,8 +18,15 @@ int last_code();
 const char* last_message();
 bool cuda_ok(cudaError_t e, const char* what);     // records UFB_ECUDA on failure
 
-// Per-device kernel status word (pipeline timeouts), allocated on first use.
+// Per-device kernel status word (pipeline timeouts): a device variable of the
+// library resolved on first use (status.cu); null with the error recorded when
+// the address cannot be resolved.
 int* device_status(int device);
+
+// Argument checks of uf_conv (src/cuda/conv.cu:65-83) shared by every
+// convolution entry point; fills the output extent.
+bool check_conv(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
+                int bias_bits, int sh, int sw, int ph, int pw, int groups, const int16_t* out, int& oh, int& ow);
 
 inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
 

@@ -61,12 +61,14 @@ extern "C" int ufb_probe_i8_peak(int iters, int ctas, void* stream, int64_t* int
     if (iters <= 0 || ctas <= 0) return err(UFB_EINVAL, "iters and ctas must be positive");
     int device = 0;
     if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return last_code();
+    int* status = device_status(device);
+    if (!status) return last_code();
     // 120 KB keeps one probe CTA per SM
     const int smem = 120 * 1024;
     if (!cuda_ok(cudaFuncSetAttribute(i8_peak_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                  "smem attribute"))
         return last_code();
-    i8_peak_kernel<<<ctas, 128, smem, static_cast<cudaStream_t>(stream)>>>(iters, device_status(device));
+    i8_peak_kernel<<<ctas, 128, smem, static_cast<cudaStream_t>(stream)>>>(iters, status);
     if (!cuda_ok(cudaGetLastError(), "peak probe launch")) return last_code();
     if (int8_ops) *int8_ops = static_cast<int64_t>(ctas) * iters * 4 * 128 * 256 * 32 * 2;
     return UFB_OK;

@@ -4,11 +4,9 @@
   the reference builds its header with Python's compact, sorted, ASCII-only
   ``json.dumps`` conventions, which this function uses directly, and hashes
   each tensor's descriptor and little-endian bytes in name order.
-* ``RefStreamCodec`` restates ``uf::IntegerCodec::encode`` and
-  ``decode_stream_impl`` (src/integer_codec.cpp:215-292, 405-493) over the
-  reference's own compiled ``IntegerModel`` (``RefModel``) and container writers
-  and reader (``RefOracle.bs_*``, src/bitstream.cpp); frames are converted to
-  YUV420 with the C oracle's ``raw_frame`` (src/integer_codec.cpp:294-323).
+* ``RefStreamCodec`` runs the reference's own ``uf::IntegerCodec`` encode and
+  decode loops (src/integer_codec.cpp:215-493, compiled from its sources into
+  oracle/_ref) over in-memory frames and archives.
 """
 from __future__ import annotations
 
@@ -22,7 +20,6 @@ ARITHMETIC = "uf-int16-q9-w13-acc64-rna-sat-v1"
 _TORCH_DTYPES = {np.dtype(np.int16): "torch.int16", np.dtype(np.uint8): "torch.uint8",
                  np.dtype(np.int32): "torch.int32", np.dtype(np.int8): "torch.int8",
                  np.dtype(np.int64): "torch.int64"}
-CHUNK = 8
 
 
 def _compact(value) -> bytes:
@@ -41,77 +38,30 @@ def prepared_identity(tensors: dict, variant: str, source_sha256: str = "", form
 
 
 class RefStreamCodec:
-    """uf::IntegerCodec for one stream over the reference's CPU models."""
+    """uf::IntegerCodec for one stream: the reference's own encode loop and
+    decode loop (src/integer_codec.cpp:215-292, 405-493) compiled from its
+    sources (``RefOracle.codec``), including its decoded-YUV SHA-256 over
+    ``IntegerCodec::raw_frame`` (src/integer_codec.cpp:294-323)."""
 
     def __init__(self, ref, ora, image_tensors: dict, video_tensors: dict | None, image_identity: bytes,
-                 video_identity: bytes = bytes(32), skip_threshold: float = 0.0):
-        self.ref, self.ora = ref, ora
-        self.image = ref.model("image", image_tensors)
-        self.video = ref.model("htl", video_tensors) if video_tensors is not None else None
-        for m in (self.image, self.video):
-            if m is not None:
-                m.set_skip_threshold(skip_threshold)
-        self.ids = (bytes(image_identity), bytes(video_identity) if video_tensors is not None else bytes(32))
+                 video_identity: bytes = bytes(32), skip_threshold: float = 0.0, threads: int = 0):
+        self.args = (image_tensors, bytes(image_identity).hex(), video_tensors,
+                     bytes(video_identity).hex() if video_tensors is not None else "", "htl", skip_threshold,
+                     threads)
+        self.ref = ref
+        self.size = None
 
     def encode(self, frames_u8, width, height, qp_i, qp_p, reset_interval=0, intra_period=-1):
         """frames_u8: [T, 3, height, width] uint8 YUV444 -> (bitstream, packets)."""
-        if width % 2 or height % 2 or not 0 <= qp_i < 64 or not 0 <= qp_p < 64 or (
-                intra_period > 1 and intra_period % CHUNK):
-            raise ValueError("Invalid UF encode settings")
-        r = self.ref
-        out = r.bs_write_preamble(*self.ids) + r.bs_write_sps(0, width, height)
-        count, packets, total = 0, 0, len(frames_u8)
-        while count < total:
-            intra = count == 0 or intra_period == 1 or (intra_period > 1 and count != 1 and
-                                                        count % intra_period == 1)
-            valid = min(1 if intra else CHUNK, total - count)
-            chunk = [frames_u8[count + i] for i in range(valid)]
-            if not intra:
-                chunk += [chunk[-1]] * (CHUNK - valid)
-            x = self.ora.from_bytes(np.concatenate(chunk, 0)[None])
-            reset = not intra and reset_interval > 0 and (count + CHUNK) % reset_interval == 1
-            if intra:
-                payload, rec = self.image.compress(x, qp_i)
-                if self.video is not None:
-                    self.video.add_ref_feature_from_frame(rec[0])
-            else:
-                payload, _ = self.video.compress(x, qp_p, reset)
-            out += r.bs_write_packet(1 if intra else 2, 0, qp_i if intra else qp_p, 1, reset, payload)
-            count += valid
-            packets += 1
-        return out, packets
+        data, _, packets = self.ref.codec(*self.args).encode(frames_u8, width, height, qp_i, qp_p, reset_interval,
+                                                             intra_period)
+        self.size = (width, height)
+        return data, packets
 
     def decode(self, data: bytes, total_frames: int, total_packets: int):
         """-> (sha256 hex of the raw YUV420 frames, [frames], packets)."""
         integer, units = self.ref.bs_parse(data)
-        ids = data[8:40], data[40:72]
-        if not integer or (bytes(ids[0]), bytes(ids[1])) != self.ids:
-            raise ValueError("UF integer runtime/prepared-model identity mismatch")
-        sps, digest, yuv, packets, first = {}, hashlib.sha256(), [], 0, True
-        for u in units:
-            if u["type"] == 0:
-                sps[u["sps_id"]] = (u["width"], u["height"])
-                continue
-            if u["sps_id"] not in sps or len(yuv) >= total_frames:
-                raise ValueError("Unexpected UF packet or unknown SPS")
-            w, h = sps[u["sps_id"]]
-            intra = u["type"] == 1
-            if first and not intra:
-                raise ValueError("UF stream must start with an I packet")
-            first = False
-            if intra:
-                frames = self.image.decompress(u["payload"], w, h, u["qp"])
-                if self.video is not None:
-                    self.video.add_ref_feature_from_frame(frames[0])
-            else:
-                frames = self.video.decompress(u["payload"], w, h, u["qp"], u["reset"])
-            for f in frames:
-                if len(yuv) == total_frames:
-                    break
-                raw = self.ora.raw_frame(f[0], h, w)
-                digest.update(raw.tobytes())
-                yuv.append(raw)
-            packets += 1
-        if len(yuv) != total_frames or packets != total_packets:
-            raise ValueError("Incomplete UF integer bitstream")
-        return digest.hexdigest(), yuv, packets
+        sps = [u for u in units if u["type"] == 0]
+        width, height = (sps[0]["width"], sps[0]["height"]) if sps else self.size
+        digest, yuv, packets = self.ref.codec(*self.args).decode(data, total_frames, total_packets, width, height)
+        return digest, yuv, packets

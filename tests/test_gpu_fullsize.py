@@ -1,12 +1,13 @@
 """GPU: size-independent properties at the benchmark's full frame size
-(1920x1088), where the CPU reference is too slow to compare
-against (about 29 minutes per P packet).
+(1920x1088), beside the reference-pinned digests of
+test_gpu_golden.py (a reference P-packet decode at this size takes over half
+an hour of CPU, so these round trips are checked live instead).
 
 * Encode -> decode round trip: the decoder, from the payload bytes alone,
   reproduces the encoder's reconstruction and decoded-picture buffer exactly
   (the encoder runs the same reconstruction the decoder does).
-* The YUV420 output equals the C oracle's raw_frame conversion of the decoded
-  int16 frames, and a whole UF16 stream's decoded-YUV SHA-256 equals the hash
+* The YUV420 output equals the reference's own IntegerCodec::raw_frame
+  conversion of the decoded int16 frames, and a whole UF16 stream's decoded-YUV SHA-256 equals the hash
   of the frames handed to the sink.
 """
 import hashlib
@@ -34,7 +35,7 @@ def _codec(ufb, model):
 
 
 @pytest.mark.parametrize("reset", [True, False])
-def test_fullsize_round_trip(ufb, ora, syn, full, reset):
+def test_fullsize_round_trip(ufb, ref, syn, full, reset):
     video = full["video"]
     ie, ve = _codec(ufb, full["image"]), _codec(ufb, full["htl"])
     ip, irec = ie.compress(syn.frames_to_chunk(video[:1]), 0, frames=True)
@@ -50,9 +51,9 @@ def test_fullsize_round_trip(ufb, ora, syn, full, reset):
     assert np.array_equal(pfr, prec)
     for k in ("reference", "memory", "context"):
         assert vdc.state_hash(k) == ve.state_hash(k), k
-    assert np.array_equal(iyuv[0, 0], ora.raw_frame(ifr[0, 0], H, W))
+    assert np.array_equal(iyuv[0, 0], ref.raw_frame(ifr[0, 0], H, W))
     for f in (0, 3, 7):
-        assert np.array_equal(pyuv[0, f], ora.raw_frame(pfr[0, f], H, W)), f
+        assert np.array_equal(pyuv[0, f], ref.raw_frame(pfr[0, f], H, W)), f
 
 
 def test_fullsize_stream_digest(ufb, full):

@@ -111,10 +111,16 @@ def test_image_compress_decompress_parity(ufb, ora, ref, syn, models, skip):
 
 
 @pytest.mark.parametrize("reset", [True, False])
-def test_video_p_packet_parity(ufb, ora, ref, syn, models, reset):
+@pytest.mark.parametrize("size", [(64, 64), (128, 128)])
+def test_video_p_packet_parity(ufb, ora, ref, syn, models, reset, size):
+    """At 128x128 a stream's latent holds 256 x 8 x 8 = 16384 positions, four
+    4096-position chunks of the spatial-prior kernels, so the per-chunk counts,
+    their per-stream scan and the emit offsets are compared with the
+    reference's index_select order (src/integer_model.cpp:202-293)."""
+    W, H = size
     mine, _ = models["htl"]
     vid_t = syn.prepared("htl", 2)
-    video = _frames(syn, 17)
+    video = _frames(syn, 17, w=W, h=H)
     iframe = ora.from_bytes(syn.frames_to_chunk(video[:1]))
     # the I frame reconstruction from the reference image path seeds both DPBs
     ri = ref.model("image", syn.prepared("image", 1))
@@ -150,7 +156,7 @@ def test_video_p_packet_parity(ufb, ora, ref, syn, models, reset):
     assert len(want) == 8
     for f in range(8):
         assert np.array_equal(got[0, f], want[f][0]), f"frame {f}"
-        assert np.array_equal(yuv[0, f], ora.raw_frame(want[f][0], H, W)), f"yuv {f}"
+        assert np.array_equal(yuv[0, f], ref.raw_frame(want[f][0], H, W)), f"yuv {f}"
     _same_states(dec, dec_ref)
 
 

@@ -105,3 +105,33 @@ def test_warp_close_to_float_semantics(ora):
     flow = flow.astype(np.int16)
     diff = np.abs(ora.warp(f, flow).astype(np.float64) - ora.warp_float(f, flow))
     assert diff.max() <= 1.0
+
+
+@pytest.mark.parametrize("size", [(72, 80), (70, 78), (352, 626)])
+def test_raw_frame_vs_reference_codec(ora, ref, size):
+    """The C restatement of raw_frame equals the reference's own
+    IntegerCodec::raw_frame (src/integer_codec.cpp:294-323) on cropped, padded
+    and saturating frames, including every rounding tie of the luma formula."""
+    h, w = size
+    rng = np.random.default_rng(h * 1000 + w)
+    fh, fw = (h + 15) // 16 * 16, (w + 15) // 16 * 16
+    frame = rng.integers(-1400, 1400, (1, 3, fh, fw)).astype(np.int16)
+    frame.reshape(-1)[: 65536] = np.arange(-32768, 32768, dtype=np.int64).astype(np.int16)[: min(65536, frame.size)]
+    want = ref.raw_frame(frame, h, w)
+    assert np.array_equal(ora.raw_frame(frame[0], h, w).reshape(-1), want)
+
+
+def test_reference_codec_stream_roundtrip(ref, syn):
+    """The reference's IntegerCodec decode loop over its own encoded archive:
+    the decoded-YUV SHA-256 it returns is the hash of the frames its sink saw."""
+    import hashlib
+
+    import oracle.stream as st
+    img_t, vid_t = syn.prepared("image", 1), syn.prepared("htl", 2)
+    ii, vi = st.prepared_identity(img_t, "image", "a"), st.prepared_identity(vid_t, "htl", "b")
+    video = syn.synthetic_video(64, 64, 9, 5)
+    data, frames, packets = ref.codec(img_t, ii, vid_t, vi, "htl", 0.2).encode(video, 64, 64, 0, 20, 8, -1)
+    assert (frames, packets) == (9, 2)
+    digest, yuv, p = ref.codec(img_t, ii, vid_t, vi, "htl", 0.2).decode(data, 9, 2, 64, 64)
+    assert p == 2 and len(yuv) == 9
+    assert hashlib.sha256(b"".join(y.tobytes() for y in yuv)).hexdigest() == digest
