@@ -11,6 +11,12 @@ Workloads
           every sequence of the rank completely (I packet, then the 4 P packets),
           host rANS included.  Unit: decoded frames/s (whole job).
   conv    BASELINE config 1 batched: 64 copies of the 1x64x88x160 int16 3x3 conv.
+  warp    BASELINE config 2: the fixed-point backward bilinear warp of int16
+          features 1x64x176x320 by an int16 Q9 flow (N(0, 4^2) px per pixel plus a
+          (3.25, -1.5) px translation, seed 1).  Unit: warps/s; roofline: HBM
+          bytes (7.21 MB features + 0.225 MB flow + 7.21 MB output per call) over
+          the measured copy bandwidth; L2 (126 MB) is flushed by a 256 MB write
+          before every timed call.
 
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
 torch.cuda.synchronize(), device time from CUDA events on the stream the
@@ -56,7 +62,7 @@ def parse():
     p.add_argument("--steps", type=int, default=2)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--workload", default="decode", choices=["decode", "conv"])
+    p.add_argument("--workload", default="decode", choices=["decode", "conv", "warp"])
     p.add_argument("--seqs", type=int, default=SEQS,
                    help="sequences in the job (default: BASELINE config 5's 64); smaller values are for profiling")
     p.add_argument("--shapes", action="store_true", help="print per launch shape convolution time to stderr")
@@ -121,11 +127,13 @@ def barrier(world):
 
 
 def reduce_over_ranks(value, world, device, op):
+    """Max / sum of a host scalar over the ranks.  The ranks share no data: the
+    group is gloo over host memory, so a multi-GPU run makes no NCCL call."""
     if world == 1:
         return value
     import torch
     import torch.distributed as dist
-    t = torch.tensor([value], dtype=torch.float64, device=device)
+    t = torch.tensor([value], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
     return float(t.item())
 
@@ -183,7 +191,8 @@ def shard(rank, world, seqs):
 def encode_sequences(ufb, syn, mi, mv, seqs, batch, dev):
     """Seeded synthetic sequences coded by this engine's encoder (untimed
     setup).  Per group of streams: ids, I payloads, the I-frame reconstruction
-    of the encoder, 4 lists of P payloads and their reset flags."""
+    of the encoder, 4 lists of P payloads, their reset flags and the SHA-256
+    of the encoder's decoded-picture-buffer states after the last P packet."""
     import torch
     groups = []
     for g0 in range(0, len(seqs), batch):
@@ -206,7 +215,8 @@ def encode_sequences(ufb, syn, mi, mv, seqs, batch, dev):
             p_pays.append(pay)
             resets.append(reset)
             count += 8
-        groups.append((ids, i_pay, i_rec if g0 == 0 else None, p_pays, resets))
+        states = {k: cv.state_hash(k) for k in ("reference", "memory", "context")}
+        groups.append((ids, i_pay, i_rec if g0 == 0 else None, p_pays, resets, states))
         del video
     return groups
 
@@ -246,7 +256,7 @@ def bench_decode_ours(args, rank, world, local):
 
     def decode_group(g, yuv):
         """One codec group: I packet, then the 4 P packets of each of its streams."""
-        (ids, i_pay, _, p_pays, resets), (di, dv), (si, sp) = groups[g], decoders[g], sinks[g]
+        (ids, i_pay, _, p_pays, resets, _), (di, dv), (si, sp) = groups[g], decoders[g], sinks[g]
         di.decompress(i_pay, W1080, H1080, QP_I, frames=False, yuv_out=si if yuv else None)
         dv.set_reference_from(di)
         frames = len(ids)
@@ -306,8 +316,14 @@ def bench_decode_ours(args, rank, world, local):
     ms_max = reduce_over_ranks(ms, world, dev, "max")
     total_frames = reduce_over_ranks(frames, world, dev, "sum")
 
-    # integrity check: decoding reproduces the encoder-side reconstruction
-    _, i_pay, i_rec, _, _ = groups[0]
+    # integrity checks: after the last decoded step every group's decoder holds
+    # the encoder's decoded-picture-buffer states (which depend on every P
+    # packet's reconstruction), and the I packet decodes to the encoder's frame
+    for g, (_, dv) in enumerate(decoders):
+        for k, want in groups[g][5].items():
+            if dv.state_hash(k) != want:
+                raise RuntimeError(f"group {g}: decoder {k} state after the P packets differs from the encoder's")
+    _, i_pay, i_rec, _, _, _ = groups[0]
     got_i, _ = decoders[0][0].decompress(i_pay, W1080, H1080, QP_I, frames=True)
     if not np.array_equal(got_i, i_rec):
         raise RuntimeError("I-packet decode differs from the encoder reconstruction")
@@ -337,6 +353,8 @@ def bench_decode_ours(args, rank, world, local):
                      "achieved": achieved, "peak": peak, "unit": "TOPS(int8)",
                      "frac": achieved / peak if achieved else None,
                      "traffic": load_traffic("decode_conv_per_launch"),
+                     "traffic_source": "ncu capture of a --seqs 8 decode (profiles/conv_i16_tc_decode_full.md), "
+                                       "not this run",
                      "traffic_launch": "DRAM read + write of one 512->512 residual-epilogue launch over 32640 "
                                        "pixels (profiles/conv_i16_tc_decode_full.md); algorithmic 100.3 MB",
                      "peak_source": "measured live: dense tcgen05 kind::i8 probe (ufb_probe_i8_peak)",
@@ -496,6 +514,7 @@ def bench_conv_ours(args, rank, world, local):
         "gpu_launches": args.steps, "clocks": clk.summary(),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS(int8)",
                      "frac": achieved / peak, "traffic": load_traffic("conv_config1_b64"),
+                     "traffic_source": "ncu capture in profiles/, not this run",
                      "peak_source": "measured live: dense tcgen05 kind::i8 probe (ufb_probe_i8_peak)"},
         "e2e": {"value": world * macs / (e2e_ms * 1e-3), "unit": "MAC/s", "h2d_bytes_per_step": int(x.nbytes),
                 "d2h_bytes_per_step": int(n * co * h * wd * 2)},
@@ -514,6 +533,137 @@ def ref_conv(threads):
     return sample * 64 * 88 * 160 * 64 * 9 / dt, f"{sample} of {CONV_BATCH} config-1 convs ({dt:.2f} s)"
 
 
+# ----------------------------------------------------------------- warp ----
+
+WARP_SHAPE = (1, 64, 176, 320)
+
+
+def warp_inputs(seed=1):
+    rng = np.random.default_rng(seed)
+    n, c, h, w = WARP_SHAPE
+    f = rng.integers(-4096, 4097, WARP_SHAPE).astype(np.int16)
+    flow = np.round(512 * (rng.normal(0, 4.0, (n, 2, h, w)) + np.array([3.25, -1.5])[None, :, None, None]))
+    return f, np.clip(flow, -32768, 32767).astype(np.int16)
+
+
+def warp_bytes():
+    n, c, h, w = WARP_SHAPE
+    return 2 * (2 * n * c * h * w) + 2 * n * 2 * h * w
+
+
+def hbm_peak():
+    """Measured copy bandwidth (MEASURED_PEAKS.json) or the pool's fallback figure."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback (6.65 TB/s)"
+
+
+def bench_warp_ours(args, rank, world, local):
+    import torch
+    import __graft_entry__ as entry
+    ufb = entry.load_package()
+    L = ufb.library()
+    L.ufb_warp.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = C.c_void_p(stream.cuda_stream)
+    f, flow = warp_inputs(1 + rank)
+    n, c, h, w = WARP_SHAPE
+    fd, fld = torch.from_numpy(f).to(dev), torch.from_numpy(flow).to(dev)
+    out = torch.empty_like(fd)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def launch(o=out, x=fd, fl=fld):
+        rc = L.ufb_warp(x.data_ptr(), fl.data_ptr(), n, c, h, w, o.data_ptr(), sp)
+        if rc:
+            raise RuntimeError(L.ufb_last_error().decode())
+
+    steps = max(args.steps, 20)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    with Clocks(local) as clk:
+        for _ in range(max(args.warmup, 3)):
+            launch()
+        t_end = time.time() + 0.5
+        while time.time() < t_end:
+            flush.fill_(1)
+            launch()
+            torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        for a, b in ev:
+            flush.fill_(1)  # L2 holds nothing of the inputs when the call starts
+            a.record(stream)
+            launch()
+            b.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+    ms_max = reduce_over_ranks(ms, world, dev, "max")
+    import oracle
+    ora = oracle.c_oracle()
+    want = ora.warp(f, flow)
+    if not np.array_equal(out.cpu().numpy(), want):
+        raise RuntimeError("warp output differs from the fixed-point oracle")
+    # end to end through the public entry point: host (pinned) inputs in, host output back
+    fh, flh = torch.from_numpy(f).pin_memory(), torch.from_numpy(flow).pin_memory()
+    oh = torch.empty_like(fh).pin_memory()
+
+    def e2e_step():
+        fd.copy_(fh, non_blocking=True)
+        fld.copy_(flh, non_blocking=True)
+        launch()
+        oh.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    e3.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = reduce_over_ranks(e2.elapsed_time(e3) / steps, world, dev, "max")
+    if not np.array_equal(oh.numpy(), want):
+        raise RuntimeError("warp e2e output differs from the fixed-point oracle")
+    peak, peak_src = hbm_peak()
+    achieved = warp_bytes() / (ms * 1e-3) / 1e9
+    return {
+        "metric": "INT16 backward bilinear warp calls/s (BASELINE config 2, 1x64x176x320)",
+        "value": world / (ms_max * 1e-3), "unit": "warps/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int16 (Q9 flow, 32-bit exact rna bilinear)", "data": "synthetic (seeded)",
+        "config": {"workload": "config 2: features 1x64x176x320 U[-4096,4096], Q9 flow N(0,4^2)+(3.25,-1.5) px, "
+                               "border clamp, seed 1", "l2": "flushed (256 MB write) before every timed call",
+                   "parallelism": f"replicas x{world}"},
+        "gpu_launches": steps, "clocks": clk.summary(),
+        "roofline": {"bound": "hbm", "kernel": "warp_tile_kernel", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "traffic": load_traffic("warp_config2_per_launch"),
+                     "traffic_source": "ncu capture (profiles/warp_tile_config2.md), not this run",
+                     "algorithmic_bytes": warp_bytes(), "peak_source": peak_src,
+                     "timing": "CUDA events around each launch on its stream, averaged"},
+        "e2e": {"value": world / (e2e_ms * 1e-3), "unit": "warps/s", "h2d_bytes_per_step": int(f.nbytes + flow.nbytes),
+                "d2h_bytes_per_step": int(f.nbytes)},
+    }
+
+
+def cpu_warp():
+    """The fixed-point restatement (oracle/uf_oracle.c, one thread) on whole config-2 calls."""
+    import oracle
+    ora = oracle.c_oracle()
+    f, flow = warp_inputs(1)
+    calls, t0 = 0, time.perf_counter()
+    while calls < 3 or time.perf_counter() - t0 < 2.0:
+        ora.warp(f, flow)
+        calls += 1
+    dt = time.perf_counter() - t0
+    return calls / dt, f"{calls} config-2 calls of the C restatement ufo_warp in {dt:.2f} s"
+
+
 # ----------------------------------------------------------------- main ----
 
 def main():
@@ -523,11 +673,19 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
+        kind, cores = "reference", threads
         if args.workload == "conv":
             runs = [ref_conv(threads) for _ in range(max(args.steps, 1))]
             value, unit, note = statistics.median(r[0] for r in runs), "MAC/s", runs[-1][1]
             metric = "INT16 3x3 conv int16-MAC/s (BASELINE config 1 shape, 64 copies per step)"
             cfg = "config-1 conv 64x[1x64x88x160] 3x3 64->64 int32 bias, pad 1"
+        elif args.workload == "warp":
+            # the reference has no integer warp: its CPU path is this repository's restatement
+            runs = [cpu_warp() for _ in range(max(args.steps, 1))]
+            value, unit, note = statistics.median(r[0] for r in runs), "warps/s", runs[-1][1]
+            metric = "INT16 backward bilinear warp calls/s (BASELINE config 2, 1x64x176x320)"
+            cfg = "config 2: features 1x64x176x320, Q9 flow N(0,4^2)+(3.25,-1.5) px, border clamp, seed 1"
+            kind, cores = "port", 1
         else:
             samples = [ref_decode_sample(threads) for _ in range(max(args.steps, 1))]
             t_p = statistics.median(s[0] for s in samples)
@@ -539,7 +697,7 @@ def main():
             "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "int16",
             "data": "synthetic (seeded)", "config": {"workload": cfg},
-            "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "reference", "sample": note},
+            "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": kind, "sample": note},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         return
     if world > 1:
@@ -547,8 +705,14 @@ def main():
         import torch.distributed as dist
         from datetime import timedelta
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
-    if args.workload == "conv":
+        # start barrier and timing reductions only: host scalars over gloo
+        dist.init_process_group("gloo", timeout=timedelta(seconds=600))
+    if args.workload == "warp":
+        res = bench_warp_ours(args, rank, world, local)
+        if rank == 0 and world == 1:
+            v, note = cpu_warp()
+            res["cpu_baseline"] = {"value": v, "unit": "warps/s", "cores": 1, "kind": "port", "sample": note}
+    elif args.workload == "conv":
         res = bench_conv_ours(args, rank, world, local)
         if rank == 0 and world == 1:
             v, note = ref_conv(1)

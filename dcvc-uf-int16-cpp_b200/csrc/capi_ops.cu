@@ -211,7 +211,12 @@ int ufb_warp(const int16_t* feature, const int16_t* flow, int n, int c, int h, i
     if (static_cast<long long>(n) * c * h * w > INT32_MAX || static_cast<long long>(w) * 512 > INT32_MAX / 2 ||
         static_cast<long long>(h) * 512 > INT32_MAX / 2)
         return err(UFB_ERANGE, "warp tensor exceeds indexing bounds");
-    return cuda_ok(warp_fixed(out, feature, flow, n, c, h, w, static_cast<cudaStream_t>(stream)), "warp")
+    if (static_cast<long long>(n) * ((c + 15) / 16) > 65535) return err(UFB_ERANGE, "warp batch exceeds grid bounds");
+    int device = 0;
+    if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return last_code();
+    int* status = device_status(device);
+    if (!status) return last_code();
+    return cuda_ok(warp_fixed(out, feature, flow, n, c, h, w, status, static_cast<cudaStream_t>(stream)), "warp")
                ? UFB_OK
                : last_code();
 }

@@ -26,7 +26,9 @@ cudaError_t ew_lut8(uint8_t* out, const int16_t* x, const uint8_t* lut, long lon
 cudaError_t ew_bytes(int16_t* out, const uint8_t* x, long long n, cudaStream_t s);
 cudaError_t ew_wsilu4(int16_t* out, const int16_t* x, const int16_t* lut, int n, int c4, long long hw,
                       cudaStream_t s);
+// Fixed-point backward bilinear warp (warp.cu); a bounded wait that gives up
+// records code 11 in *status.
 cudaError_t warp_fixed(int16_t* out, const int16_t* feature, const int16_t* flow, int n, int c, int h, int w,
-                       cudaStream_t s);
+                       int* status, cudaStream_t s);
 
 }  // namespace ufb

@@ -1,7 +1,7 @@
 // Memory-bound INT16 kernels: layout conversion between
 // the reference's NCHW tensors and split NHWC, the direct (grouped / strided /
 // depthwise) convolution, the elementwise operators of the reference's CUDA
-// extension (src/cuda/elementwise.cu:16-46) and the fixed-point warp.
+// extension (src/cuda/elementwise.cu:16-46).
 #include "kernels.h"
 #include "conv_epi.cuh"
 #include "uf_common.cuh"
@@ -146,40 +146,6 @@ __global__ void wsilu4_kernel(int16_t* out, const int16_t* x, const int16_t* lut
     }
 }
 
-// Fixed-point backward bilinear warp (config-2 kernel; this repository's spec,
-// no reference counterpart).  One thread per output pixel and channel group;
-// neighbour fetches stay inside the 2x2 footprint of the displaced position.
-__global__ void warp_kernel(int16_t* __restrict__ out, const int16_t* __restrict__ feature,
-                            const int16_t* __restrict__ flow, int n, int c, int h, int w) {
-    const long long total = static_cast<long long>(n) * h * w;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int x = static_cast<int>(i % w);
-        const int y = static_cast<int>((i / w) % h);
-        const long long b = i / (static_cast<long long>(w) * h);
-        const long long plane = static_cast<long long>(h) * w;
-        const int fx = flow[(b * 2 + 0) * plane + static_cast<long long>(y) * w + x];
-        const int fy = flow[(b * 2 + 1) * plane + static_cast<long long>(y) * w + x];
-        int px = x * 512 + fx, py = y * 512 + fy;
-        px = px < 0 ? 0 : (px > (w - 1) * 512 ? (w - 1) * 512 : px);
-        py = py < 0 ? 0 : (py > (h - 1) * 512 ? (h - 1) * 512 : py);
-        const int x0 = px >> 9, y0 = py >> 9;
-        const int x1 = x0 + 1 < w ? x0 + 1 : w - 1, y1 = y0 + 1 < h ? y0 + 1 : h - 1;
-        const int ax = px & 511, ay = py & 511;
-        const int64_t wa = static_cast<int64_t>(512 - ax) * (512 - ay), wb = static_cast<int64_t>(512 - ax) * ay;
-        const int64_t wc = static_cast<int64_t>(ax) * (512 - ay), wd = static_cast<int64_t>(ax) * ay;
-        const long long o00 = static_cast<long long>(y0) * w + x0, o10 = static_cast<long long>(y1) * w + x0;
-        const long long o01 = static_cast<long long>(y0) * w + x1, o11 = static_cast<long long>(y1) * w + x1;
-        const int16_t* f = feature + b * c * plane;
-        int16_t* o = out + b * c * plane + static_cast<long long>(y) * w + x;
-        for (int ch = 0; ch < c; ++ch) {
-            const int16_t* p = f + ch * plane;
-            const int64_t s = wa * __ldg(p + o00) + wb * __ldg(p + o10) + wc * __ldg(p + o01) + wd * __ldg(p + o11);
-            o[ch * plane] = sat16(rna_div(s, 1 << 18));
-        }
-    }
-}
-
 unsigned grid_for(long long n) {
     const long long b = (n + kBlock - 1) / kBlock;
     const long long cap = 148ll * 16;
@@ -242,12 +208,6 @@ cudaError_t ew_wsilu4(int16_t* out, const int16_t* x, const int16_t* lut, int n,
                       cudaStream_t s) {
     const long long total = static_cast<long long>(n) * (c4 / 4) * hw;
     wsilu4_kernel<<<grid_for(total), kBlock, 0, s>>>(out, x, lut, total, c4 / 4, hw);
-    return cudaGetLastError();
-}
-
-cudaError_t warp_fixed(int16_t* out, const int16_t* feature, const int16_t* flow, int n, int c, int h, int w,
-                       cudaStream_t s) {
-    warp_kernel<<<grid_for(static_cast<long long>(n) * h * w), kBlock, 0, s>>>(out, feature, flow, n, c, h, w);
     return cudaGetLastError();
 }
 

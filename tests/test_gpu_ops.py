@@ -203,12 +203,35 @@ def test_depthwise_extremes_and_ties(ufb, ora, dev, xv, wv):
     _status_clean(ufb)
 
 
-def test_warp_matches_oracle(ufb, ora, dev):
-    rng = np.random.default_rng(1)
-    f = rng.integers(-4096, 4097, (1, 8, 44, 80)).astype(np.int16)
-    flow = np.round(512 * (rng.normal(0, 4, (1, 2, 44, 80)) + np.array([3.25, -1.5])[None, :, None, None]))
-    flow = np.clip(flow, -32768, 32767).astype(np.int16)
-    assert np.array_equal(N(ufb.warp(T(f, dev), T(flow, dev))), ora.warp(f, flow))
+def _config2_flow(rng, n, h, w, sigma=4.0, shift=(3.25, -1.5)):
+    """BASELINE config 2's flow: int16 Q9 of N(0, sigma^2) px per pixel plus a global translation."""
+    flow = np.round(512 * (rng.normal(0, sigma, (n, 2, h, w)) + np.array(shift)[None, :, None, None]))
+    return np.clip(flow, -32768, 32767).astype(np.int16)
+
+
+@pytest.mark.parametrize("n,c,h,w,sigma,shift,lo,hi", [
+    (1, 64, 176, 320, 4.0, (3.25, -1.5), -4096, 4097),        # BASELINE config 2 (TMA-staged windows)
+    (1, 8, 44, 80, 4.0, (3.25, -1.5), -4096, 4097),
+    (2, 6, 37, 72, 2.0, (-0.5, 0.75), -32768, 32768),         # batch 2, ragged tiles, full int16 range
+    (1, 4, 40, 64, 40.0, (0.0, 0.0), -32768, 32768),          # wide spread: windows exceed the ring (global gathers)
+    (1, 4, 30, 50, 4.0, (3.25, -1.5), -4096, 4097),           # W % 8 != 0: no tensor map (global gathers)
+    (1, 3, 24, 64, 4.0, (3.25, -1.5), -4096, 4097),           # odd channel count: no tensor map
+    (1, 2, 16, 16, 0.0, (100.0, -100.0), -4096, 4097),        # every sample clamped to the border
+])
+def test_warp_matches_oracle(ufb, ora, dev, n, c, h, w, sigma, shift, lo, hi):
+    """The integer warp equals the fixed-point spec (ufo_warp) exactly; against
+    the float semantics of src/dcvc_fm_motion.cu:41-58 it differs by at most
+    one Q9 step (reported for config 2)."""
+    rng = np.random.default_rng(c * 1000 + h)
+    f = rng.integers(lo, hi, (n, c, h, w)).astype(np.int16)
+    flow = _config2_flow(rng, n, h, w, sigma, shift)
+    got = N(ufb.warp(T(f, dev), T(flow, dev)))
+    assert np.array_equal(got, ora.warp(f, flow))
+    if (c, h, w) == (64, 176, 320):
+        delta = np.abs(got.astype(np.float64) - ora.warp_float(f, flow))
+        print(f"config 2: max |integer - float| = {delta.max():.4f} Q9 steps")
+        assert delta.max() <= 1.0
+    _status_clean(ufb)
 
 
 def test_errors_are_raised_not_computed(ufb, dev):

@@ -156,11 +156,22 @@ def test_state_hashes_match_reference(ufb, ref, ora, syn, setup):
     video = syn.synthetic_video(W, H, 9, 61)
     r = st.RefStreamCodec(ref, ora, setup["img_t"], setup["vid_t"], *setup["ids"], skip_threshold=SKIP)
     data, packets = r.encode(video, W, H, 0, 20, 0, -1)
-    r.decode(data, 9, packets)
+    # the reference models' states after decoding the archive's packets in
+    # order, as IntegerCodec::decode_stream_impl does (src/integer_codec.cpp:445-461)
+    image, vid = ref.model("image", setup["img_t"]), ref.model("htl", setup["vid_t"])
+    for m in (image, vid):
+        m.set_skip_threshold(SKIP)
+    for u in ref.bs_parse(data)[1]:
+        if u["type"] == 1:
+            frames = image.decompress(u["payload"], W, H, u["qp"])
+            vid.clear_dpb()
+            vid.add_ref_feature_from_frame(frames[0])
+        elif u["type"] == 2:
+            vid.decompress(u["payload"], W, H, u["qp"], u["reset"])
     sc, (ic, vc) = _engine(ufb, setup)
     sc.decode([data], 9, packets)
     for k in ("reference", "memory", "context"):
-        mine, want = vc.state_hash(k), r.video.state(k)
+        mine, want = vc.state_hash(k), vid.state(k)
         assert (mine is None) == (want is None), k
         if want is not None:
             assert mine == hashlib.sha256(np.ascontiguousarray(want, "<i2").tobytes()).hexdigest(), k
