@@ -28,7 +28,8 @@ int conv_direct_path(const int16_t* x, int n, int ci, int h, int w, const int16_
 }
 
 int conv_tc_path(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
-                 const void* bias, int bias_bits, int ph, int pw, int oh, int ow, int16_t* out, cudaStream_t s) {
+                 const void* bias, int bias_bits, int stride, int ph, int pw, int oh, int ow, int16_t* out,
+                 cudaStream_t s) {
     int device = 0;
     if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return last_code();
     const int cip = round_up(ci, 16), cop = round_up(co, 16);
@@ -48,7 +49,7 @@ int conv_tc_path(const int16_t* x, int n, int ci, int h, int w, const int16_t* w
     Epilogue epi{};
     epi.bias = bias_bits ? bias : nullptr;
     epi.bias32 = bias_bits == 32;
-    if (conv_tc_run(tw, in, ov, epi, ph, pw, s, status, msg) != 0) return err(UFB_ECUDA, msg);
+    if (conv_tc_run(tw, in, ov, epi, ph, pw, s, status, msg, stride) != 0) return err(UFB_ECUDA, msg);
     if (!cuda_ok(split_to_nchw(ov, 1, out, s), "output layout")) return last_code();
     return UFB_OK;
 }
@@ -86,8 +87,11 @@ int conv_dispatch(const int16_t* x, int n, int ci, int h, int w, const int16_t* 
     if (allow_tc && groups == ci && ci == co && ci % 4 == 0 && kh == 3 && kw == 3 && sh == 1 && sw == 1 && ph == 1 &&
         pw == 1 && bias_bits != 32)
         return conv_depthwise_path(x, n, ci, h, w, weight, bias_bits ? bias : nullptr, out, s);
-    const bool tc_ok = allow_tc && groups == 1 && sh == 1 && sw == 1 && static_cast<long long>(ci) * kh * kw <= kTcMaxReduction;
-    if (tc_ok) return conv_tc_path(x, n, ci, h, w, weight, co, kh, kw, bias, bias_bits, ph, pw, oh, ow, out, s);
+    // stride 1, or stride 2 in both directions (TMA element strides)
+    const bool tc_ok = allow_tc && groups == 1 && sh == sw && (sh == 1 || sh == 2) &&
+                       static_cast<long long>(ci) * kh * kw <= kTcMaxReduction;
+    if (tc_ok)
+        return conv_tc_path(x, n, ci, h, w, weight, co, kh, kw, bias, bias_bits, sh, ph, pw, oh, ow, out, s);
     if (!allow_direct && !allow_tc) return err(UFB_EINVAL, "no convolution path");
     return conv_direct_path(x, n, ci, h, w, weight, co, kh, kw, bias, bias_bits, sh, sw, ph, pw, groups, oh, ow, out,
                             s);
@@ -211,7 +215,7 @@ int ufb_warp(const int16_t* feature, const int16_t* flow, int n, int c, int h, i
     if (static_cast<long long>(n) * c * h * w > INT32_MAX || static_cast<long long>(w) * 512 > INT32_MAX / 2 ||
         static_cast<long long>(h) * 512 > INT32_MAX / 2)
         return err(UFB_ERANGE, "warp tensor exceeds indexing bounds");
-    if (static_cast<long long>(n) * ((c + 15) / 16) > 65535) return err(UFB_ERANGE, "warp batch exceeds grid bounds");
+    if (static_cast<long long>(n) * ((c + 7) / 8) > 65535) return err(UFB_ERANGE, "warp batch exceeds grid bounds");
     int device = 0;
     if (!cuda_ok(cudaGetDevice(&device), "cudaGetDevice")) return last_code();
     int* status = device_status(device);

@@ -94,6 +94,7 @@ struct ConvTcArgs {
     Act out;
     Epilogue epi;
     int co, ci, taps_h, taps_w, pad_h, pad_w, cpad;
+    int stride;  // spatial mode: 1, or 2 (every second input pixel per tap, TMA element strides)
     int oh, ow;
     int tile_w, tile_h, tiles_x, tiles_y;
     long long m_total;  // flat mode: output pixels
@@ -317,7 +318,8 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
                     const int c0 = cb * kBK;
                     if (SPATIAL) {
-                        const int ix = tc.x0 + kx - args.pad_w, iy = tc.y0 + ky - args.pad_h;
+                        const int ix = tc.x0 * args.stride + kx - args.pad_w;
+                        const int iy = tc.y0 * args.stride + ky - args.pad_h;
                         tma_load_5d(st, &mapA, &full_bar[s], c0, 0, ix, iy, tc.img);
                         tma_load_5d(st + kABytes, &mapA, &full_bar[s], c0, 1, ix, iy, tc.img);
                     } else {
@@ -721,13 +723,16 @@ EncodeTiledFn encode_fn() {
 }
 
 bool encode(CUtensorMap* map, void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
-            const cuuint32_t* box, std::string& err, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+            const cuuint32_t* box, std::string& err, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B,
+            const cuuint32_t* element_strides = nullptr) {
     auto fn = encode_fn();
     if (!fn) {
         err = "cuTensorMapEncodeTiled is unavailable";
         return false;
     }
     cuuint32_t elem[5] = {1, 1, 1, 1, 1};
+    if (element_strides)
+        for (int i = 0; i < rank; ++i) elem[i] = element_strides[i];
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, base, dims, strides, box, elem,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
@@ -802,9 +807,11 @@ cudaError_t launch(const ConvMaps& m, const ConvTcArgs& args, size_t smem, int s
 
 // Tensor map of a split-NHWC view in tile order: flat {c, plane, pixels} (box
 // of tw * th pixels) or spatial {c, plane, w, h, n} (box tw x th), box of
-// `box_c` channels of one plane.
+// `box_c` channels of one plane.  stride 2 (spatial only): the box spans
+// 2 tw x 2 th pixels traversed with element stride 2, so it brings the tw x th
+// input pixels a stride-2 convolution tap reads for a tw x th output tile.
 bool act_map(CUtensorMap* map, const Act& v, bool flat, int tw, int th, cuuint32_t box_c,
-             CUtensorMapSwizzle swizzle, std::string& err) {
+             CUtensorMapSwizzle swizzle, std::string& err, int stride = 1) {
     if (flat) {
         const cuuint64_t dims[3] = {static_cast<cuuint64_t>(v.c), 2, static_cast<cuuint64_t>(v.pixels())};
         const cuuint64_t strides[2] = {static_cast<cuuint64_t>(v.pitch), static_cast<cuuint64_t>(2 * v.pitch)};
@@ -816,8 +823,9 @@ bool act_map(CUtensorMap* map, const Act& v, bool flat, int tw, int th, cuuint32
     const cuuint64_t strides[4] = {static_cast<cuuint64_t>(v.pitch), static_cast<cuuint64_t>(2 * v.pitch),
                                    static_cast<cuuint64_t>(2 * v.pitch) * v.row_px,
                                    static_cast<cuuint64_t>(2 * v.pitch) * v.img_px};
-    const cuuint32_t box[5] = {box_c, 1, static_cast<cuuint32_t>(tw), static_cast<cuuint32_t>(th), 1};
-    return encode(map, v.base, 5, dims, strides, box, err, swizzle);
+    const cuuint32_t box[5] = {box_c, 1, static_cast<cuuint32_t>(tw * stride), static_cast<cuuint32_t>(th * stride), 1};
+    const cuuint32_t elem[5] = {1, 1, static_cast<cuuint32_t>(stride), static_cast<cuuint32_t>(stride), 1};
+    return encode(map, v.base, 5, dims, strides, box, err, swizzle, elem);
 }
 
 }  // namespace
@@ -893,10 +901,18 @@ bool tc_prepare(TcWeights& w, const int16_t* weight, int co, int ci, int kh, int
 }
 
 int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogue& epi, int pad_h, int pad_w,
-                cudaStream_t stream, int* status, std::string& err) {
-    const int oh = in.h + 2 * pad_h - w.kh + 1, ow = in.w + 2 * pad_w - w.kw + 1;
-    if (oh <= 0 || ow <= 0) {
+                cudaStream_t stream, int* status, std::string& err, int stride) {
+    if (stride != 1 && stride != 2) {
+        err = "tensor-core convolutions take stride 1 or 2";
+        return -1;
+    }
+    if (in.h + 2 * pad_h < w.kh || in.w + 2 * pad_w < w.kw) {
         err = "kernel exceeds input";
+        return -1;
+    }
+    const int oh = (in.h + 2 * pad_h - w.kh) / stride + 1, ow = (in.w + 2 * pad_w - w.kw) / stride + 1;
+    if (stride != 1 && (epi.shuffle2 || epi.wsilu4 || epi.lut || epi.res1.base)) {
+        err = "strided convolutions take no fused epilogue step";
         return -1;
     }
     if (in.c != w.ci) {
@@ -945,7 +961,7 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
         err = "reduction longer than the tensor-core path's 32-bit recombination bound";
         return -1;
     }
-    const bool flat = w.kh == 1 && w.kw == 1 && pad_h == 0 && pad_w == 0 && in.dense() && out.dense() &&
+    const bool flat = stride == 1 && w.kh == 1 && w.kw == 1 && pad_h == 0 && pad_w == 0 && in.dense() && out.dense() &&
                       !epi.shuffle2 && (!epi.res1.base || epi.res1.dense()) && (!epi.res2.base || epi.res2.dense()) &&
                       in.pixels() < (1ll << 31);
     ConvTcArgs args{};
@@ -962,6 +978,7 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     args.pad_h = pad_h;
     args.pad_w = pad_w;
     args.cpad = w.cpad;
+    args.stride = stride;
     args.oh = oh;
     args.ow = ow;
     args.signed_split = w.signed_split ? 1 : 0;
@@ -986,7 +1003,7 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
         m_tiles = static_cast<long long>(args.tiles_x) * args.tiles_y * in.n;
     }
     // the activation box is the tile's input window (shifted per tap in spatial mode)
-    if (!act_map(&maps.a, in, flat, tw, th, kBK, CU_TENSOR_MAP_SWIZZLE_128B, err)) return -1;
+    if (!act_map(&maps.a, in, flat, tw, th, kBK, CU_TENSOR_MAP_SWIZZLE_128B, err, stride)) return -1;
     // output box: one epilogue warp's 32 pixels, 64 channels (64-byte swizzle) or,
     // for wsilu4, 16 channels (unswizzled); the map's extent is the view's, so
     // tails are clipped

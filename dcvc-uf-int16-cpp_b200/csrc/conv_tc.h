@@ -62,10 +62,11 @@ bool tc_encode_map(CUtensorMap* map, void* base, int rank, const cuuint64_t* dim
 // CTAs every CTA walks many tiles, which exercises both TMEM accumulator sets.
 void tc_set_max_ctas(int n);
 
-// out = epilogue(conv(in, w)), stride 1, zero padding (pad_h, pad_w).
-// Both views must have 16-byte aligned pitch and base.  Asynchronous on
-// `stream`; pipeline timeouts are reported through *status.
+// out = epilogue(conv(in, w)), zero padding (pad_h, pad_w), stride 1 or 2
+// (strided: plain epilogue only).  Both views must have 16-byte aligned pitch
+// and base.  Asynchronous on `stream`; pipeline timeouts are reported through
+// *status.
 int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogue& epi, int pad_h, int pad_w,
-                cudaStream_t stream, int* status, std::string& err);
+                cudaStream_t stream, int* status, std::string& err, int stride = 1);
 
 }  // namespace ufb

@@ -295,7 +295,7 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
         count();
         return out;
     }
-    if (stride == 1 && L->tc.planes) {
+    if (L->tc.planes && (stride == 1 || !(f.lut || f.wsilu4 || f.shuffle2 || f.res1 || f.mulq))) {
         Epilogue e{};
         e.bias = L->bias;
         e.bias32 = 0;
@@ -315,14 +315,14 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
             ev0 = stats_->take_event();
             ck(cudaEventRecord(ev0, s_), "event");
         }
-        if (conv_tc_run(L->tc, in.a, out.a, e, pad, pad, s_, status_, err) != 0)
+        if (conv_tc_run(L->tc, in.a, out.a, e, pad, pad, s_, status_, err, stride) != 0)
             throw std::runtime_error(name + ": " + err);
         if (ev0) {
             cudaEvent_t ev1 = stats_->take_event();
             ck(cudaEventRecord(ev1, s_), "event");
             char key[96];
-            snprintf(key, sizeof(key), "conv %d>%d %dx%d @ %lld", L->ci, L->co, L->kh, L->kw,
-                     static_cast<long long>(in.a.n) * oh * ow);
+            snprintf(key, sizeof(key), "conv %d>%d %dx%d%s @ %lld", L->ci, L->co, L->kh, L->kw,
+                     stride == 2 ? "/2" : "", static_cast<long long>(in.a.n) * oh * ow);
             stats_->pending.push_back({ev0, ev1, key, true});
             auto& sh = stats_->shapes[key];
             ++sh.launches;
@@ -335,7 +335,9 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
         }
         return out;
     }
-    // Strided convolution: direct int64 kernel on NCHW copies (encode only).
+    // Strided convolution whose reduction exceeds the tensor-core bound: direct
+    // int64 kernel on NCHW copies (encode only; the HT-L and image strided
+    // layers, encoder.down and enc.enc_2.6, run on the tensor cores above).
     if (f.lut || f.wsilu4 || f.shuffle2 || f.res1 || f.mulq) throw std::invalid_argument("unsupported fusion for " + name);
     const size_t in_el = static_cast<size_t>(in.a.n) * in.a.c * in.a.h * in.a.w;
     const size_t out_el = static_cast<size_t>(in.a.n) * L->co * oh * ow;

@@ -7,10 +7,10 @@
 // rna(sum / 2^18) (always inside the int16 range: the weights sum to 2^18).
 //
 // Layout: NCHW int16 feature planes, as the float kernel takes them.  A CTA
-// owns a 64 x 16 output tile and a slab of 16 channels.  From the tile's flow it
+// owns a 64 x 16 output tile and a slab of 8 channels.  From the tile's flow it
 // finds the source window every bilinear footprint of the tile falls in (its
 // bounding box), and TMA brings that window for two channels at a time into a
-// three-stage shared-memory ring (boxes of 128 px x 8 rows x 2 planes, only as
+// two-stage shared-memory ring (boxes of 128 px x 8 rows x 2 planes, only as
 // many row blocks as the window needs); the gathers then read shared memory,
 // and each thread writes its two horizontally adjacent outputs per row as one
 // 32-bit store, so every output row leaves the SM as whole coalesced lines.
@@ -31,9 +31,9 @@ namespace {
 
 constexpr int kTW = 64, kTH = 16;              // output tile
 constexpr int kThreads = 256;                  // 8 warps x (2 rows x 64 px)
-constexpr int kSlab = 16;                      // channels per CTA
+constexpr int kSlab = 8;                       // channels per CTA
 constexpr int kCG = 2;                         // channels per TMA stage
-constexpr int kStages = 3;
+constexpr int kStages = 2;
 constexpr int kBoxW = 128;                     // window width limit (px)
 constexpr int kRowBlk = 8;                     // rows per TMA box
 constexpr int kMaxRows = 64;                   // window height limit
@@ -42,23 +42,18 @@ constexpr int kStageElems = (kMaxRows / kRowBlk) * kBlkElems;  // 16384 int16 = 
 constexpr int kSmemBytes = kStages * kStageElems * 2;
 constexpr int kWarpTimeoutCode = 11;
 
-// rna(((512 - ay)((512 - ax) v00 + ax v01) + ay((512 - ax) v10 + ax v11)) / 2^18)
-// in 32-bit arithmetic.  The row interpolations t = 512 v0 + ax (v1 - v0) fit
-// in 25 bits; the column step would need 34, so t is split as 512 h + l
-// (0 <= l < 512): s = 512 H + L with H = 512 h0 + ay (h1 - h0) and
-// L = 512 l0 + ay (l1 - l0) in [0, 2^18).  Then s < 0 iff H + (L >> 9) < 0, and
-// rna(s / 2^18) = floor((s + 2^17 - [s < 0]) / 2^18)
-//               = (H + ((L + 2^17 - [s < 0]) >> 9)) >> 9.
-// (Checked against the int64 formula on 4e8 random, extreme and tie cases.)
-__device__ __forceinline__ int32_t bilerp_q9(int32_t v00, int32_t v01, int32_t v10, int32_t v11, int32_t ax,
-                                             int32_t ay) {
-    const int32_t t0 = (v00 << 9) + ax * (v01 - v00);
-    const int32_t t1 = (v10 << 9) + ax * (v11 - v10);
-    const int32_t h0 = t0 >> 9, l0 = t0 & 511, h1 = t1 >> 9, l1 = t1 & 511;
-    const int32_t H = (h0 << 9) + ay * (h1 - h0);
-    const int32_t L = (l0 << 9) + ay * (l1 - l0);
-    const int32_t neg = (H + (L >> 9)) >> 31;
-    return (H + ((L + (1 << 17) + neg) >> 9)) >> 9;
+// rna(sum / 2^18) of the Q18 bilinear sum s = wa v00 + wb v10 + wc v01 + wd v11
+// (weights (512 - ax)(512 - ay), (512 - ax) ay, ax (512 - ay), ax ay; they sum
+// to 2^18, so |s| < 2^33 and the result is inside the int16 range).  The sum
+// needs 35 bits: four 32 x 32 -> 64-bit multiply-adds form it exactly, and
+// rna(s / 2^18) = floor((s + 2^17 - [s < 0]) / 2^18) is one 64-bit add and one
+// funnel shift.
+__device__ __forceinline__ int32_t bilerp_q18(int32_t v00, int32_t v01, int32_t v10, int32_t v11, int32_t wa,
+                                              int32_t wb, int32_t wc, int32_t wd) {
+    const int64_t s = static_cast<int64_t>(wa) * v00 + static_cast<int64_t>(wb) * v10 +
+                      static_cast<int64_t>(wc) * v01 + static_cast<int64_t>(wd) * v11;
+    const int32_t neg = static_cast<int32_t>(s >> 32) >> 31;
+    return static_cast<int32_t>((s + ((1 << 17) + neg)) >> 18);
 }
 
 __device__ __forceinline__ void store_pair(int16_t* row, int x, int w, bool pair_ok, bool v0, bool v1, int32_t a,
@@ -71,7 +66,7 @@ __device__ __forceinline__ void store_pair(int16_t* row, int x, int w, bool pair
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 3)
     warp_tile_kernel(const __grid_constant__ CUtensorMap map, int map_ok, const int16_t* __restrict__ feature,
                      const int16_t* __restrict__ flow, int16_t* __restrict__ out, int c, int h, int w, int slabs,
                      int pair_ok, int* status) {
@@ -95,7 +90,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         window[3] = -1;
     }
     // per pixel: p = row (0, 1) * 2 + column (0, 1)
-    int x0[4], x1[4], y0[4], y1[4], ax[4], ay[4];
+    int x0[4], x1[4], y0[4], y1[4], wa[4], wb[4], wc[4], wd[4];
     bool valid[4];
     int mnx = INT_MAX, mxx = -1, mny = INT_MAX, mxy = -1;
     const int16_t* fl = flow + static_cast<long long>(b) * 2 * plane;
@@ -103,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int p = 0; p < 4; ++p) {
         const int x = xs + (p & 1), y = ty0 + 2 * wid + (p >> 1);
         valid[p] = x < w && y < h;
-        x0[p] = x1[p] = y0[p] = y1[p] = ax[p] = ay[p] = 0;
+        x0[p] = x1[p] = y0[p] = y1[p] = wa[p] = wb[p] = wc[p] = wd[p] = 0;
         if (valid[p]) {
             const long long i = static_cast<long long>(y) * w + x;
             int px = x * 512 + static_cast<int>(__ldg(fl + i));
@@ -114,8 +109,11 @@ __global__ void __launch_bounds__(kThreads, 2)
             y0[p] = py >> 9;
             x1[p] = min(x0[p] + 1, w - 1);
             y1[p] = min(y0[p] + 1, h - 1);
-            ax[p] = px & 511;
-            ay[p] = py & 511;
+            const int ax = px & 511, ay = py & 511;
+            wa[p] = (512 - ax) * (512 - ay);
+            wb[p] = (512 - ax) * ay;
+            wc[p] = ax * (512 - ay);
+            wd[p] = ax * ay;
             mnx = min(mnx, x0[p]);
             mxx = max(mxx, x1[p]);
             mny = min(mny, y0[p]);
@@ -154,8 +152,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                 if (valid[p]) {
                     const int16_t* a = fp + static_cast<long long>(y0[p]) * w;
                     const int16_t* bb = fp + static_cast<long long>(y1[p]) * w;
-                    r[p] = bilerp_q9(__ldg(a + x0[p]), __ldg(a + x1[p]), __ldg(bb + x0[p]), __ldg(bb + x1[p]), ax[p],
-                                     ay[p]);
+                    r[p] = bilerp_q18(__ldg(a + x0[p]), __ldg(a + x1[p]), __ldg(bb + x0[p]), __ldg(bb + x1[p]),
+                                      wa[p], wb[p], wc[p], wd[p]);
                 }
             }
             store_pair(orow0 + ch * plane, xs, w, pair_ok, valid[0], valid[1], r[0], r[1]);
@@ -206,7 +204,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                 int32_t r[4];
 #pragma unroll
                 for (int p = 0; p < 4; ++p)
-                    r[p] = bilerp_q9(sb[o0[p]], sb[o0[p] + d[p]], sb[o1[p]], sb[o1[p] + d[p]], ax[p], ay[p]);
+                    r[p] = bilerp_q18(sb[o0[p]], sb[o0[p] + d[p]], sb[o1[p]], sb[o1[p] + d[p]], wa[p], wb[p], wc[p],
+                                      wd[p]);
                 const long long co = static_cast<long long>(s * kCG + cc) * plane;
                 store_pair(orow0 + co, xs, w, pair_ok, valid[0], valid[1], r[0], r[1]);
                 store_pair(orow1 + co, xs, w, pair_ok, valid[2], valid[3], r[2], r[3]);

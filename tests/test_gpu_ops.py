@@ -171,6 +171,29 @@ def test_depthwise_and_stride2(ufb, ora, dev):
     assert np.array_equal(N(ufb.conv2d(T(x, dev), T(w2, dev), None, 2, 2, 1, 1)), ora.conv2d(x, w2, None, 2, 1))
 
 
+@pytest.mark.parametrize("n,ci,co,h,w,k,ctas", [
+    (1, 512, 256, 68, 120, 3, 0),    # HT-L encoder.down at 1080p latent-feature scale /2
+    (2, 384, 256, 45, 37, 3, 0),     # image enc.enc_2.6 shape, odd sizes, batch 2
+    (1, 64, 40, 33, 70, 3, 3),       # channel tails (K and N), few CTAs walking many tiles
+    (1, 128, 96, 21, 22, 1, 0),      # 1x1 stride 2 (spatial tensor map)
+    (1, 16, 16, 3, 3, 3, 0),         # a single output row of two pixels
+])
+def test_stride2_tensor_core(ufb, ora, dev, n, ci, co, h, w, k, ctas):
+    """Stride-2 convolutions (encoder.down, enc.enc_2.6) on the tensor cores:
+    each tap's activation box is a 2x-sized TMA box with element stride 2."""
+    rng = np.random.default_rng(ci + co + h)
+    x = rng.integers(-32768, 32768, (n, ci, h, w)).astype(np.int16)
+    wt = rng.integers(-32768, 32768, (co, ci, k, k)).astype(np.int16)
+    b = rng.integers(-32768, 32768, (co,)).astype(np.int16)
+    ufb.set_conv_max_ctas(ctas)
+    try:
+        got = ufb.conv2d(T(x, dev), T(wt, dev), T(b, dev), 2, 2, k // 2, k // 2)
+    finally:
+        ufb.set_conv_max_ctas(0)
+    assert np.array_equal(N(got), ora.conv2d(x, wt, b, 2, k // 2))
+    _status_clean(ufb)
+
+
 @pytest.mark.parametrize("n,c,h,w", [(1, 64, 10, 12), (2, 256, 37, 45), (1, 192, 16, 33), (1, 512, 35, 50),
                                      (3, 4, 5, 7), (1, 132, 1, 1)])
 def test_depthwise_split_kernel(ufb, ora, dev, n, c, h, w):
