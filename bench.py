@@ -9,7 +9,11 @@ Workloads
           reset_interval 8 -> every P packet resets, skip 0.2), sharded
           64/N streams per GPU with no inter-GPU communication.  One step decodes
           every sequence of the rank completely (I packet, then the 4 P packets),
-          host rANS included.  Unit: decoded frames/s (whole job).
+          host rANS included.  Unit: decoded frames/s (whole job).  At N=1 the
+          line also carries `secondary`: the same decode at 626x352 (BASELINE
+          configs 3-4; 64 sequences, seeds 3..66), the single-stream 120-frame
+          config-4 GOP, the per-P-packet latency, and the reference CPU decode
+          time of the config-3 packets when tests/golden/config3.json has it.
   conv    BASELINE config 1 batched: 64 copies of the 1x64x88x160 int16 3x3 conv.
   warp    BASELINE config 2: the fixed-point backward bilinear warp of int16
           features 1x64x176x320 by an int16 Q9 flow (N(0, 4^2) px per pixel plus a
@@ -66,6 +70,7 @@ def parse():
     p.add_argument("--seqs", type=int, default=SEQS,
                    help="sequences in the job (default: BASELINE config 5's 64); smaller values are for profiling")
     p.add_argument("--shapes", action="store_true", help="print per launch shape convolution time to stderr")
+    p.add_argument("--no-secondary", action="store_true", help="skip the 626x352 measurements (decode workload, N=1)")
     return p.parse_args()
 
 
@@ -188,16 +193,20 @@ def shard(rank, world, seqs):
     return list(range(rank * per, (rank + 1) * per))
 
 
-def encode_sequences(ufb, syn, mi, mv, seqs, batch, dev):
+def p_packets(frames):
+    return (frames - 1 + 7) // 8
+
+
+def encode_sequences(ufb, syn, mi, mv, seqs, batch, dev, width=W1080, height=H1080, frames=FRAMES, seed_base=100):
     """Seeded synthetic sequences coded by this engine's encoder (untimed
     setup).  Per group of streams: ids, I payloads, the I-frame reconstruction
-    of the encoder, 4 lists of P payloads, their reset flags and the SHA-256
+    of the encoder, the lists of P payloads, their reset flags and the SHA-256
     of the encoder's decoded-picture-buffer states after the last P packet."""
     import torch
     groups = []
     for g0 in range(0, len(seqs), batch):
         ids = seqs[g0:g0 + batch]
-        video = torch.stack([syn.synthetic_video_gpu(W1080, H1080, FRAMES, 100 + s, dev) for s in ids])
+        video = torch.stack([syn.synthetic_video_gpu(width, height, frames, seed_base + s, dev) for s in ids])
         ci = ufb.Codec(mi, len(ids))
         ci.set_skip_threshold(SKIP)
         cv = ufb.Codec(mv, len(ids))
@@ -206,12 +215,12 @@ def encode_sequences(ufb, syn, mi, mv, seqs, batch, dev):
         cv.set_reference_from(ci)
         p_pays, resets = [], []
         count = 1
-        for k in range(4):
+        for k in range(p_packets(frames)):
             chunk = video[:, 1 + 8 * k: 9 + 8 * k]
             if chunk.shape[1] < 8:  # pad by repeating the last frame (src/integer_codec.cpp:257-261)
                 chunk = torch.cat([chunk] + [chunk[:, -1:]] * (8 - chunk.shape[1]), 1)
             reset = (count + 8) % 8 == 1  # reset_interval 8 (src/integer_codec.cpp:263-264)
-            pay, _ = cv.compress(chunk.reshape(len(ids), 24, H1080, W1080).cpu().numpy(), QP_P, reset)
+            pay, _ = cv.compress(chunk.reshape(len(ids), 24, height, width).cpu().numpy(), QP_P, reset)
             p_pays.append(pay)
             resets.append(reset)
             count += 8
@@ -336,6 +345,10 @@ def bench_decode_ours(args, rank, world, local):
 
     per_step_ms = ms / args.steps
     achieved = 8 * pst["conv_int16_macs"] / (pst["conv_ms"] * 1e-3) / 1e12 if pst["conv_ms"] else None
+    secondary = None
+    if world == 1 and not args.no_secondary:
+        del decoders, sinks
+        secondary = bench_626(ufb, syn, mi, mv, dev, stream, peak)
     return {
         "metric": "INT16 HT-L decoded frames/s (1920x1088, BASELINE config 5)",
         "value": total_frames / (ms_max * 1e-3), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
@@ -366,7 +379,137 @@ def bench_decode_ours(args, rank, world, local):
                      "conv_int16_macs_per_step": pst["conv_int16_macs"]},
         "e2e": {"value": e2e_total / (e2e_ms * 1e-3), "unit": "frames/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
+        "secondary": secondary,
     }
+
+
+def bench_626(ufb, syn, mi, mv, dev, stream, peak):
+    """626x352: the config-5 multi-stream decode at the
+    smaller frame size (64 sequences x 32 frames, seeds 3..66) and the
+    single-stream 120-frame config-4 GOP (seed 3), with per-packet latency."""
+    import torch
+    W, H = 626, 352
+    out = {"metric": "INT16 HT-L decoded frames/s (626x352, BASELINE configs 3-4)", "unit": "frames/s"}
+
+    # multi-stream throughput: two concurrent codec groups, as the main workload
+    groups = encode_sequences(ufb, syn, mi, mv, list(range(SEQS)), SEQS // 2, dev, W, H, FRAMES, seed_base=3)
+    gstreams = [torch.cuda.Stream(dev) for _ in groups]
+    decoders = []
+    for (ids, *_), gs in zip(groups, gstreams):
+        pair = ufb.Codec(mi, len(ids)), ufb.Codec(mv, len(ids))
+        for c in pair:
+            c.set_skip_threshold(SKIP)
+            c.set_stream(gs)
+        decoders.append(pair)
+    pool = ThreadPoolExecutor(max_workers=len(groups))
+
+    def decode_group(g):
+        (ids, i_pay, _, p_pays, resets, _), (di, dv) = groups[g], decoders[g]
+        di.decompress(i_pay, W, H, QP_I, frames=False)
+        dv.set_reference_from(di)
+        n = len(ids)
+        for k, pay in enumerate(p_pays):
+            dv.decompress(pay, W, H, QP_P, resets[k], frames=False)
+            n += len(ids) * min(8, FRAMES - 1 - 8 * k)
+        return n
+
+    def run(steps, profile=False):
+        for pair in decoders:
+            for c in pair:
+                c.stats(reset=True)
+                c.profile(profile)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for gs in gstreams:
+            gs.wait_event(e0)
+        if profile:
+            n = sum(decode_group(g) for _ in range(steps) for g in range(len(groups)))
+        else:
+            n = sum(sum(pool.map(decode_group, range(len(groups)))) for _ in range(steps))
+        for gs in gstreams:
+            stream.wait_stream(gs)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        st = {"conv_int16_macs": 0.0, "conv_ms": 0.0}
+        for pair in decoders:
+            for c in pair:
+                x = c.stats()
+                c.profile(False)
+                for k in st:
+                    st[k] += x[k]
+        return n, e0.elapsed_time(e1), st
+
+    run(2)
+    frames, ms, _ = run(3)
+    _, _, pst = run(1, profile=True)
+    for g, (_, dv) in enumerate(decoders):
+        for k, want in groups[g][5].items():
+            if dv.state_hash(k) != want:
+                raise RuntimeError(f"626x352 group {g}: decoder {k} state differs from the encoder's")
+    achieved = 8 * pst["conv_int16_macs"] / (pst["conv_ms"] * 1e-3) / 1e12 if pst["conv_ms"] else None
+    out["multi_stream"] = {
+        "value": frames / (ms * 1e-3), "unit": "frames/s", "ms_per_step": ms / 3, "steps": 3,
+        "workload": f"{SEQS} seqs x {FRAMES} frames 626x352 (seeds 3..{2 + SEQS}), I + 4 P packets each, "
+                    "qp_i 0 qp_p 20, reset 8, skip 0.2, two concurrent codec groups",
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS(int8)",
+                     "frac": achieved / peak if achieved else None,
+                     "measured_on": "one extra step, groups in turn, every tensor-core convolution bracketed "
+                                    "by CUDA events"}}
+    del decoders, groups
+
+    # single stream: the config-4 GOP (120 frames: I + 15 P packets), batch 1
+    gop = encode_sequences(ufb, syn, mi, mv, [0], 1, dev, W, H, 120, seed_base=3)[0]
+    gs = torch.cuda.Stream(dev)
+    di, dv = ufb.Codec(mi, 1), ufb.Codec(mv, 1)
+    for c in (di, dv):
+        c.set_skip_threshold(SKIP)
+        c.set_stream(gs)
+    _, i_pay, _, p_pays, resets, states = gop
+
+    def gop_decode(events=None):
+        di.decompress(i_pay, W, H, QP_I, frames=False)
+        dv.set_reference_from(di)
+        for k, pay in enumerate(p_pays):
+            if events is not None:
+                events[k][0].record(gs)
+            dv.decompress(pay, W, H, QP_P, resets[k], frames=False)
+            if events is not None:
+                events[k][1].record(gs)
+
+    for _ in range(2):
+        gop_decode()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in p_pays]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(gs)
+    gop_decode(ev)
+    e1.record(gs)
+    torch.cuda.synchronize()
+    for k, want in states.items():
+        if dv.state_hash(k) != want:
+            raise RuntimeError(f"config-4 GOP: decoder {k} state differs from the encoder's")
+    gop_ms = e0.elapsed_time(e1)
+    p_ms = [a.elapsed_time(b) for a, b in ev]
+    out["config4_gop"] = {"value": 120 / (gop_ms * 1e-3), "unit": "frames/s", "ms": gop_ms,
+                          "workload": "one 120-frame 626x352 stream (seed 3): I + 15 P packets, batch 1, host rANS "
+                                      "included"}
+    out["config3_p_packet"] = {"ms_mean": statistics.mean(p_ms), "ms_min": min(p_ms),
+                               "workload": "decode of one 8-frame reset P packet of one 626x352 stream (the GOP's)"}
+    try:
+        with open(os.path.join(ROOT, "tests", "golden", "config3.json")) as f:
+            g = json.load(f)
+        p = [pk.get("decode_seconds") for pk in g["packets"] if pk["type"] == "P" and pk.get("reset")]
+        i = g["packets"][0].get("decode_seconds")
+        if p and p[0] and i:
+            out["reference_cpu"] = {
+                "p_packet_decode_s": p[0], "i_packet_decode_s": i, "cores": g["threads"],
+                "frames_per_s": FRAMES / (i + 4 * p[0]),
+                "source": "the reference's IntegerModel::decompress (oracle/_ref) on the same 626x352 config-3 "
+                          "packets, timed on the build host by tests/golden/make_model_golden.py"}
+    except (OSError, KeyError, ValueError):
+        pass
+    return out
 
 
 def ref_decode_sample(threads):

@@ -24,6 +24,7 @@
 #include <climits>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 namespace ufb {
 
@@ -56,10 +57,22 @@ __device__ __forceinline__ int32_t bilerp_q18(int32_t v00, int32_t v01, int32_t 
     return static_cast<int32_t>((s + ((1 << 17) + neg)) >> 18);
 }
 
+__device__ __forceinline__ uint32_t pack_pair(int32_t a, int32_t b) {
+    return (static_cast<uint32_t>(a) & 0xffffu) | (static_cast<uint32_t>(b) << 16);
+}
+
+// Sign-extending 16-bit shared-memory load at addr + OFF (an immediate).
+template <int OFF>
+__device__ __forceinline__ int32_t lds_s16(uint32_t addr) {
+    int32_t v;
+    asm volatile("ld.shared.s16 %0, [%1+%2];" : "=r"(v) : "r"(addr), "n"(OFF) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void store_pair(int16_t* row, int x, int w, bool pair_ok, bool v0, bool v1, int32_t a,
                                            int32_t b) {
     if (pair_ok && v0 && v1) {
-        *reinterpret_cast<uint32_t*>(row + x) = (static_cast<uint32_t>(a) & 0xffffu) | (static_cast<uint32_t>(b) << 16);
+        *reinterpret_cast<uint32_t*>(row + x) = pack_pair(a, b);
     } else {
         if (v0) row[x] = static_cast<int16_t>(a);
         if (v1) row[x + 1] = static_cast<int16_t>(b);
@@ -162,21 +175,27 @@ __global__ void __launch_bounds__(kThreads, 3)
         return;
     }
 
-    // shared-memory element offsets of the footprint rows inside a stage:
-    // layout [row block][channel][8 rows][128 px]
-    int o0[4], o1[4], d[4];
+    // shared-memory byte offsets of the four footprint samples inside a stage,
+    // layout [row block][channel][8 rows][128 px]; the stage and channel parts
+    // of an address are compile-time immediates of the loads below
+    uint32_t a00[4], a01[4], a10[4], a11[4];
+    const uint32_t ring_s = smem_u32(ring);
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-        const int r0 = y0[p] - wy0, r1 = y1[p] - wy0, xx = x0[p] - wx0;
-        o0[p] = (r0 >> 3) * kBlkElems + (r0 & 7) * kBoxW + xx;
-        o1[p] = (r1 >> 3) * kBlkElems + (r1 & 7) * kBoxW + xx;
-        d[p] = x1[p] - x0[p];
-        if (!valid[p]) o0[p] = o1[p] = d[p] = 0;
+        const int r0 = y0[p] - wy0, r1 = y1[p] - wy0, xx = x0[p] - wx0, dx = x1[p] - x0[p];
+        const uint32_t o0 = 2u * ((r0 >> 3) * kBlkElems + (r0 & 7) * kBoxW + xx);
+        const uint32_t o1 = 2u * ((r1 >> 3) * kBlkElems + (r1 & 7) * kBoxW + xx);
+        a00[p] = valid[p] ? ring_s + o0 : ring_s;
+        a01[p] = valid[p] ? ring_s + o0 + 2u * dx : ring_s;
+        a10[p] = valid[p] ? ring_s + o1 : ring_s;
+        a11[p] = valid[p] ? ring_s + o1 + 2u * dx : ring_s;
     }
     const int blocks = (wh + kRowBlk - 1) / kRowBlk;
     const uint32_t stage_bytes = static_cast<uint32_t>(blocks) * kBlkElems * 2;
     const int stages = cn / kCG;
     const int plane0 = b * c + c0;
+    // interior tiles with paired stores need no per-pixel checks
+    const bool full_tile = pair_ok && tx0 + kTW <= w && ty0 + kTH <= h;
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
         fence_mbar_init();
@@ -194,25 +213,51 @@ __global__ void __launch_bounds__(kThreads, 3)
     if (tid == 0)
         for (; issued < min(kStages, stages); ++issued) issue(issued);
     bool alive = true;
-    for (int s = 0; s < stages; ++s) {
-        if (alive) alive = mbar_wait(&full[s % kStages], (s / kStages) & 1, status, kWarpTimeoutCode);
+    int16_t* o_row0 = orow0 + xs;
+    int16_t* o_row1 = orow1 + xs;
+    // one stage: kCG channels from ring buffer BUF
+    auto consume = [&](auto buf_tag, int s) {
+        constexpr int BUF = decltype(buf_tag)::value;
+        if (alive) alive = mbar_wait(&full[BUF], (s / kStages) & 1, status, kWarpTimeoutCode);
         if (alive) {
-            const int16_t* st = ring + (s % kStages) * kStageElems;
 #pragma unroll
             for (int cc = 0; cc < kCG; ++cc) {
-                const int16_t* sb = st + cc * (kRowBlk * kBoxW);
+                constexpr int kBufBytes = BUF * kStageElems * 2;
                 int32_t r[4];
 #pragma unroll
-                for (int p = 0; p < 4; ++p)
-                    r[p] = bilerp_q18(sb[o0[p]], sb[o0[p] + d[p]], sb[o1[p]], sb[o1[p] + d[p]], wa[p], wb[p], wc[p],
-                                      wd[p]);
-                const long long co = static_cast<long long>(s * kCG + cc) * plane;
-                store_pair(orow0 + co, xs, w, pair_ok, valid[0], valid[1], r[0], r[1]);
-                store_pair(orow1 + co, xs, w, pair_ok, valid[2], valid[3], r[2], r[3]);
+                for (int p = 0; p < 4; ++p) {
+                    int32_t v00, v01, v10, v11;
+                    if (cc == 0) {
+                        v00 = lds_s16<kBufBytes>(a00[p]);
+                        v01 = lds_s16<kBufBytes>(a01[p]);
+                        v10 = lds_s16<kBufBytes>(a10[p]);
+                        v11 = lds_s16<kBufBytes>(a11[p]);
+                    } else {
+                        v00 = lds_s16<kBufBytes + kRowBlk * kBoxW * 2>(a00[p]);
+                        v01 = lds_s16<kBufBytes + kRowBlk * kBoxW * 2>(a01[p]);
+                        v10 = lds_s16<kBufBytes + kRowBlk * kBoxW * 2>(a10[p]);
+                        v11 = lds_s16<kBufBytes + kRowBlk * kBoxW * 2>(a11[p]);
+                    }
+                    r[p] = bilerp_q18(v00, v01, v10, v11, wa[p], wb[p], wc[p], wd[p]);
+                }
+                if (full_tile) {
+                    *reinterpret_cast<uint32_t*>(o_row0) = pack_pair(r[0], r[1]);
+                    *reinterpret_cast<uint32_t*>(o_row1) = pack_pair(r[2], r[3]);
+                } else {
+                    store_pair(o_row0 - xs, xs, w, pair_ok, valid[0], valid[1], r[0], r[1]);
+                    store_pair(o_row1 - xs, xs, w, pair_ok, valid[2], valid[3], r[2], r[3]);
+                }
+                o_row0 += plane;
+                o_row1 += plane;
             }
         }
         __syncthreads();  // every thread is done with this stage's buffer
         if (tid == 0 && alive && issued < stages) issue(issued++);
+    };
+    static_assert(kStages == 2, "the stage loop alternates between two ring buffers");
+    for (int s = 0; s < stages; s += 2) {
+        consume(std::integral_constant<int, 0>{}, s);
+        if (s + 1 < stages) consume(std::integral_constant<int, 1>{}, s + 1);
     }
     // after a timeout, let this CTA's own copies in flight land (bounded)
     // before its shared memory is released

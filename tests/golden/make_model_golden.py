@@ -10,7 +10,8 @@ reconstruct and the DPB states), ``uf::IntegerCodec`` (src/integer_codec.cpp:
 the seeded random-init prepared tables of ``synthetic.make_prepared`` (image
 seed 1, HT-L seed 2) and the inputs come from ``synthetic.synthetic_video``;
 SHA-256 digests of the inputs are stored too, so a test can tell an input
-mismatch from an engine mismatch.
+mismatch from an engine mismatch, and so are the reference's CPU seconds per
+encode and decode (the thread count is recorded).
 
 Cases (the reference's FFmpeg testsrc2 clip is not
 available, the seeded synthetic scene stands in for it):
@@ -95,35 +96,41 @@ def packet_case(ref, ora, syn, width, height, seed, p_resets, decode, log):
         m.set_skip_threshold(SKIP)
     t = time.time()
     first, frames = image.compress(ora.from_bytes(video[0:1].reshape(1, 3, height, width)), 0)
-    log(f"  I encode {time.time() - t:.0f} s")
+    dt = time.time() - t
+    log(f"  I encode {dt:.0f} s")
     rec["packets"].append({"type": "I", "payload_sha256": sha(first), "payload_bytes": len(first),
-                           "frames": frames_record(ref, frames, width, height)})
+                           "frames": frames_record(ref, frames, width, height), "encode_seconds": round(dt, 2)})
     hv.add_ref_feature_from_frame(frames[0])
     payloads = []
     for k, reset in enumerate(p_resets):
         chunk = video[1 + 8 * k: 9 + 8 * k].reshape(1, 24, height, width)
         t = time.time()
         payload, frames = hv.compress(ora.from_bytes(chunk), 20, reset)
-        log(f"  P{k + 1} encode {time.time() - t:.0f} s")
+        dt = time.time() - t
+        log(f"  P{k + 1} encode {dt:.0f} s")
         payloads.append(payload)
         rec["packets"].append({"type": "P", "reset": bool(reset), "payload_sha256": sha(payload),
                                "payload_bytes": len(payload), "frames": frames_record(ref, frames, width, height),
-                               "states": states(hv)})
+                               "states": states(hv), "encode_seconds": round(dt, 2)})
     if decode:
         image_d, hv_d = ref.model("image", img_t), ref.model("htl", vid_t)
         for m in (image_d, hv_d):
             m.set_skip_threshold(SKIP)
         t = time.time()
         frames = image_d.decompress(first, width, height, 0)
-        log(f"  I decode {time.time() - t:.0f} s")
+        dt = time.time() - t
+        log(f"  I decode {dt:.0f} s")
         rec["packets"][0]["decoded"] = frames_record(ref, frames, width, height)
+        rec["packets"][0]["decode_seconds"] = round(dt, 2)
         hv_d.add_ref_feature_from_frame(frames[0])
         for k, reset in enumerate(p_resets):
             pk = rec["packets"][1 + k]
             t = time.time()
             frames = hv_d.decompress(payloads[k], width, height, 20, reset)
-            log(f"  P{k + 1} decode {time.time() - t:.0f} s")
+            dt = time.time() - t
+            log(f"  P{k + 1} decode {dt:.0f} s")
             pk["decoded"] = frames_record(ref, frames, width, height)
+            pk["decode_seconds"] = round(dt, 2)
             pk["decoded_states"] = states(hv_d)
     return rec
 
@@ -139,12 +146,16 @@ def gop_case(ref, syn, width, height, frames, seed, threads, log):
     enc = ref.codec(img_t, ii, vid_t, vi, "htl", SKIP, threads=threads)
     t = time.time()
     data, nframes, packets = enc.encode(video, width, height, 0, 20, 8, -1)
-    log(f"  encode {time.time() - t:.0f} s, {packets} packets, {len(data)} bytes")
-    rec.update({"archive_sha256": sha(data), "archive_bytes": len(data), "packets": packets})
+    dt = time.time() - t
+    log(f"  encode {dt:.0f} s, {packets} packets, {len(data)} bytes")
+    rec.update({"archive_sha256": sha(data), "archive_bytes": len(data), "packets": packets,
+                "encode_seconds": round(dt, 1)})
     dec = ref.codec(img_t, ii, vid_t, vi, "htl", SKIP, threads=threads)
     t = time.time()
     digest, yuv, dpk = dec.decode(data, frames, packets, width, height)
-    log(f"  decode {time.time() - t:.0f} s")
+    dt = time.time() - t
+    log(f"  decode {dt:.0f} s")
+    rec["decode_seconds"] = round(dt, 1)
     assert dpk == packets
     rec.update({"decoded_yuv_sha256": digest, "frame_yuv_sha256": [sha(y) for y in yuv]})
     return rec
