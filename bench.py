@@ -263,14 +263,18 @@ def bench_decode_ours(args, rank, world, local):
         sinks.append(tuple(torch.empty((len(ids), f, yuv_bytes), dtype=torch.uint8, pin_memory=True).numpy()
                            for f in (1, 8)))
 
+    host_s = [0.0] * len(groups)  # host entropy-coding seconds per codec group (Codec::host_seconds)
+
     def decode_group(g, yuv):
         """One codec group: I packet, then the 4 P packets of each of its streams."""
         (ids, i_pay, _, p_pays, resets, _), (di, dv), (si, sp) = groups[g], decoders[g], sinks[g]
         di.decompress(i_pay, W1080, H1080, QP_I, frames=False, yuv_out=si if yuv else None)
+        host_s[g] += di.host_seconds()
         dv.set_reference_from(di)
         frames = len(ids)
         for k in range(4):
             dv.decompress(p_pays[k], W1080, H1080, QP_P, resets[k], frames=False, yuv_out=sp if yuv else None)
+            host_s[g] += dv.host_seconds()
             frames += len(ids) * (8 if k < 3 else FRAMES - 1 - 24)
         return frames
 
@@ -317,7 +321,10 @@ def bench_decode_ours(args, rank, world, local):
         for _ in range(args.warmup):
             step(False)
         torch.cuda.synchronize()
+        for g in range(len(groups)):
+            host_s[g] = 0.0
         frames, ms, st = timed(False, args.steps)
+        host_per_step = [x / args.steps for x in host_s]
     clocks = clk.summary()
     # roofline of the tensor-core convolutions: one more step, groups in turn,
     # every convolution bracketed by events (not part of the timed value)
@@ -362,6 +369,10 @@ def bench_decode_ours(args, rank, world, local):
                    "parallelism": f"stream sharding x{world}, no inter-GPU communication"},
         "gpu_launches": int(st["launches"]),
         "clocks": clocks,
+        "host": {"entropy_seconds_per_step_per_group": host_per_step,
+                 "note": "host rANS (and its device<->host hand-offs) of each concurrent codec group per timed "
+                         "step (Codec host_seconds), beside ms_per_step: where a rank's host work approaches "
+                         "its step time, the host, not the GPU, bounds that rank"},
         "roofline": {"bound": "tensor", "kernel": "conv_i16_tc_kernel (all tensor-core convolution launches)",
                      "achieved": achieved, "peak": peak, "unit": "TOPS(int8)",
                      "frac": achieved / peak if achieved else None,
