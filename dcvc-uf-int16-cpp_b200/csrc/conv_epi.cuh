@@ -77,7 +77,9 @@ struct LutView {
 
     __device__ __forceinline__ int32_t operator()(int32_t v) const {
         if (win) {
-            const int32_t r = win[min(max(v - start, 0), n - 1)];
+            int32_t i;  // max(min(v - start, n - 1), 0) in one instruction
+            asm("min.relu.s32 %0, %1, %2;" : "=r"(i) : "r"(v - start), "r"(n - 1));
+            const int32_t r = win[i];
             return v > hi ? v : r;
         }
         return __ldg(global + v + 32768);

@@ -399,6 +399,11 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         const bool issuer = warp == kFirstEpiWarp && lane == 0;  // residual prefetches
         const int ew = warp - kFirstEpiWarp;
         uint8_t* stage = staging + ew * kStage;  // this warp's own stage
+        // Multipliers the compiler cannot see: products with them stay integer
+        // multiply-adds on the FMA pipe instead of becoming shift-adds on the
+        // ALU pipe, which the epilogue's compares, selects and shifts keep busy.
+        int32_t c8 = 8, c256 = 256;
+        asm volatile("" : "+r"(c8), "+r"(c256));
         int res_issued = 0, res_seen = 0;
         const Act& out = args.out;
         int ti = 0;
@@ -440,7 +445,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
 #pragma unroll
                     for (int t = 0; t < 32; ++t) {
                         const int j = 32 * i + t;
-                        V[j] = static_cast<int32_t>(hh[t]) * 8 + (static_cast<int32_t>(xx[t]) >> 5);
+                        V[j] = static_cast<int32_t>(hh[t]) * c8 + (static_cast<int32_t>(xx[t]) >> 5);
                         F[j / 6] |= (xx[t] & 31u) << (5 * (j % 6));
                     }
                 }
@@ -458,7 +463,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         for (int t = 0; t < 4; ++t) {
                             const int j = 16 * h + 4 * q + t;
                             const int32_t f = static_cast<int32_t>((F[j / 6] >> (5 * (j % 6))) & 31u);
-                            r[t] = finish_rna(V[j], static_cast<int32_t>(ll[4 * q + t]) + (f << 8) + 4096) + bb[t];
+                            r[t] = finish_rna(V[j], f * c256 + (static_cast<int32_t>(ll[4 * q + t]) + 4096)) + bb[t];
                         }
                         p[8 * h + 2 * q] = pack2_sat(r[0], r[1]);
                         p[8 * h + 2 * q + 1] = pack2_sat(r[2], r[3]);
@@ -482,7 +487,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
 #pragma unroll
                     for (int t = 0; t < 32; ++t) {
                         const int32_t x = static_cast<int32_t>(xx[t]);
-                        const int32_t U = static_cast<int32_t>(ll[t]) + ((x & 31) << 8) + 4096;
+                        const int32_t U = (x & 31) * c256 + (static_cast<int32_t>(ll[t]) + 4096);
                         W[32 * i + t] = (x >> 5) + (U >> 13);
                         ties[i] |= static_cast<uint32_t>((U & 8191) == 0) << t;
                     }
@@ -500,7 +505,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
 #pragma unroll
                         for (int t = 0; t < 4; ++t) {
                             const int j = 16 * h + 4 * q + t;
-                            const int32_t T = static_cast<int32_t>(hh[4 * q + t]) * 8 + W[j];
+                            const int32_t T = static_cast<int32_t>(hh[4 * q + t]) * c8 + W[j];
                             r[t] = T - static_cast<int32_t>(((ties[j / 32] >> (j % 32)) & 1u) & (T <= 0)) + bb[t];
                         }
                         p[8 * h + 2 * q] = pack2_sat(r[0], r[1]);

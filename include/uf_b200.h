@@ -63,8 +63,10 @@ int ufb_device_status(int device);
  * x [n, ci, h, w], weight [co, ci/groups, kh, kw], bias [co] or NULL with
  * bias_bits 16 (int16, the reference's type) or 32 (int32, widened exactly as
  * src/int16_ops.cpp:163-167 does on the CPU path), out [n, co, oh, ow].
- * groups == 1, stride 1 and ci*kh*kw <= 8192 run on the tcgen05 tensor cores;
- * other geometries use the direct int64 kernel (as the reference does). */
+ * groups == 1, stride 1 or 2 (equal in both directions) and ci*kh*kw <= 8192
+ * run on the tcgen05 tensor cores, depthwise 3x3 (stride 1, padding 1, int16
+ * or no bias) on the depthwise kernel; other geometries use the direct int64
+ * kernel (as the reference does). */
 int ufb_conv2d(const int16_t* x, int n, int ci, int h, int w, const int16_t* weight, int co, int kh, int kw,
                const void* bias, int bias_bits, int stride_h, int stride_w, int pad_h, int pad_w, int groups,
                int16_t* out, void* stream);
@@ -104,7 +106,9 @@ int ufb_wsilu4(const int16_t* x, int n, int c4, int h, int w, const int16_t* tab
  * reference's only warp is the float DCVC-FM kernel block_mc_forward,
  * src/dcvc_fm_motion.cu:29-111, which no build target compiles).
  * feature [n, c, h, w] int16, flow [n, 2, h, w] int16 in Q9 pixels (x, y),
- * border clamp, out = sat(rna(sum of Q18 bilinear weights * taps / 2^18)). */
+ * border clamp, out = sat(rna(sum of Q18 bilinear weights * taps / 2^18)).
+ * Pipeline timeouts of its bounded waits are reported by ufb_device_status
+ * (code 11). */
 int ufb_warp(const int16_t* feature, const int16_t* flow, int n, int c, int h, int w, int16_t* out,
              void* stream);
 
