@@ -551,8 +551,10 @@ void fill_prepared(uf::PreparedModel& p, const char* variant, const char* identi
 extern "C" {
 
 // IntegerCodec(image, video, variant, kCPU, skip_threshold).  The constructor
-// applies the reference's inference environment (which sets one intra-op
-// thread); `threads` > 0 is applied afterwards.  video_count < 0: no video model.
+// applies the reference's inference environment, which sets one intra-op
+// thread (src/inference_environment.cpp:11-21); `threads` > 0 is requested
+// afterwards, but the codec's loops were observed to keep running on one core,
+// as the reference runs them by design.  video_count < 0: no video model.
 void* ufref_codec_new(const char* variant, double skip_threshold, int threads,
                       const char* image_identity, int image_count, const char* const* image_names,
                       const int* image_dtypes, const int* image_ndims, const int64_t* image_shapes,
