@@ -71,6 +71,8 @@ def parse():
                    help="sequences in the job (default: BASELINE config 5's 64); smaller values are for profiling")
     p.add_argument("--shapes", action="store_true", help="print per launch shape convolution time to stderr")
     p.add_argument("--no-secondary", action="store_true", help="skip the 626x352 measurements (decode workload, N=1)")
+    p.add_argument("--groups", type=int, default=2,
+                   help="concurrent codec groups per rank (each with its own CUDA stream and host thread)")
     return p.parse_args()
 
 
@@ -241,7 +243,8 @@ def bench_decode_ours(args, rank, world, local):
     stream = torch.cuda.current_stream(dev)
     seqs = shard(rank, world, args.seqs)
     # at least two codec groups per rank (when it has two streams), so host rANS overlaps GPU work
-    batch = min(32, max(1, (len(seqs) + 1) // 2))
+    groups_wanted = max(2, args.groups)
+    batch = max(1, (len(seqs) + groups_wanted - 1) // groups_wanted)
     mi = ufb.Model("image", syn.prepared("image", 1), device=local)
     mv = ufb.Model("htl", syn.prepared("htl", 2), device=local)
     groups = encode_sequences(ufb, syn, mi, mv, seqs, batch, dev)
