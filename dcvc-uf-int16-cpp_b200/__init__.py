@@ -52,6 +52,7 @@ def library():
         L.ufb_warp.argtypes = [vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp]
         L.ufb_device_status.argtypes = [C.c_int]
         L.ufb_set_conv_max_ctas.argtypes = [C.c_int]
+        L.ufb_set_conv_narrow.argtypes = [C.c_int]
         _LIB = L
     return _LIB
 
@@ -74,6 +75,12 @@ def _cuda(t: torch.Tensor, dtype, what: str) -> torch.Tensor:
 def set_conv_max_ctas(n: int) -> None:
     """Testing aid: cap the persistent convolution grid at n CTAs (0: one per SM)."""
     _check(library().ufb_set_conv_max_ctas(int(n)))
+
+
+def set_conv_narrow(enable: bool) -> None:
+    """Testing aid: enable or disable the narrow convolution recombination
+    (identical outputs either way)."""
+    _check(library().ufb_set_conv_narrow(1 if enable else 0))
 
 
 def device_status(device: int = 0) -> int:

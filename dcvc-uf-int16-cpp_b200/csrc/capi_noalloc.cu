@@ -63,7 +63,10 @@ extern "C" int ufb_conv2d_noalloc(const int16_t* x, int n, int ci, int h, int w,
     uint8_t* base = scratch_for_current_device();
     if (!base) return last_code();
 
-    const bool tensor_core = groups == 1 && sh == 1 && sw == 1 && static_cast<long long>(ci) * kh * kw <= kTcMaxReduction;
+    // (a full 8192-term reduction with an int32 bias could wrap the 32-bit epilogue sum)
+    const long long k_total = static_cast<long long>(ci) * kh * kw;
+    const bool tensor_core = groups == 1 && sh == 1 && sw == 1 &&
+                             (k_total < kTcMaxReduction || (k_total == kTcMaxReduction && bias_bits != 32));
     if (!tensor_core) {
         // the direct int64 kernel reads NCHW in place and needs no scratch
         return cuda_ok(conv_direct(out, x, weight, bias_bits ? bias : nullptr, bias_bits == 32, n, ci, co, h, w, oh,

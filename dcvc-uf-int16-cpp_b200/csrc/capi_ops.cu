@@ -88,8 +88,10 @@ int conv_dispatch(const int16_t* x, int n, int ci, int h, int w, const int16_t* 
         pw == 1 && bias_bits != 32)
         return conv_depthwise_path(x, n, ci, h, w, weight, bias_bits ? bias : nullptr, out, s);
     // stride 1, or stride 2 in both directions (TMA element strides)
+    // (a full 8192-term reduction with an int32 bias could wrap the 32-bit epilogue sum)
+    const long long k_total = static_cast<long long>(ci) * kh * kw;
     const bool tc_ok = allow_tc && groups == 1 && sh == sw && (sh == 1 || sh == 2) &&
-                       static_cast<long long>(ci) * kh * kw <= kTcMaxReduction;
+                       (k_total < kTcMaxReduction || (k_total == kTcMaxReduction && bias_bits != 32));
     if (tc_ok)
         return conv_tc_path(x, n, ci, h, w, weight, co, kh, kw, bias, bias_bits, sh, ph, pw, oh, ow, out, s);
     if (!allow_direct && !allow_tc) return err(UFB_EINVAL, "no convolution path");
@@ -107,6 +109,13 @@ int ufb_set_conv_max_ctas(int n) {
     clear_error();
     if (n < 0) return err(UFB_EINVAL, "CTA cap must be >= 0");
     tc_set_max_ctas(n);
+    return UFB_OK;
+}
+
+int ufb_set_conv_narrow(int enable) {
+    clear_error();
+    if (enable != 0 && enable != 1) return err(UFB_EINVAL, "narrow switch must be 0 or 1");
+    tc_set_narrow(enable != 0);
     return UFB_OK;
 }
 

@@ -86,6 +86,19 @@ struct LutView {
     }
 };
 
+// lut[sat16(v + start)] - start through a window of differences
+// d[i] = lut[start + i] - (start + i), i in [0, last], of a table that is
+// lut[start] below start and the identity above start + last (or whose window
+// reaches 32767); cap = 32767 - start.  The two clamps of v do the int16
+// saturation: below the window d[0] + 0 = lut[start] - start, inside it
+// d[v] + v, above it d[last] + v = v - start (capped at 32767 - start).
+__device__ __forceinline__ int32_t lut_window(const int16_t* d, int last, int cap, int32_t v) {
+    int32_t i, c;
+    asm("min.relu.s32 %0, %1, %2;" : "=r"(i) : "r"(v), "r"(last));
+    asm("min.relu.s32 %0, %1, %2;" : "=r"(c) : "r"(v), "r"(cap));
+    return d[i] + c;
+}
+
 // Fused elementwise step applied by the epilogue (compile-time, so each
 // kernel instantiation is short straight-line code).
 enum EpiMode : int { kEpiPlain = 0, kEpiLut = 1, kEpiRes = 2, kEpiWsilu4 = 3, kEpiShuffle2 = 4 };

@@ -238,7 +238,7 @@ __device__ __forceinline__ void tma_store_quarter(const CUtensorMap* map, const 
         tma_store_3d(map, src, c0, plane, static_cast<int>(tc.p0) + quarter * 32);
 }
 
-template <bool SPATIAL, int MODE, int SIGNED>
+template <bool SPATIAL, int MODE, int SIGNED, bool NARROW>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapOut, const __grid_constant__ CUtensorMap mapRes1,
@@ -279,20 +279,26 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         tmem_alloc(&tmem_holder, kTmemCols);
         tmem_relinquish();
     }
+    // window start of the fused table step: the staged bias carries -lut_start
+    const int lut_start = (MODE == kEpiLut || MODE == kEpiWsilu4) && args.epi.lut_n > 0 ? args.epi.lut_start : 0;
     // the whole bias vector, zero padded to the tile grid, once per CTA
     for (int i = threadIdx.x; i < args.n_tiles * kBN; i += kThreads) {
         long long b = 0;
         if (args.epi.bias && i < args.co)
             b = args.epi.bias32 ? static_cast<const int32_t*>(args.epi.bias)[i]
                                 : static_cast<const int16_t*>(args.epi.bias)[i];
-        bias_s[i] = static_cast<BiasT>(MODE == kEpiRes ? b : stage_bias(b));
+        bias_s[i] = static_cast<BiasT>(MODE == kEpiRes ? b : stage_bias(b) - lut_start);
     }
-    LutView lut{args.epi.lut, nullptr, 0, 0, 0};
+    // table window as differences lut[v] - v (the host checked that they fit
+    // int16); lut_window() turns them back into lut[sat16(v)]
+    const LutView lut{args.epi.lut, nullptr, 0, 0, 0};  // whole table (no window)
+    const int16_t* lut_d = nullptr;
     if ((MODE == kEpiLut || MODE == kEpiWsilu4) && args.epi.lut_n > 0) {
         for (int i = threadIdx.x; i < args.epi.lut_n; i += kThreads)
-            lut_s[i] = args.epi.lut[args.epi.lut_start + 32768 + i];
-        lut = LutView{args.epi.lut, lut_s, args.epi.lut_start, args.epi.lut_n, args.epi.lut_hi};
+            lut_s[i] = static_cast<int16_t>(args.epi.lut[lut_start + 32768 + i] - (lut_start + i));
+        lut_d = lut_s;
     }
+    const int lut_last = args.epi.lut_n - 1, lut_cap = 32767 - lut_start;
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -303,10 +309,15 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         if (lane == 0) {
             prefetch_tmap(&mapA);
             prefetch_tmap(&mapB);
-            int it = 0, s = 0;
+            int it = 0, s = 0, ti = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x) {
+            for (int tile = blockIdx.x; ok && tile < args.total_tiles; tile += gridDim.x, ++ti) {
                 const TileCoord tc = tile_coord<SPATIAL>(args, tile);
+                // weight rows of the tile: low-byte block at row w_row, high-byte block
+                // 128 rows on; even tiles stack them high over low, odd tiles low over high
+                const int w_row = (tc.co0 / kBN) * 2 * kBN;
+                const int first_rows = (ti & 1) ? w_row : w_row + kBN;
+                const int second_rows = (ti & 1) ? w_row + kBN : w_row;
                 for (int k = 0; k < num_k; ++k, ++it) {
                     if (it >= kStages && !mbar_wait(&empty_bar[s], ((it / kStages) - 1) & 1, args.status, 1)) {
                         ok = false;
@@ -326,7 +337,8 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         tma_load_3d(st, &mapA, &full_bar[s], c0, 0, static_cast<int>(tc.p0));
                         tma_load_3d(st + kABytes, &mapA, &full_bar[s], c0, 1, static_cast<int>(tc.p0));
                     }
-                    tma_load_2d(st + 2 * kABytes, &mapB, &full_bar[s], tap * args.cpad + c0, (tc.co0 / kBN) * 2 * kBN);
+                    tma_load_2d(st + 2 * kABytes, &mapB, &full_bar[s], tap * args.cpad + c0, first_rows);
+                    tma_load_2d(st + 2 * kABytes + kBN * kBK, &mapB, &full_bar[s], tap * args.cpad + c0, second_rows);
                     issued = it + 1;
                     if (++s == kStages) s = 0;
                 }
@@ -349,7 +361,17 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_ll = tmem + (ti & 1) * kBN, d_x = d_ll + kBN, d_hh = d_ll + 2 * kBN;
+                // Accumulator slots (columns): even tiles HH [0, 128), X [128, 256),
+                // LL [256, 384); odd tiles LL [128, 256), X [256, 384), HH [384, 512).
+                // Both sets keep LL and X in the two slots they share, HH in the
+                // slot of their own, and the weight tile is stacked [wh; wl] for
+                // even tiles and [wl; wh] for odd ones, so one N=256 MMA of the
+                // low activation bytes always lands at column 128 and one of the
+                // high bytes at column 0 (even) or 256 (odd).
+                const bool even = (ti & 1) == 0;
+                const uint32_t d_ll = tmem + (even ? 2 : 1) * kBN, d_x = tmem + (even ? 1 : 2) * kBN,
+                               d_hh = tmem + (even ? 0 : 3) * kBN;
+                const uint32_t d_lo2 = tmem + kBN, d_hi2 = tmem + (even ? 0 : 2) * kBN;
                 for (int k = 0; k < num_k; ++k, ++it) {
                     if (!mbar_wait(&full_bar[s], (it / kStages) & 1, args.status, 2)) {
                         ok = false;
@@ -357,19 +379,20 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     }
                     tc_fence_after();
                     const uint32_t base = smem_u32(smem + size_t(s) * kStageBytes);
-                    const uint32_t a_lo = base, a_hi = base + kABytes, b_lo = base + 2 * kABytes,
-                                   b_hi = b_lo + kBN * kBK;
+                    const uint32_t a_lo = base, a_hi = base + kABytes, b_first = base + 2 * kABytes,
+                                   b_second = b_first + kBN * kBK;
+                    const uint32_t b_lo = even ? b_second : b_first, b_hi = even ? b_first : b_second;
 #pragma unroll
                     for (int kk = 0; kk < kBK / 32; ++kk) {
                         const uint32_t o = kk * 32;
                         const bool first = k == 0 && kk == 0;
                         if (SIGNED) {
-                            mma_i8(d_ll, sw128_desc(a_lo + o), sw128_desc(b_lo + o), i_us2, first ? 0u : 1u);
+                            mma_i8(d_lo2, sw128_desc(a_lo + o), sw128_desc(b_first + o), i_us2, first ? 0u : 1u);
                             if (first) {
                                 mma_i8(d_x, sw128_desc(a_hi + o), sw128_desc(b_lo + o), i_ss, 1u);
                                 mma_i8(d_hh, sw128_desc(a_hi + o), sw128_desc(b_hi + o), i_ss, 0u);
                             } else {
-                                mma_i8(d_x, sw128_desc(a_hi + o), sw128_desc(b_lo + o), i_ss2, 1u);
+                                mma_i8(d_hi2, sw128_desc(a_hi + o), sw128_desc(b_first + o), i_ss2, 1u);
                             }
                         } else {
                             const uint32_t acc = first ? 0u : 1u;
@@ -426,90 +449,93 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
             if (MODE == kEpiRes) ++res_issued;
             if (!mbar_wait(&tmem_full, ti & 1, args.status, 4)) break;
             tc_fence_after();
-            uint32_t p[kWords];
-            if ((ti & 1) == 0) {
-                // set at [0, 384); the next tile's set [128, 512) overlaps X and HH.
-                // Drain them 32 columns at a time, folding each pair into
-                // V = 8 HH + (X >> 5) and 5-bit fields X & 31 (six per word).
-                int32_t V[kCols];
-                uint32_t F[(kCols + 5) / 6];
+            uint32_t p[kWords];   // packed int16 pairs of the kCols outputs
+            int32_t o4[kCols / 4];  // wsilu4: the kCols / 4 reduced outputs
+            // LL and X sit in the two slots every accumulator set shares, HH in
+            // the set's own slot (see the MMA warp)
+            const bool even = (ti & 1) == 0;
+            const uint32_t a_ll = acc + (even ? 2 : 1) * kBN, a_x = acc + (even ? 1 : 2) * kBN,
+                           a_hh = acc + (even ? 0 : 3) * kBN;
+            // Drain LL and X 32 columns at a time, then hand the shared slots back
+            // to the MMA warp.  NARROW: D = P = LL + 256 X + 4096 (fits 32 bits
+            // for this layer's weights), so S + 4096 = 65536 HH + P.  Otherwise
+            // D = (X >> 5) + (U >> 13) with U = LL + 256 (X & 31) + 4096 and a
+            // tie bit U % 8192 == 0, so S + 4096 = 8192 (8 HH + D) + (U & 8191).
+            int32_t D[kCols];
+            uint32_t ties[kLd];
 #pragma unroll
-                for (int i = 0; i < (kCols + 5) / 6; ++i) F[i] = 0;
+            for (int i = 0; i < kLd; ++i) {
+                uint32_t ll[32], xx[32];
+                tmem_ld32(a_ll + 32 * i, ll);
+                tmem_ld32(a_x + 32 * i, xx);
+                tmem_wait_ld();
+                if (i == kLd - 1) release_tmem(&tmem_empty, lane);
+                ties[i] = 0;
 #pragma unroll
-                for (int i = 0; i < kLd; ++i) {
-                    uint32_t xx[32], hh[32];
-                    tmem_ld32(acc + kBN + 32 * i, xx);
-                    tmem_ld32(acc + 2 * kBN + 32 * i, hh);
-                    tmem_wait_ld();
-                    if (i == kLd - 1) release_tmem(&tmem_empty, lane);
-#pragma unroll
-                    for (int t = 0; t < 32; ++t) {
-                        const int j = 32 * i + t;
-                        V[j] = static_cast<int32_t>(hh[t]) * c8 + (static_cast<int32_t>(xx[t]) >> 5);
-                        F[j / 6] |= (xx[t] & 31u) << (5 * (j % 6));
-                    }
-                }
-#pragma unroll
-                for (int h = 0; h < kCols / 16; ++h) {
-                    uint32_t ll[16];
-                    tmem_ld16(acc + 16 * h, ll);  // LL stays clear of the next tile's set
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int4 b = load_bias4(bias_s + cbase + 16 * h + 4 * q);
-                        const int bb[4] = {b.x, b.y, b.z, b.w};
-                        int32_t r[4];
-#pragma unroll
-                        for (int t = 0; t < 4; ++t) {
-                            const int j = 16 * h + 4 * q + t;
-                            const int32_t f = static_cast<int32_t>((F[j / 6] >> (5 * (j % 6))) & 31u);
-                            r[t] = finish_rna(V[j], f * c256 + (static_cast<int32_t>(ll[4 * q + t]) + 4096)) + bb[t];
-                        }
-                        p[8 * h + 2 * q] = pack2_sat(r[0], r[1]);
-                        p[8 * h + 2 * q + 1] = pack2_sat(r[2], r[3]);
-                    }
-                }
-            } else {
-                // set at [128, 512); the next tile's set [0, 384) overlaps LL and X.
-                // Drain them 32 columns at a time into U = LL + 256 (X & 31) + 4096,
-                // W = (X >> 5) + (U >> 13) and a tie bit (U % 8192 == 0).
-                const uint32_t a = acc + kBN;
-                int32_t W[kCols];
-                uint32_t ties[kLd];
-#pragma unroll
-                for (int i = 0; i < kLd; ++i) {
-                    uint32_t ll[32], xx[32];
-                    tmem_ld32(a + 32 * i, ll);
-                    tmem_ld32(a + kBN + 32 * i, xx);
-                    tmem_wait_ld();
-                    if (i == kLd - 1) release_tmem(&tmem_empty, lane);
-                    ties[i] = 0;
-#pragma unroll
-                    for (int t = 0; t < 32; ++t) {
-                        const int32_t x = static_cast<int32_t>(xx[t]);
+                for (int t = 0; t < 32; ++t) {
+                    const int32_t x = static_cast<int32_t>(xx[t]);
+                    if (NARROW) {
+                        D[32 * i + t] = x * c256 + (static_cast<int32_t>(ll[t]) + 4096);
+                    } else {
                         const int32_t U = (x & 31) * c256 + (static_cast<int32_t>(ll[t]) + 4096);
-                        W[32 * i + t] = (x >> 5) + (U >> 13);
+                        D[32 * i + t] = (x >> 5) + (U >> 13);
                         ties[i] |= static_cast<uint32_t>((U & 8191) == 0) << t;
                     }
                 }
+            }
+            // HH 16 columns at a time: T = floor((S + 4096) / 8192) rounds half up;
+            // an exact tie with S < 0 (T <= 0) takes T - 1 (half away from zero).
+            // Then the bias and the fused table step.
 #pragma unroll
-                for (int h = 0; h < kCols / 16; ++h) {
-                    uint32_t hh[16];
-                    tmem_ld16(a + 2 * kBN + 16 * h, hh);  // HH stays clear of the next tile's set
-                    tmem_wait_ld();
+            for (int h = 0; h < kCols / 16; ++h) {
+                uint32_t hh[16];
+                tmem_ld16(a_hh + 16 * h, hh);
+                tmem_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int4 b = load_bias4(bias_s + cbase + 16 * h + 4 * q);
-                        const int bb[4] = {b.x, b.y, b.z, b.w};
-                        int32_t r[4];
+                for (int q = 0; q < 4; ++q) {
+                    const int4 b = load_bias4(bias_s + cbase + 16 * h + 4 * q);
+                    const int bb[4] = {b.x, b.y, b.z, b.w};
+                    int32_t r[4];
 #pragma unroll
-                        for (int t = 0; t < 4; ++t) {
-                            const int j = 16 * h + 4 * q + t;
-                            const int32_t T = static_cast<int32_t>(hh[4 * q + t]) * c8 + W[j];
-                            r[t] = T - static_cast<int32_t>(((ties[j / 32] >> (j % 32)) & 1u) & (T <= 0)) + bb[t];
+                    for (int t = 0; t < 4; ++t) {
+                        const int j = 16 * h + 4 * q + t;
+                        const int32_t H8 = static_cast<int32_t>(hh[4 * q + t]) * c8;
+                        int32_t T;
+                        bool tie;
+                        if (NARROW) {
+                            T = H8 + (D[j] >> 13);
+                            tie = (D[j] & 8191) == 0;
+                        } else {
+                            T = H8 + D[j];
+                            tie = (ties[j / 32] >> (j % 32)) & 1u;
                         }
+                        r[t] = T - static_cast<int32_t>(tie & (T <= 0)) + bb[t];
+                    }
+                    if ((MODE == kEpiLut || MODE == kEpiWsilu4) && lut_d) {
+                        // table window: r is conv - window start (the staged bias
+                        // carries the shift)
+                        int32_t v[4];
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) v[t] = lut_window(lut_d, lut_last, lut_cap, r[t]);
+                        if (MODE == kEpiWsilu4) {
+                            o4[4 * h + q] = v[0] + v[1] + v[2] + v[3] + 4 * lut_start;
+                        } else {
+                            p[8 * h + 2 * q] = pack2(v[0] + lut_start, v[1] + lut_start);
+                            p[8 * h + 2 * q + 1] = pack2(v[2] + lut_start, v[3] + lut_start);
+                        }
+                    } else {
                         p[8 * h + 2 * q] = pack2_sat(r[0], r[1]);
                         p[8 * h + 2 * q + 1] = pack2_sat(r[2], r[3]);
+                        if (MODE == kEpiLut) {
+                            // whole table from global memory
+                            p[8 * h + 2 * q] = pack2(lut(lo16(p[8 * h + 2 * q])), lut(hi16(p[8 * h + 2 * q])));
+                            p[8 * h + 2 * q + 1] =
+                                pack2(lut(lo16(p[8 * h + 2 * q + 1])), lut(hi16(p[8 * h + 2 * q + 1])));
+                        }
+                        if (MODE == kEpiWsilu4) {
+                            const uint32_t a0 = p[8 * h + 2 * q], a1 = p[8 * h + 2 * q + 1];
+                            o4[4 * h + q] = lut(lo16(a0)) + lut(hi16(a0)) + lut(lo16(a1)) + lut(hi16(a1));
+                        }
                     }
                 }
             }
@@ -544,11 +570,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                 }
                 continue;
             }
-            // fused elementwise step (residual rows outside the image read nothing)
-            if (MODE == kEpiLut) {
-#pragma unroll
-                for (int i = 0; i < kWords; ++i) p[i] = pack2(lut(lo16(p[i])), lut(hi16(p[i])));
-            }
+            // fused residual step (residual rows outside the image read nothing)
             if (MODE == kEpiRes) {
                 // first residual from the stage (64-byte swizzle, like the output)
                 ++res_seen;
@@ -637,13 +659,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                 // at once as [plane][32 pixels][16 channels] (16-byte rows)
 #pragma unroll
                 for (int h = 0; h < kCols / 16; ++h) {
-                    int32_t r[4];
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        const uint32_t a0 = p[8 * h + 2 * g], a1 = p[8 * h + 2 * g + 1];
-                        r[g] = lut(lo16(a0)) + lut(hi16(a0)) + lut(lo16(a1)) + lut(hi16(a1));
-                    }
-                    const uint32_t w0 = pack2_sat(r[0], r[1]), w1 = pack2_sat(r[2], r[3]);
+                    const uint32_t w0 = pack2_sat(o4[4 * h], o4[4 * h + 1]), w1 = pack2_sat(o4[4 * h + 2], o4[4 * h + 3]);
                     *reinterpret_cast<uint32_t*>(stage + lane * (kCols / 4) + 4 * h) = __byte_perm(w0, w1, 0x6420);
                     *reinterpret_cast<uint32_t*>(stage + 8 * kCols + lane * (kCols / 4) + 4 * h) =
                         __byte_perm(w0, w1, 0x7531);
@@ -748,6 +764,7 @@ bool encode(CUtensorMap* map, void* base, int rank, const cuuint64_t* dims, cons
 }
 
 std::atomic<int> g_max_ctas{0};
+std::atomic<bool> g_narrow{true};
 
 int current_device() {
     int device = 0;
@@ -771,9 +788,9 @@ struct ConvMaps {
     CUtensorMap a, b, out, res1, res2;
 };
 
-template <bool SPATIAL, int MODE, int SIGNED>
+template <bool SPATIAL, int MODE, int SIGNED, bool NARROW>
 cudaError_t launch_mode(const ConvMaps& m, const ConvTcArgs& args, size_t smem, int sms, cudaStream_t stream) {
-    auto kernel = conv_i16_tc_kernel<SPATIAL, MODE, SIGNED>;
+    auto kernel = conv_i16_tc_kernel<SPATIAL, MODE, SIGNED, NARROW>;
     // The attribute is per function and device and shared by every thread that
     // launches the kernel, so it is always the kernel's full allowance (a
     // per-launch value could be lowered by another thread between its set and
@@ -794,20 +811,24 @@ cudaError_t launch_mode(const ConvMaps& m, const ConvTcArgs& args, size_t smem, 
     return cudaGetLastError();
 }
 
-template <bool SPATIAL, int SIGNED>
+template <bool SPATIAL, int SIGNED, bool NARROW>
 cudaError_t launch_signed(const ConvMaps& m, const ConvTcArgs& args, size_t smem, int sms, cudaStream_t stream) {
     const Epilogue& e = args.epi;
-    if (e.shuffle2) return launch_mode<SPATIAL, kEpiShuffle2, SIGNED>(m, args, smem, sms, stream);
-    if (e.wsilu4) return launch_mode<SPATIAL, kEpiWsilu4, SIGNED>(m, args, smem, sms, stream);
-    if (e.lut) return launch_mode<SPATIAL, kEpiLut, SIGNED>(m, args, smem, sms, stream);
-    if (e.res1.base) return launch_mode<SPATIAL, kEpiRes, SIGNED>(m, args, smem, sms, stream);
-    return launch_mode<SPATIAL, kEpiPlain, SIGNED>(m, args, smem, sms, stream);
+    if (e.shuffle2) return launch_mode<SPATIAL, kEpiShuffle2, SIGNED, NARROW>(m, args, smem, sms, stream);
+    if (e.wsilu4) return launch_mode<SPATIAL, kEpiWsilu4, SIGNED, NARROW>(m, args, smem, sms, stream);
+    if (e.lut) return launch_mode<SPATIAL, kEpiLut, SIGNED, NARROW>(m, args, smem, sms, stream);
+    if (e.res1.base) return launch_mode<SPATIAL, kEpiRes, SIGNED, NARROW>(m, args, smem, sms, stream);
+    return launch_mode<SPATIAL, kEpiPlain, SIGNED, NARROW>(m, args, smem, sms, stream);
 }
 
 template <bool SPATIAL>
-cudaError_t launch(const ConvMaps& m, const ConvTcArgs& args, size_t smem, int sms, cudaStream_t stream) {
-    return args.signed_split ? launch_signed<SPATIAL, 1>(m, args, smem, sms, stream)
-                             : launch_signed<SPATIAL, 0>(m, args, smem, sms, stream);
+cudaError_t launch(const ConvMaps& m, const ConvTcArgs& args, bool narrow, size_t smem, int sms,
+                   cudaStream_t stream) {
+    if (narrow)
+        return args.signed_split ? launch_signed<SPATIAL, 1, true>(m, args, smem, sms, stream)
+                                 : launch_signed<SPATIAL, 0, true>(m, args, smem, sms, stream);
+    return args.signed_split ? launch_signed<SPATIAL, 1, false>(m, args, smem, sms, stream)
+                             : launch_signed<SPATIAL, 0, false>(m, args, smem, sms, stream);
 }
 
 // Tensor map of a split-NHWC view in tile order: flat {c, plane, pixels} (box
@@ -837,6 +858,24 @@ bool act_map(CUtensorMap* map, const Act& v, bool flat, int tw, int th, cuuint32
 
 void tc_set_max_ctas(int n) { g_max_ctas.store(n > 0 ? n : 0, std::memory_order_relaxed); }
 
+void tc_set_narrow(bool enable) { g_narrow.store(enable, std::memory_order_relaxed); }
+
+bool tc_narrow_ok(const int16_t* weight_host, int co, int ci, int kh, int kw, bool signed_split) {
+    const long long k = static_cast<long long>(ci) * kh * kw;
+    for (int o = 0; o < co; ++o) {
+        // |LL + 256 X| = |sum_k wl x + 256 wh xl| <= sum_k 32768 |wl| + 65280 |wh|
+        long long bound = 4096;
+        for (long long i = 0; i < k; ++i) {
+            const int32_t v = weight_host[o * k + i];
+            const int32_t lo = signed_split ? ((v + 128) & 255) - 128 : (v & 255);
+            const int32_t hi = (v - lo) >> 8;
+            bound += 32768ll * (lo < 0 ? -lo : lo) + 65280ll * (hi < 0 ? -hi : hi);
+        }
+        if (bound > INT32_MAX) return false;
+    }
+    return true;
+}
+
 bool tc_encode_map(CUtensorMap* map, void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
                    const cuuint32_t* box, std::string& err, CUtensorMapSwizzle swizzle) {
     return encode(map, base, rank, dims, strides, box, err, swizzle);
@@ -860,6 +899,10 @@ void tc_lut_window(const int16_t* table, int& start, int& n, int& hi) {
     hi = last_moved;
     const int end = last_moved < 32767 ? last_moved + 1 : 32767;   // inclusive
     n = end >= start && end - start + 1 <= 8192 ? end - start + 1 : 0;
+    for (int i = 0; i < n; ++i) {
+        const int d = table[start + i + 32768] - (start + i);
+        if (d < -32768 || d > 32767) n = 0;
+    }
 }
 
 bool tc_signed_split_ok(const int16_t* weight_host, size_t count) {
@@ -886,7 +929,7 @@ bool tc_describe(TcWeights& w, int co, int ci, int kh, int kw, bool signed_split
     w.planes = planes;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(w.kpad), static_cast<cuuint64_t>(w.co_tiles) * 2 * bn};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(w.kpad)};
-    const cuuint32_t box[2] = {kBK, static_cast<cuuint32_t>(2 * bn)};
+    const cuuint32_t box[2] = {kBK, static_cast<cuuint32_t>(bn)};
     return encode(&w.map, planes, 2, dims, strides, box, err);
 }
 
@@ -954,6 +997,10 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
         err = "fused residual adds take an int16 bias";
         return -1;
     }
+    if ((epi.lut || epi.wsilu4) && epi.bias && epi.bias32) {
+        err = "fused table steps take an int16 bias";
+        return -1;
+    }
     const int mode_id = res_mode ? 2 : 0;
     const size_t base_smem = 1024 + size_t(kStages) * kStageBytes + size_t(warp_stage_bytes(mode_id)) * kEpiWarps +
                              size_t(w.co_tiles) * kBN * (res_mode ? 2 : 4);
@@ -964,6 +1011,12 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     const long long k_total = static_cast<long long>(w.kh) * w.kw * w.ci;
     if (k_total > kTcMaxReduction) {
         err = "reduction longer than the tensor-core path's 32-bit recombination bound";
+        return -1;
+    }
+    if (k_total == kTcMaxReduction && epi.bias && epi.bias32) {
+        // |rna(S / 8192)| reaches 2^30 only here; with an int32 bias staged at
+        // up to 2^30 + 2^16 the 32-bit sum could wrap
+        err = "a reduction of 8192 terms takes an int16 bias on the tensor-core path";
         return -1;
     }
     const bool flat = stride == 1 && w.kh == 1 && w.kw == 1 && pad_h == 0 && pad_w == 0 && in.dense() && out.dense() &&
@@ -1032,8 +1085,9 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     }
     args.total_tiles = static_cast<int>(total);
     const int sms = sm_count(current_device());
-    const cudaError_t e =
-        flat ? launch<false>(maps, args, smem, sms, stream) : launch<true>(maps, args, smem, sms, stream);
+    const bool narrow = w.narrow && g_narrow.load(std::memory_order_relaxed);
+    const cudaError_t e = flat ? launch<false>(maps, args, narrow, smem, sms, stream)
+                               : launch<true>(maps, args, narrow, smem, sms, stream);
     if (e != cudaSuccess) {
         err = std::string("conv launch failed: ") + cudaGetErrorString(e);
         return -1;

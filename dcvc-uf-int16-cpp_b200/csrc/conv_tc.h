@@ -26,7 +26,10 @@ struct TcWeights {
     uint8_t* planes = nullptr;
     int co = 0, ci = 0, kh = 0, kw = 0, cpad = 0, kpad = 0, co_tiles = 0, bn = 128;
     bool signed_split = false;
-    CUtensorMap map{};  // TMA map over the [co_tiles * 2bn][kpad] byte matrix, 2bn-row box
+    // LL + 256 X + 4096 fits int32 for every input (tc_narrow_ok): the epilogue
+    // then recombines with one multiply-add less per output and no 5-bit split
+    bool narrow = false;
+    CUtensorMap map{};  // TMA map over the [co_tiles * 2bn][kpad] byte matrix, bn-row box (one byte block)
 };
 
 // Bytes needed for the prepared planes of a [co, ci, kh, kw] convolution.
@@ -47,7 +50,8 @@ bool tc_prepare(TcWeights& w, const int16_t* weight, int co, int ci, int kh, int
 // Shared-memory window of a 65536-entry lookup table (host data, index
 // v + 32768): lut[v] == 0 for every v < start + 1, lut[v] == v for every
 // v > hi, and entries [start, start + n) cover the rest (n == 0: no window;
-// kernels then read the global table).
+// kernels then read the global table).  Kernels stage the window as the
+// differences lut[v] - v, so n is 0 as well when one of them leaves int16.
 void tc_lut_window(const int16_t* table, int& start, int& n, int& hi);
 
 // True when every weight allows the signed split (host data).
@@ -61,6 +65,16 @@ bool tc_encode_map(CUtensorMap* map, void* base, int rank, const cuuint64_t* dim
 // Caps the persistent grid at n CTAs (0: one per SM).  A testing aid: with few
 // CTAs every CTA walks many tiles, which exercises both TMEM accumulator sets.
 void tc_set_max_ctas(int n);
+
+// True when, for every output channel o of these int16 [co, ci, kh, kw] weights
+// (host data) in the given byte split, sum_k 32768 |wl| + 65280 |wh| + 4096 fits
+// int32: then LL + 256 X + 4096 = sum_k wl x + 256 wh xl + 4096 fits int32 for
+// every int16 input, and TcWeights::narrow may be set.
+bool tc_narrow_ok(const int16_t* weight_host, int co, int ci, int kh, int kw, bool signed_split);
+
+// Process-wide switch for the narrow recombination (default on); off runs every
+// layer through the general one.  A testing aid: both give identical outputs.
+void tc_set_narrow(bool enable);
 
 // out = epilogue(conv(in, w)), zero padding (pad_h, pad_w), stride 1 or 2
 // (strided: plain epilogue only).  Both views must have 16-byte aligned pitch

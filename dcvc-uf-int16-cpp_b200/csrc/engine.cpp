@@ -146,6 +146,7 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
     };
     const HostTensor *zc = nullptr, *zl = nullptr, *yc = nullptr, *yl = nullptr;
     std::map<std::string, bool> signed_ok;  // every weight <= 32639: signed byte split allowed
+    std::map<std::string, bool> narrow_ok;  // narrow tensor-core recombination allowed (tc_narrow_ok)
     for (const auto& t : tensors) {
         names_.insert(t.name);
         size_t numel = 1;
@@ -158,8 +159,10 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
             L.kh = static_cast<int>(t.shape[2]);
             L.kw = static_cast<int>(t.shape[3]);
             L.weights16 = static_cast<int16_t*>(upload(t.data, numel * 2));
-            signed_ok[t.name.substr(0, t.name.size() - 7)] =
-                tc_signed_split_ok(static_cast<const int16_t*>(t.data), numel);
+            const bool sgn = tc_signed_split_ok(static_cast<const int16_t*>(t.data), numel);
+            signed_ok[t.name.substr(0, t.name.size() - 7)] = sgn;
+            narrow_ok[t.name.substr(0, t.name.size() - 7)] =
+                tc_narrow_ok(static_cast<const int16_t*>(t.data), L.co, L.ci, L.kh, L.kw, sgn);
         } else if (ends(t.name, ".bias")) {
             if (t.dtype != 0 || t.shape.size() != 1) throw std::invalid_argument("bias must be int16 1-D: " + t.name);
             convs_[t.name.substr(0, t.name.size() - 5)].bias = static_cast<int16_t*>(upload(t.data, numel * 2));
@@ -211,6 +214,7 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
         if (!tc_prepare(L.tc, L.weights16, L.co, L.ci, L.kh, L.kw, sgn, bn, static_cast<uint8_t*>(planes), nullptr,
                         err))
             throw std::runtime_error(err);
+        L.tc.narrow = narrow_ok[kv.first];
     }
     ck(cudaDeviceSynchronize(), "model upload");
 }

@@ -47,6 +47,13 @@ const char* ufb_last_error(void);
  * problems still run many tiles per CTA.  Process-wide; not for production. */
 int ufb_set_conv_max_ctas(int n);
 
+/* Testing aid (no reference counterpart): enable (1, the default) or disable
+ * (0) the narrow recombination of the tensor-core convolution epilogue, used
+ * for model layers whose weights keep LL + 256 X + 4096 within 32 bits for
+ * every input.  Both settings give identical outputs; the switch lets tests
+ * compare them.  Process-wide; not for production. */
+int ufb_set_conv_narrow(int enable);
+
 /* Synchronise `device` and return then clear its kernel status word:
  * 0 when no kernel reported a pipeline timeout since the last call, else the
  * first recorded code (1..4 = TMA producer / MMA / epilogue / drain wait). */

@@ -293,3 +293,75 @@ def test_signed_split_weight_extremes(ufb, ref, syn, extreme):
     mine, theirs = ufb.Model("htl", t), ref.model("htl", t)
     x = rng.integers(-6000, 6000, (1, 512, 6, 9)).astype(np.int16)
     assert np.array_equal(mine.run("feature_extractor", x), theirs.run("feature_extractor", x))
+
+
+def _narrow_ok(w):
+    """Host restatement of the engine's narrow-recombination bound: per output
+    channel, 4096 + sum_k 32768 |wl| + 65280 |wh| <= 2^31 - 1 (signed byte
+    split when every weight is <= 32639, else unsigned)."""
+    w = w.astype(np.int64).reshape(w.shape[0], -1)
+    lo = ((w + 128) & 255) - 128 if w.max() <= 32639 else (w & 255)
+    hi = (w - lo) >> 8
+    return bool((4096 + (32768 * np.abs(lo) + 65280 * np.abs(hi)).sum(1)).max() <= 2**31 - 1)
+
+
+@pytest.mark.parametrize("module,shapes", [
+    ("feature_extractor", [(1, 512, 8, 10)]),
+    ("recon_head.conv.3", [(1, 512, 8, 8)]),
+    ("y_spatial_prior", [(1, 512, 3, 5)]),
+    ("decoder", [(1, 256, 4, 4), (1, 512, 8, 8)]),
+])
+def test_narrow_recombination_matches_general(ufb, syn, models, module, shapes):
+    """Most HT-L layers (1x1 convolutions of up to 512 input channels) keep
+    LL + 256 X + 4096 within 32 bits and use the narrow recombination; with the
+    switch off every layer takes the general one.  Both must give the
+    reference's outputs."""
+    t = syn.prepared("htl", 2)
+    assert sum(_narrow_ok(v) for k, v in t.items() if k.startswith(module) and k.endswith(".weight")
+               and v.shape[1] > 1) > 0
+    mine, theirs = models["htl"]
+    rng = np.random.default_rng(17)
+    args = [rnd(rng, s, -9000, 9000) for s in shapes]
+    q = "q_decoder" if module == "decoder" else None
+    want = theirs.run(module, *(args + ([theirs.parameter(q, 20)] if q else [])))
+    got = mine.run(module, *args, q_name=q, qp=20)
+    ufb.set_conv_narrow(False)
+    try:
+        general = mine.run(module, *args, q_name=q, qp=20)
+    finally:
+        ufb.set_conv_narrow(True)
+    assert np.array_equal(got, want)
+    assert np.array_equal(general, want)
+
+
+@pytest.mark.parametrize("margin", ["inside", "outside"])
+def test_narrow_bound_edges(ufb, ref, syn, margin):
+    """Weights with |low byte| = 127 everywhere and a few high bytes put the
+    narrow bound within 2^24 of int32's limit ("inside": narrow path) or just
+    past it ("outside": general path); inputs of -32768 and 32767 then drive
+    LL + 256 X + 4096 to that limit.  The module must match the reference."""
+    t = dict(syn.prepared("htl", 2))
+    rng = np.random.default_rng(23)
+    sign_in = rng.choice(np.array([-1, 1]), 512)  # one sign pattern over the input channels
+    for name in ("feature_extractor.conv.0.dc.0.weight", "feature_extractor.conv.0.ffn.0.weight",
+                 "feature_extractor.conv.0.dc.3.weight"):
+        co, ci = t[name].shape[:2]
+        sign = np.broadcast_to(sign_in[:ci], (co, ci)).copy()
+        sign[1::2] *= -1  # odd output channels take the opposite pattern
+        w = sign * 127
+        # 4096 + 512 * 127 * 32768 leaves 16,773,119 for the high bytes: 256
+        # of them at |wh| = 1 fit (65280 each), 257 do not
+        n_hi = 256 if margin == "inside" else 300
+        w[:, :n_hi] += sign[:, :n_hi] * 256
+        w = w.astype(np.int16).reshape(t[name].shape)
+        assert _narrow_ok(w) == (margin == "inside")
+        t[name] = w
+    mine, theirs = ufb.Model("htl", t), ref.model("htl", t)
+    # pixels whose channels follow the sign pattern (32767 / -32768): every
+    # output channel of dc.0 sits at +-(the bound) before the rounding
+    x = np.where(sign_in[None, :, None, None] > 0, np.int16(32767), np.int16(-32768))
+    x = np.broadcast_to(x, (1, 512, 6, 9)).copy()
+    x[..., 3:6] = rng.choice(np.array([-32768, 32767, -32767, 0, 255, -256], np.int16), (1, 512, 6, 3))
+    x[..., 6:] = rng.integers(-32768, 32768, (1, 512, 6, 3))
+    x[:, :, 3:] = -x[:, :, 3:]  # and the opposite signs (-(-32768) wraps to -32768)
+    assert np.array_equal(mine.run("feature_extractor", x), theirs.run("feature_extractor", x))
