@@ -65,27 +65,6 @@ __device__ __forceinline__ void join_bytes(uint32_t lo, uint32_t hi, uint32_t& p
     p1 = __byte_perm(lo, hi, 0x7362);
 }
 
-// The 65536-entry lookup table, optionally through a shared-memory window.
-// A table such as WSiLU is zero below some v_lo and the identity above some
-// v_hi; the window holds entries [start, start + n) with start = v_lo - 1
-// (a zero entry, which also serves every v below) and every v > hi maps to
-// itself.  win == null: read the global table.
-struct LutView {
-    const int16_t* global;
-    const int16_t* win;
-    int start, n, hi;
-
-    __device__ __forceinline__ int32_t operator()(int32_t v) const {
-        if (win) {
-            int32_t i;  // max(min(v - start, n - 1), 0) in one instruction
-            asm("min.relu.s32 %0, %1, %2;" : "=r"(i) : "r"(v - start), "r"(n - 1));
-            const int32_t r = win[i];
-            return v > hi ? v : r;
-        }
-        return __ldg(global + v + 32768);
-    }
-};
-
 // lut[sat16(v + start)] - start through a window of differences
 // d[i] = lut[start + i] - (start + i), i in [0, last], of a table that is
 // lut[start] below start and the identity above start + last (or whose window

@@ -280,7 +280,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
         tmem_relinquish();
     }
     // window start of the fused table step: the staged bias carries -lut_start
-    const int lut_start = (MODE == kEpiLut || MODE == kEpiWsilu4) && args.epi.lut_n > 0 ? args.epi.lut_start : 0;
+    const int lut_start = MODE == kEpiLut || MODE == kEpiWsilu4 ? args.epi.lut_start : 0;
     // the whole bias vector, zero padded to the tile grid, once per CTA
     for (int i = threadIdx.x; i < args.n_tiles * kBN; i += kThreads) {
         long long b = 0;
@@ -291,12 +291,10 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
     }
     // table window as differences lut[v] - v (the host checked that they fit
     // int16); lut_window() turns them back into lut[sat16(v)]
-    const LutView lut{args.epi.lut, nullptr, 0, 0, 0};  // whole table (no window)
-    const int16_t* lut_d = nullptr;
-    if ((MODE == kEpiLut || MODE == kEpiWsilu4) && args.epi.lut_n > 0) {
+    const int16_t* lut_d = lut_s;
+    if (MODE == kEpiLut || MODE == kEpiWsilu4) {
         for (int i = threadIdx.x; i < args.epi.lut_n; i += kThreads)
             lut_s[i] = static_cast<int16_t>(args.epi.lut[lut_start + 32768 + i] - (lut_start + i));
-        lut_d = lut_s;
     }
     const int lut_last = args.epi.lut_n - 1, lut_cap = 32767 - lut_start;
     tc_fence_before();
@@ -511,7 +509,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         }
                         r[t] = T - static_cast<int32_t>(tie & (T <= 0)) + bb[t];
                     }
-                    if ((MODE == kEpiLut || MODE == kEpiWsilu4) && lut_d) {
+                    if (MODE == kEpiLut || MODE == kEpiWsilu4) {
                         // table window: r is conv - window start (the staged bias
                         // carries the shift)
                         int32_t v[4];
@@ -526,16 +524,6 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     } else {
                         p[8 * h + 2 * q] = pack2_sat(r[0], r[1]);
                         p[8 * h + 2 * q + 1] = pack2_sat(r[2], r[3]);
-                        if (MODE == kEpiLut) {
-                            // whole table from global memory
-                            p[8 * h + 2 * q] = pack2(lut(lo16(p[8 * h + 2 * q])), lut(hi16(p[8 * h + 2 * q])));
-                            p[8 * h + 2 * q + 1] =
-                                pack2(lut(lo16(p[8 * h + 2 * q + 1])), lut(hi16(p[8 * h + 2 * q + 1])));
-                        }
-                        if (MODE == kEpiWsilu4) {
-                            const uint32_t a0 = p[8 * h + 2 * q], a1 = p[8 * h + 2 * q + 1];
-                            o4[4 * h + q] = lut(lo16(a0)) + lut(hi16(a0)) + lut(lo16(a1)) + lut(hi16(a1));
-                        }
                     }
                 }
             }
@@ -881,6 +869,17 @@ bool tc_encode_map(CUtensorMap* map, void* base, int rank, const cuuint64_t* dim
     return encode(map, base, rank, dims, strides, box, err, swizzle);
 }
 
+// Dynamic shared memory of a launch without its table window: alignment slack,
+// the operand ring, the epilogue warps' stages and the staged bias vector.
+size_t conv_smem_bytes(const TcWeights& w, bool res_mode) {
+    return 1024 + size_t(kStages) * kStageBytes + size_t(warp_stage_bytes(res_mode ? 2 : 0)) * kEpiWarps +
+           size_t(w.co_tiles) * kBN * (res_mode ? 2 : 4);
+}
+
+bool tc_table_window_fits(const TcWeights& w, int lut_n, bool res_mode) {
+    return lut_n > 0 && conv_smem_bytes(w, res_mode) + (static_cast<size_t>(lut_n) * 2 + 15) / 16 * 16 <= kSmemBudget;
+}
+
 size_t tc_weight_bytes(int co, int ci, int kh, int kw, int bn) {
     const int cpad = (ci + kBK - 1) / kBK * kBK;
     const int co_tiles = (co + bn - 1) / bn;
@@ -1001,9 +1000,7 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
         err = "fused table steps take an int16 bias";
         return -1;
     }
-    const int mode_id = res_mode ? 2 : 0;
-    const size_t base_smem = 1024 + size_t(kStages) * kStageBytes + size_t(warp_stage_bytes(mode_id)) * kEpiWarps +
-                             size_t(w.co_tiles) * kBN * (res_mode ? 2 : 4);
+    const size_t base_smem = conv_smem_bytes(w, res_mode);
     if (base_smem > kSmemBudget) {
         err = "too many output channels for the staged bias";
         return -1;
@@ -1025,10 +1022,13 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     ConvTcArgs args{};
     args.out = out;
     args.epi = epi;
-    // the LUT window rides in shared memory after the bias when it fits
-    const size_t lut_bytes = (static_cast<size_t>(epi.lut_n) * 2 + 15) / 16 * 16;
-    if (!epi.lut || epi.lut_n <= 0 || base_smem + lut_bytes > kSmemBudget) args.epi.lut_n = 0;
-    const size_t smem = base_smem + (args.epi.lut_n > 0 ? lut_bytes : 0);
+    // the table window rides in shared memory after the bias
+    const size_t lut_bytes = (epi.lut || epi.wsilu4) ? (static_cast<size_t>(epi.lut_n) * 2 + 15) / 16 * 16 : 0;
+    if ((epi.lut || epi.wsilu4) && !tc_table_window_fits(w, epi.lut_n, res_mode)) {
+        err = "fused table steps need a table window that fits shared memory";
+        return -1;
+    }
+    const size_t smem = base_smem + lut_bytes;
     args.co = w.co;
     args.ci = w.ci;
     args.taps_h = w.kh;

@@ -54,6 +54,11 @@ bool tc_prepare(TcWeights& w, const int16_t* weight, int co, int ci, int kh, int
 // differences lut[v] - v, so n is 0 as well when one of them leaves int16.
 void tc_lut_window(const int16_t* table, int& start, int& n, int& hi);
 
+// True when a fused table step (LUT or wsilu4 epilogue) of a layer with these
+// weights can stage a table window of lut_n entries in shared memory (res_mode:
+// the residual epilogue's larger stages; table steps use the others).
+bool tc_table_window_fits(const TcWeights& w, int lut_n, bool res_mode = false);
+
 // True when every weight allows the signed split (host data).
 bool tc_signed_split_ok(const int16_t* weight_host, size_t count);
 

@@ -299,6 +299,15 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
         count();
         return out;
     }
+    if ((f.lut || f.wsilu4) && (!L->tc.planes || !tc_table_window_fits(L->tc, m_.wsilu_n()))) {
+        // a table without a shared-memory window (not WSiLU-shaped): the plain
+        // convolution, then the table step as its own pass
+        Fuse plain;
+        const Tensor t = conv(name, in, plain);
+        ck(lut_split(t.a, m_.wsilu(), f.wsilu4 ? 4 : 1, out.a, s_), "table step");
+        count();
+        return out;
+    }
     if (L->tc.planes && (stride == 1 || !(f.lut || f.wsilu4 || f.shuffle2 || f.res1 || f.mulq))) {
         Epilogue e{};
         e.bias = L->bias;

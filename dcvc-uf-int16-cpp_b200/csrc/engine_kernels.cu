@@ -117,6 +117,26 @@ __global__ void mul_channels_kernel(Act in, const int16_t* __restrict__ q, Act o
     }
 }
 
+// out = lut[in] (groups == 1) or out[c] = sat(sum_{k<4} lut[in[4c + k]])
+// (groups == 4): int16::lookup / int16::wsilu4 (src/int16_ops.cpp:107-130) on
+// split views, for tables the convolution epilogue cannot window.
+__global__ void lut_split_kernel(Act in, const int16_t* __restrict__ lut, int groups, Act out) {
+    GRID_LOOP(i, out.pixels() * out.c) {
+        const int c = static_cast<int>(i % out.c);
+        int b, y, x;
+        px_of(out, i / out.c, b, y, x);
+        const long long p = in.pixel(b, y, x), op = out.pixel(b, y, x);
+        int32_t v = 0;
+        for (int k = 0; k < groups; ++k) {
+            const int ic = c * groups + k;
+            v += lut[join16(in.lo(p)[ic], in.hi(p)[ic]) + 32768];
+        }
+        const int16_t r = sat16(v);
+        out.lo(op)[c] = static_cast<uint8_t>(r & 0xff);
+        out.hi(op)[c] = static_cast<uint8_t>((r >> 8) & 0xff);
+    }
+}
+
 // IntegerModel::prior tail (src/integer_model.cpp:209-210, 292):
 // out = multiply(restored, max(q_raw, 256)) elementwise.
 __global__ void yhat_kernel(Act restored, Act qraw, Act out) {
@@ -495,6 +515,11 @@ cudaError_t mul_unshuffle2(const Act& in, const int16_t* q, const Act& out, cuda
 
 cudaError_t mul_channels(const Act& in, const int16_t* q, const Act& out, cudaStream_t s) {
     mul_channels_kernel<<<grid_for(in.pixels() * in.c), kBlock, 0, s>>>(in, q, out);
+    return cudaGetLastError();
+}
+
+cudaError_t lut_split(const Act& in, const int16_t* lut, int groups, const Act& out, cudaStream_t s) {
+    lut_split_kernel<<<grid_for(out.pixels() * out.c), kBlock, 0, s>>>(in, lut, groups, out);
     return cudaGetLastError();
 }
 

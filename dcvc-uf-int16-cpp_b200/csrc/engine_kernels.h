@@ -15,6 +15,8 @@ cudaError_t split_to_symbols(const Act& in, int8_t* sym, cudaStream_t s);
 cudaError_t mul_unshuffle2(const Act& in, const int16_t* q, const Act& out, cudaStream_t s);
 cudaError_t mul_channels(const Act& in, const int16_t* q, const Act& out, cudaStream_t s);
 cudaError_t yhat(const Act& restored, const Act& qraw, const Act& out, cudaStream_t s);
+// out = lut[in] (groups 1) or the wsilu4 reduction of groups of 4 channels (groups 4)
+cudaError_t lut_split(const Act& in, const int16_t* lut, int groups, const Act& out, cudaStream_t s);
 
 int prior_blocks_per_stream(int channels, int h, int w);
 // count + per-stream scan: block_counts becomes per-block offsets, totals[n]
