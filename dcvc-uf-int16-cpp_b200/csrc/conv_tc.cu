@@ -459,36 +459,45 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
             // for this layer's weights), so S + 4096 = 65536 HH + P.  Otherwise
             // D = (X >> 5) + (U >> 13) with U = LL + 256 (X & 31) + 4096 and a
             // tie bit U % 8192 == 0, so S + 4096 = 8192 (8 HH + D) + (U & 8191).
+            // Both slots come in with one wait, so the MMA warp gets them back
+            // after a single TMEM round trip.
+            static_assert(kCols == 64, "drain loads 64 columns per slot");
             int32_t D[kCols];
             uint32_t ties[kLd];
-#pragma unroll
-            for (int i = 0; i < kLd; ++i) {
-                uint32_t ll[32], xx[32];
-                tmem_ld32(a_ll + 32 * i, ll);
-                tmem_ld32(a_x + 32 * i, xx);
+            {
+                uint32_t ll[kCols], xx[kCols];
+                tmem_ld64(a_ll, ll);
+                tmem_ld64(a_x, xx);
                 tmem_wait_ld();
-                if (i == kLd - 1) release_tmem(&tmem_empty, lane);
-                ties[i] = 0;
+                release_tmem(&tmem_empty, lane);
 #pragma unroll
-                for (int t = 0; t < 32; ++t) {
-                    const int32_t x = static_cast<int32_t>(xx[t]);
-                    if (NARROW) {
-                        D[32 * i + t] = x * c256 + (static_cast<int32_t>(ll[t]) + 4096);
-                    } else {
-                        const int32_t U = (x & 31) * c256 + (static_cast<int32_t>(ll[t]) + 4096);
-                        D[32 * i + t] = (x >> 5) + (U >> 13);
-                        ties[i] |= static_cast<uint32_t>((U & 8191) == 0) << t;
+                for (int i = 0; i < kLd; ++i) {
+                    ties[i] = 0;
+#pragma unroll
+                    for (int t = 0; t < 32; ++t) {
+                        const int32_t x = static_cast<int32_t>(xx[32 * i + t]);
+                        const int32_t l = static_cast<int32_t>(ll[32 * i + t]);
+                        if (NARROW) {
+                            D[32 * i + t] = x * c256 + (l + 4096);
+                        } else {
+                            const int32_t U = (x & 31) * c256 + (l + 4096);
+                            D[32 * i + t] = (x >> 5) + (U >> 13);
+                            ties[i] |= static_cast<uint32_t>((U & 8191) == 0) << t;
+                        }
                     }
                 }
             }
-            // HH 16 columns at a time: T = floor((S + 4096) / 8192) rounds half up;
-            // an exact tie with S < 0 (T <= 0) takes T - 1 (half away from zero).
-            // Then the bias and the fused table step.
+            // HH 16 columns at a time, the next 16 in flight while these are
+            // finished: T = floor((S + 4096) / 8192) rounds half up; an exact tie
+            // with S < 0 (T <= 0) takes T - 1 (half away from zero).  Then the
+            // bias and the fused table step.
+            uint32_t hh_buf[2][16];
+            tmem_ld16(a_hh, hh_buf[0]);
+            tmem_wait_ld_regs(hh_buf[0]);
 #pragma unroll
             for (int h = 0; h < kCols / 16; ++h) {
-                uint32_t hh[16];
-                tmem_ld16(a_hh + 16 * h, hh);
-                tmem_wait_ld();
+                if (h + 1 < kCols / 16) tmem_ld16(a_hh + 16 * (h + 1), hh_buf[(h + 1) & 1]);
+                const uint32_t(&hh)[16] = hh_buf[h & 1];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     const int4 b = load_bias4(bias_s + cbase + 16 * h + 4 * q);
@@ -526,6 +535,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         p[8 * h + 2 * q + 1] = pack2_sat(r[2], r[3]);
                     }
                 }
+                if (h + 1 < kCols / 16) tmem_wait_ld_regs(hh_buf[(h + 1) & 1]);
             }
             const int n_valid = args.co - cbase < 0 ? 0 : (args.co - cbase < kCols ? args.co - cbase : kCols);
             bool valid;
