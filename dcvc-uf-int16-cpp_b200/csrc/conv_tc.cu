@@ -858,6 +858,8 @@ void tc_set_max_ctas(int n) { g_max_ctas.store(n > 0 ? n : 0, std::memory_order_
 
 void tc_set_narrow(bool enable) { g_narrow.store(enable, std::memory_order_relaxed); }
 
+bool tc_narrow_enabled() { return g_narrow.load(std::memory_order_relaxed); }
+
 bool tc_narrow_ok(const int16_t* weight_host, int co, int ci, int kh, int kw, bool signed_split) {
     const long long k = static_cast<long long>(ci) * kh * kw;
     for (int o = 0; o < co; ++o) {

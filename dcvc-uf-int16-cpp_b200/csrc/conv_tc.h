@@ -80,6 +80,7 @@ bool tc_narrow_ok(const int16_t* weight_host, int co, int ci, int kh, int kw, bo
 // Process-wide switch for the narrow recombination (default on); off runs every
 // layer through the general one.  A testing aid: both give identical outputs.
 void tc_set_narrow(bool enable);
+bool tc_narrow_enabled();
 
 // out = epilogue(conv(in, w)), zero padding (pad_h, pad_w), stride 1 or 2
 // (strided: plain epilogue only).  Both views must have 16-byte aligned pitch

@@ -24,6 +24,8 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <climits>
+#include <cstdlib>
 #include <string>
 
 namespace ufb {
@@ -147,6 +149,75 @@ __device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], 
     }
 }
 
+// Narrow layers (every channel: 32768 sum|w| + 4096 + 8192 |bias| < 2^31, see
+// dw_narrow_ok): the whole sum S + 4096 + 8192 bias fits one int32, so each tap
+// is one multiply-add of full int16 values and the store needs one compare.
+struct DwAccN {
+    int32_t s[kCols][4];
+};
+
+// Window row r as int16 values sign-extended to 32 bits: x[p][c] for window
+// columns 2t + p and channels 4q + c (one byte permute per value).
+struct DwRowN {
+    int32_t x[kCols + 2][4];
+};
+
+// prmt.b32 in its default mode: a selector nibble with bit 3 set fills the
+// byte with the sign of the selected source byte.
+__device__ __forceinline__ int32_t prmt_sx(uint32_t a, uint32_t b, uint32_t sel) {
+    int32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ void dw_row_n(const uint8_t* buf, int r, int t, int q, DwRowN& row) {
+#pragma unroll
+    for (int p = 0; p < kCols + 2; ++p) {
+        const uint32_t off = (static_cast<uint32_t>(r) * kInW + kCols * t + p) * kLine + 4 * q;
+        const uint32_t lw = *reinterpret_cast<const uint32_t*>(buf + off);
+        const uint32_t hw = *reinterpret_cast<const uint32_t*>(buf + kPlane + off);
+        // bytes [lo c, hi c, sign(hi c), sign(hi c)]: selector nibbles 8-15 replicate a byte's sign
+        row.x[p][0] = prmt_sx(lw, hw, 0xCC40);
+        row.x[p][1] = prmt_sx(lw, hw, 0xDD51);
+        row.x[p][2] = prmt_sx(lw, hw, 0xEE62);
+        row.x[p][3] = prmt_sx(lw, hw, 0xFF73);
+    }
+}
+
+// Adds one input row through weight row w[kx][c]; FRESH starts the sums from
+// 4096 + 8192 bias (held in s0).
+template <bool FRESH>
+__device__ __forceinline__ void dw_add_n(DwAccN& a, const DwRowN& row, const int32_t (&w)[3][4],
+                                         const int32_t (&s0)[4]) {
+#pragma unroll
+    for (int j = 0; j < kCols; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            int32_t v = FRESH ? s0[c] : a.s[j][c];
+            v += row.x[j][c] * w[0][c];
+            v += row.x[j + 1][c] * w[1][c];
+            v += row.x[j + 2][c] * w[2][c];
+            a.s[j][c] = v;
+        }
+}
+
+// sat(rna(S / 8192) + bias) from s = S + 4096 + 8192 bias: rna(S / 8192) =
+// floor((S + 4096 - [S < 0]) / 8192), and S < 0 exactly when s < s0.
+__device__ __forceinline__ void dw_store_n(const DwAccN& a, const int32_t (&s0)[4], const Act& out, int img, int oy,
+                                           int ox, int c0) {
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) {
+        if (ox + j >= out.w) break;
+        int32_t r[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) r[c] = (a.s[j][c] - static_cast<int32_t>(a.s[j][c] < s0[c])) >> 13;
+        const uint32_t p0 = pack2_sat(r[0], r[1]), p1 = pack2_sat(r[2], r[3]);
+        const long long px = out.pixel(img, oy, ox + j);
+        *reinterpret_cast<uint32_t*>(out.lo(px) + c0) = __byte_perm(p0, p1, 0x6420);
+        *reinterpret_cast<uint32_t*>(out.hi(px) + c0) = __byte_perm(p0, p1, 0x7531);
+    }
+}
+
 // Window row r, columns 2t .. 2t + 3, channels 4q .. 4q + 3 of both planes.
 __device__ __forceinline__ void dw_row(const uint8_t* buf, int r, int t, int q, DwRow& lo, DwRow& hi) {
     uint32_t lw[kCols + 2], hw[kCols + 2];
@@ -160,6 +231,7 @@ __device__ __forceinline__ void dw_row(const uint8_t* buf, int r, int t, int q, 
     dw_prep(hw, hi);
 }
 
+template <bool NARROW>
 __global__ void __launch_bounds__(kThreads, 2)
 dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t* __restrict__ weight,
                      const int16_t* __restrict__ bias, int channels, int tiles_x, int tiles_y, int images,
@@ -192,7 +264,8 @@ dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t
     __syncthreads();
     if (threadIdx.x == 0 && blockIdx.x < total_tiles) issue(blockIdx.x, 0);
 
-    uint32_t wp[3][4], ws[3][4];
+    uint32_t wp[3][4], ws[3][4];  // general: taps (0, 1) packed, tap 2
+    int32_t wn[3][3][4];           // narrow: [ky][kx][channel]
     int32_t bv[4];
     int loaded_cb = -1;
     int i = 0;
@@ -215,11 +288,16 @@ dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t
                 const bool ok = c0 + c < channels;
 #pragma unroll
                 for (int ky = 0; ky < 3; ++ky) {
-                    const uint32_t w0 = ok ? static_cast<uint16_t>(weight[(c0 + c) * 9 + 3 * ky]) : 0;
-                    const uint32_t w1 = ok ? static_cast<uint16_t>(weight[(c0 + c) * 9 + 3 * ky + 1]) : 0;
-                    const uint32_t w2 = ok ? static_cast<uint16_t>(weight[(c0 + c) * 9 + 3 * ky + 2]) : 0;
-                    wp[ky][c] = w0 | (w1 << 16);
-                    ws[ky][c] = w2;
+                    if (NARROW) {
+#pragma unroll
+                        for (int kx = 0; kx < 3; ++kx) wn[ky][kx][c] = ok ? weight[(c0 + c) * 9 + 3 * ky + kx] : 0;
+                    } else {
+                        const uint32_t w0 = ok ? static_cast<uint16_t>(weight[(c0 + c) * 9 + 3 * ky]) : 0;
+                        const uint32_t w1 = ok ? static_cast<uint16_t>(weight[(c0 + c) * 9 + 3 * ky + 1]) : 0;
+                        const uint32_t w2 = ok ? static_cast<uint16_t>(weight[(c0 + c) * 9 + 3 * ky + 2]) : 0;
+                        wp[ky][c] = w0 | (w1 << 16);
+                        ws[ky][c] = w2;
+                    }
                 }
                 bv[c] = ok && bias ? bias[c0 + c] : 0;
             }
@@ -234,7 +312,30 @@ dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t
         const uint8_t* buf = smem + b * kBuffer;
         const int oy0 = ty * kTileH, ox = tx * kTileW + kCols * t;
         const bool active = c0 < channels && ox < out.w;
-        if (active) {
+        if (active && NARROW) {
+            // the general path's row schedule with whole-value sums
+            const int32_t s0[4] = {4096 + 8192 * bv[0], 4096 + 8192 * bv[1], 4096 + 8192 * bv[2],
+                                   4096 + 8192 * bv[3]};
+            DwAccN a0, a1, a2;
+            DwRowN row;
+            auto step = [&](DwAccN& next, DwAccN& mid, DwAccN& done, int wr) {
+                dw_row_n(buf, wr, t, q, row);
+                dw_add_n<true>(next, row, wn[0], s0);
+                if (wr >= 1) dw_add_n<false>(mid, row, wn[1], s0);
+                if (wr >= 2) {
+                    dw_add_n<false>(done, row, wn[2], s0);
+                    if (oy0 + wr - 2 < out.h) dw_store_n(done, s0, out, img, oy0 + wr - 2, ox, c0);
+                }
+            };
+#pragma unroll 1
+            for (int wr = 0; wr < kInH; wr += 3) {
+                step(a0, a1, a2, wr);
+                if (wr + 1 >= kInH) break;
+                step(a2, a0, a1, wr + 1);
+                if (wr + 2 >= kInH) break;
+                step(a1, a2, a0, wr + 2);
+            }
+        } else if (active) {
             // output rows r - 2, r - 1, r take window row r through weight rows
             // 2, 1, 0; row r starts there (the rows -1 and -2 of the first two
             // steps are never stored)
@@ -265,8 +366,17 @@ dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t
 
 }  // namespace
 
+bool dw_narrow_ok(const int16_t* weight_host, const int16_t* bias_host, int channels) {
+    for (int c = 0; c < channels; ++c) {
+        long long bound = 4096 + 8192ll * (bias_host ? std::abs(static_cast<int>(bias_host[c])) : 0);
+        for (int k = 0; k < 9; ++k) bound += 32768ll * std::abs(static_cast<int>(weight_host[c * 9 + k]));
+        if (bound > INT32_MAX) return false;
+    }
+    return true;
+}
+
 cudaError_t dwconv3x3(const Act& in, const Act& out, const int16_t* weight, const int16_t* bias, int* status,
-                      cudaStream_t s) {
+                      cudaStream_t s, bool narrow) {
     if (in.c % 4 || in.c != out.c || in.h != out.h || in.w != out.w || in.n != out.n || in.pitch % 16 ||
         out.pitch % 16 || reinterpret_cast<uintptr_t>(in.base) % 16 || reinterpret_cast<uintptr_t>(out.base) % 16 ||
         !status)
@@ -287,15 +397,17 @@ cudaError_t dwconv3x3(const Act& in, const Act& out, const int16_t* weight, cons
     const int tiles_x = (in.w + kTileW - 1) / kTileW, tiles_y = (in.h + kTileH - 1) / kTileH;
     const long long total = static_cast<long long>(ch_blocks) * tiles_x * tiles_y * in.n;
     if (total > INT32_MAX) return cudaErrorInvalidValue;
+    narrow = narrow && tc_narrow_enabled();
+    auto kernel = narrow ? dwconv3x3_kernel<true> : dwconv3x3_kernel<false>;
     // per device; always the same value, so concurrent callers cannot disagree
     const cudaError_t attr =
-        cudaFuncSetAttribute(dwconv3x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem));
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem));
     if (attr != cudaSuccess) return attr;
     int device = 0, sms = 148;
     if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     const long long grid = total < 2ll * sms ? total : 2ll * sms;
-    dwconv3x3_kernel<<<static_cast<unsigned>(grid), kThreads, kSmem, s>>>(
-        map, out, weight, bias, in.c, tiles_x, tiles_y, in.n, static_cast<int>(total), status);
+    kernel<<<static_cast<unsigned>(grid), kThreads, kSmem, s>>>(map, out, weight, bias, in.c, tiles_x, tiles_y, in.n,
+                                                                 static_cast<int>(total), status);
     return cudaGetLastError();
 }
 

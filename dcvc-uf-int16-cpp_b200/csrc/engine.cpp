@@ -147,6 +147,7 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
     const HostTensor *zc = nullptr, *zl = nullptr, *yc = nullptr, *yl = nullptr;
     std::map<std::string, bool> signed_ok;  // every weight <= 32639: signed byte split allowed
     std::map<std::string, bool> narrow_ok;  // narrow tensor-core recombination allowed (tc_narrow_ok)
+    std::map<std::string, const int16_t*> host_w, host_b;  // host data of each layer's weight and bias
     for (const auto& t : tensors) {
         names_.insert(t.name);
         size_t numel = 1;
@@ -159,6 +160,7 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
             L.kh = static_cast<int>(t.shape[2]);
             L.kw = static_cast<int>(t.shape[3]);
             L.weights16 = static_cast<int16_t*>(upload(t.data, numel * 2));
+            host_w[t.name.substr(0, t.name.size() - 7)] = static_cast<const int16_t*>(t.data);
             const bool sgn = tc_signed_split_ok(static_cast<const int16_t*>(t.data), numel);
             signed_ok[t.name.substr(0, t.name.size() - 7)] = sgn;
             narrow_ok[t.name.substr(0, t.name.size() - 7)] =
@@ -166,6 +168,7 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
         } else if (ends(t.name, ".bias")) {
             if (t.dtype != 0 || t.shape.size() != 1) throw std::invalid_argument("bias must be int16 1-D: " + t.name);
             convs_[t.name.substr(0, t.name.size() - 5)].bias = static_cast<int16_t*>(upload(t.data, numel * 2));
+            host_b[t.name.substr(0, t.name.size() - 5)] = static_cast<const int16_t*>(t.data);
         } else if (begins(t.name, "q_")) {
             if (t.dtype != 0 || t.shape.size() != 2) throw std::invalid_argument("QP table must be int16 2-D: " + t.name);
             ParamTable& p = params_[t.name];
@@ -204,6 +207,10 @@ Model::Model(int device, const std::string& variant, const std::vector<HostTenso
         ConvLayer& L = kv.second;
         if (!L.weights16) throw std::runtime_error("Missing prepared UF tensor: " + kv.first + ".weight");
         L.depthwise = L.ci == 1 && L.co > 1;
+        if (L.depthwise && L.kh == 3 && L.kw == 3) {
+            auto b = host_b.find(kv.first);
+            L.dw_narrow = dw_narrow_ok(host_w[kv.first], b == host_b.end() ? nullptr : b->second, L.co);
+        }
         if (L.depthwise || static_cast<long long>(L.ci) * L.kh * L.kw > kTcMaxReduction) continue;
         const bool sgn = signed_ok[kv.first];
         const int bn = tc_choose_bn(L.ci, L.kh, L.kw, sgn);
@@ -285,7 +292,7 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
             ev0 = stats_->take_event();
             ck(cudaEventRecord(ev0, s_), "event");
         }
-        ck(dwconv3x3(in.a, out.a, L->weights16, L->bias, status_, s_), "depthwise conv");
+        ck(dwconv3x3(in.a, out.a, L->weights16, L->bias, status_, s_, L->dw_narrow), "depthwise conv");
         if (ev0) {
             cudaEvent_t ev1 = stats_->take_event();
             ck(cudaEventRecord(ev1, s_), "event");

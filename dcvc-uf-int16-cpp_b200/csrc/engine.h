@@ -64,6 +64,7 @@ struct Tensor {
 struct ConvLayer {
     int co = 0, ci = 0, kh = 0, kw = 0;
     bool depthwise = false;
+    bool dw_narrow = false;       // depthwise sums fit one int32 (dw_narrow_ok)
     TcWeights tc;                 // groups == 1 layers
     int16_t* weights16 = nullptr; // original int16 weights (depthwise, strided, direct paths)
     int16_t* bias = nullptr;      // int16 [co] or null

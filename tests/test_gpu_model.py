@@ -365,3 +365,32 @@ def test_narrow_bound_edges(ufb, ref, syn, margin):
     x[..., 6:] = rng.integers(-32768, 32768, (1, 512, 6, 3))
     x[:, :, 3:] = -x[:, :, 3:]  # and the opposite signs (-(-32768) wraps to -32768)
     assert np.array_equal(mine.run("feature_extractor", x), theirs.run("feature_extractor", x))
+
+
+@pytest.mark.parametrize("margin", ["inside", "outside"])
+def test_depthwise_narrow_bound_edges(ufb, ref, syn, margin):
+    """The depthwise dc.2 sums run in one int32 when, per channel,
+    32768 sum|w| + 4096 + 8192 |bias| fits ("inside": sum|w| = 57343 with
+    |bias| at its maximum) and in split byte sums otherwise ("outside").  An
+    identity table and an identity dc.0 hand the input to dc.2 unchanged, so
+    inputs at 32767 / -32768 following the weight signs drive the sum to the
+    bound; a wrapped sum would flip the sign of dc.3's result."""
+    t = dict(syn.prepared("htl", 2))
+    rng = np.random.default_rng(29)
+    t["tables.wsilu"] = np.arange(-32768, 32768).astype(np.int16)
+    pre = "feature_extractor.conv.0."
+    t[pre + "dc.0.weight"] = (8192 * np.eye(512)).astype(np.int16).reshape(512, 512, 1, 1)
+    t[pre + "dc.0.bias"] = np.zeros(512, np.int16)
+    sign = rng.choice(np.array([-1, 1]), 512)
+    taps = np.array([6371] * 8 + [6375 if margin == "inside" else 6432])
+    t[pre + "dc.2.weight"] = (sign[:, None] * taps[None, :]).astype(np.int16).reshape(512, 1, 3, 3)
+    t[pre + "dc.2.bias"] = np.where(np.arange(512) % 2, 32767, -32768).astype(np.int16)
+    w = t[pre + "dc.2.weight"].astype(np.int64).reshape(512, 9)
+    bound = 4096 + 8192 * np.abs(t[pre + "dc.2.bias"].astype(np.int64)) + 32768 * np.abs(w).sum(1)
+    assert (bound.max() <= 2**31 - 1) == (margin == "inside")
+    mine, theirs = ufb.Model("htl", t), ref.model("htl", t)
+    x = np.where(sign[None, :, None, None] > 0, np.int16(32767), np.int16(-32768))
+    x = np.broadcast_to(x, (1, 512, 8, 9)).copy()
+    x[:, :, 4:6] = -x[:, :, 4:6]
+    x[:, :, 6:] = rng.integers(-32768, 32768, (1, 512, 2, 9))
+    assert np.array_equal(mine.run("feature_extractor", x), theirs.run("feature_extractor", x))
