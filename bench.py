@@ -379,11 +379,11 @@ def bench_decode_ours(args, rank, world, local):
         "roofline": {"bound": "tensor", "kernel": "conv_i16_tc_kernel (all tensor-core convolution launches)",
                      "achieved": achieved, "peak": peak, "unit": "TOPS(int8)",
                      "frac": achieved / peak if achieved else None,
-                     "traffic": load_traffic("decode_conv_per_launch"),
-                     "traffic_source": "ncu capture of a --seqs 8 decode (profiles/conv_i16_tc_decode_full.md), "
-                                       "not this run",
-                     "traffic_launch": "DRAM read + write of one 512->512 residual-epilogue launch over 32640 "
-                                       "pixels (profiles/conv_i16_tc_decode_full.md); algorithmic 100.3 MB",
+                     "traffic": load_traffic("htl_conv_res512_per_launch"),
+                     "traffic_source": "from profile: ncu capture of an HT-L module run "
+                                       "(profiles/conv_i16_tc_htl_blocks.md), not this run",
+                     "traffic_launch": "DRAM read + write of one 512->512 residual-epilogue launch over 130560 "
+                                       "pixels; algorithmic 401.1 MB (input, residual, output)",
                      "peak_source": "measured live: dense tcgen05 kind::i8 probe (ufb_probe_i8_peak)",
                      "algorithmic": "8 int8 ops per int16 MAC",
                      "measured_on": "one extra step with the codec groups in turn, every convolution "
