@@ -455,8 +455,8 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
             const uint32_t a_ll = acc + (even ? 2 : 1) * kBN, a_x = acc + (even ? 1 : 2) * kBN,
                            a_hh = acc + (even ? 0 : 3) * kBN;
             // Drain LL and X 32 columns at a time, then hand the shared slots back
-            // to the MMA warp.  NARROW: D = P = LL + 256 X + 4096 (fits 32 bits
-            // for this layer's weights), so S + 4096 = 65536 HH + P.  Otherwise
+            // to the MMA warp.  NARROW: D = P = LL + 256 X (P + 4096 fits 32 bits
+            // for this layer's weights), so S = 65536 HH + P.  Otherwise
             // D = (X >> 5) + (U >> 13) with U = LL + 256 (X & 31) + 4096 and a
             // tie bit U % 8192 == 0, so S + 4096 = 8192 (8 HH + D) + (U & 8191).
             // Both slots come in with one wait, so the MMA warp gets them back
@@ -478,7 +478,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         const int32_t x = static_cast<int32_t>(xx[32 * i + t]);
                         const int32_t l = static_cast<int32_t>(ll[32 * i + t]);
                         if (NARROW) {
-                            D[32 * i + t] = x * c256 + (l + 4096);
+                            D[32 * i + t] = x * c256 + l;
                         } else {
                             const int32_t U = (x & 31) * c256 + (l + 4096);
                             D[32 * i + t] = (x >> 5) + (U >> 13);
@@ -488,9 +488,10 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                 }
             }
             // HH 16 columns at a time, the next 16 in flight while these are
-            // finished: T = floor((S + 4096) / 8192) rounds half up; an exact tie
-            // with S < 0 (T <= 0) takes T - 1 (half away from zero).  Then the
-            // bias and the fused table step.
+            // finished: rna(S / 8192) = floor((S + 4096 - [S < 0]) / 8192) (half
+            // away from zero); the general form takes T = floor((S + 4096) / 8192)
+            // and, at an exact tie with S < 0 (T <= 0), T - 1.  Then the bias and
+            // the fused table step.
             uint32_t hh_buf[2][16];
             tmem_ld16(a_hh, hh_buf[0]);
             tmem_wait_ld_regs(hh_buf[0]);
@@ -507,16 +508,16 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     for (int t = 0; t < 4; ++t) {
                         const int j = 16 * h + 4 * q + t;
                         const int32_t H8 = static_cast<int32_t>(hh[4 * q + t]) * c8;
-                        int32_t T;
-                        bool tie;
                         if (NARROW) {
-                            T = H8 + (D[j] >> 13);
-                            tie = (D[j] & 8191) == 0;
+                            // q = floor(S / 8192) is negative exactly when S is, and
+                            // rna(S / 8192) = 8 HH + floor((P + 4096 - [S < 0]) / 8192)
+                            const int32_t q = H8 + (D[j] >> 13);
+                            r[t] = H8 + ((D[j] + 4096 + (q >> 31)) >> 13) + bb[t];
                         } else {
-                            T = H8 + D[j];
-                            tie = (ties[j / 32] >> (j % 32)) & 1u;
+                            const int32_t T = H8 + D[j];
+                            const bool tie = (ties[j / 32] >> (j % 32)) & 1u;
+                            r[t] = T - static_cast<int32_t>(tie & (T <= 0)) + bb[t];
                         }
-                        r[t] = T - static_cast<int32_t>(tie & (T <= 0)) + bb[t];
                     }
                     if (MODE == kEpiLut || MODE == kEpiWsilu4) {
                         // table window: r is conv - window start (the staged bias
