@@ -86,7 +86,7 @@ constexpr size_t kSmemBudget = kSmemOptin - 256;  // host-side planning: static 
 // How an output tile is written.
 enum StoreKind : int {
     kStoreTma = 0,      // both planes through the stage, 128-channel boxes
-    kStoreTmaQuarter,   // wsilu4: 32 output channels per tile, both planes in one stage
+    kStoreThreadRows,   // wsilu4: each thread stores its pixel's 16 output channels per plane
     kStoreThreads,      // pixel shuffle: per-thread stores to four target pixels
 };
 
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapOut, const __grid_constant__ CUtensorMap mapRes1,
                    const __grid_constant__ CUtensorMap mapRes2, const ConvTcArgs args) {
-    constexpr int STORE = MODE == kEpiShuffle2 ? kStoreThreads : (MODE == kEpiWsilu4 ? kStoreTmaQuarter : kStoreTma);
+    constexpr int STORE = MODE == kEpiShuffle2 ? kStoreThreads : (MODE == kEpiWsilu4 ? kStoreThreadRows : kStoreTma);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr uint32_t kStage = warp_stage_bytes(MODE);
@@ -654,24 +654,31 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     __syncwarp();
                 }
             } else {
-                // wsilu4: kCols / 4 output channels per thread, both planes staged
-                // at once as [plane][32 pixels][16 channels] (16-byte rows)
+                // wsilu4: each thread holds kCols / 4 = 16 output channels of its
+                // pixel, stored as one 16-byte word per plane (the two column
+                // groups of a pixel fill its 32-byte sector together)
+                static_assert(kCols / 4 == 16, "wsilu4 stores 16 channels per thread");
+                uint32_t lw[4], hw[4];
 #pragma unroll
                 for (int h = 0; h < kCols / 16; ++h) {
                     const uint32_t w0 = pack2_sat(o4[4 * h], o4[4 * h + 1]), w1 = pack2_sat(o4[4 * h + 2], o4[4 * h + 3]);
-                    *reinterpret_cast<uint32_t*>(stage + lane * (kCols / 4) + 4 * h) = __byte_perm(w0, w1, 0x6420);
-                    *reinterpret_cast<uint32_t*>(stage + 8 * kCols + lane * (kCols / 4) + 4 * h) =
-                        __byte_perm(w0, w1, 0x7531);
+                    lw[h] = __byte_perm(w0, w1, 0x6420);
+                    hw[h] = __byte_perm(w0, w1, 0x7531);
                 }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    tma_store_quarter<SPATIAL>(&mapOut, stage, args, tc, quarter, cbase / 4, 0);
-                    tma_store_quarter<SPATIAL>(&mapOut, stage + 8 * kCols, args, tc, quarter, cbase / 4, 1);
-                    bulk_commit();
-                    bulk_wait_read();
+                const int oc = cbase / 4;
+                const int n_out = args.out.c - oc < 16 ? args.out.c - oc : 16;
+                if (valid && n_out > 0) {
+                    const long long opx = SPATIAL ? out.pixel(tc.img, oy, ox) : rpx1;
+                    if (n_out == 16) {
+                        *reinterpret_cast<uint4*>(out.lo(opx) + oc) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                        *reinterpret_cast<uint4*>(out.hi(opx) + oc) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    } else {
+                        for (int j = 0; j < n_out; ++j) {
+                            out.lo(opx)[oc + j] = static_cast<uint8_t>(lw[j >> 2] >> (8 * (j & 3)));
+                            out.hi(opx)[oc + j] = static_cast<uint8_t>(hw[j >> 2] >> (8 * (j & 3)));
+                        }
+                    }
                 }
-                __syncwarp();
             }
         }
         // abort path only: a residual load issued for a tile that was not finished
@@ -1075,15 +1082,12 @@ int conv_tc_run(const TcWeights& w, const Act& in, const Act& out, const Epilogu
     }
     // the activation box is the tile's input window (shifted per tap in spatial mode)
     if (!act_map(&maps.a, in, flat, tw, th, kBK, CU_TENSOR_MAP_SWIZZLE_128B, err, stride)) return -1;
-    // output box: one epilogue warp's 32 pixels, 64 channels (64-byte swizzle) or,
-    // for wsilu4, 16 channels (unswizzled); the map's extent is the view's, so
-    // tails are clipped
-    if (!epi.shuffle2) {
-        const cuuint32_t box_c = epi.wsilu4 ? kWarpCols / 4 : kWarpCols;
-        const CUtensorMapSwizzle sw = epi.wsilu4 ? CU_TENSOR_MAP_SWIZZLE_NONE : kStageSwizzle;
-        if (!act_map(&maps.out, out, flat, tw, 32 / tw, box_c, sw, err)) return -1;
+    // output box: one epilogue warp's 32 pixels, 64 channels (64-byte swizzle);
+    // the map's extent is the view's, so tails are clipped
+    if (!epi.shuffle2 && !epi.wsilu4) {
+        if (!act_map(&maps.out, out, flat, tw, 32 / tw, kWarpCols, kStageSwizzle, err)) return -1;
     } else {
-        maps.out = maps.a;  // unused: pixel-shuffled tiles are stored by the threads
+        maps.out = maps.a;  // unused: pixel-shuffled and wsilu4 tiles are stored by the threads
     }
     maps.res1 = maps.res2 = maps.a;  // unused unless residuals are fused
     // first residual: loaded per epilogue warp like the output box; second: L2 prefetch per tile
