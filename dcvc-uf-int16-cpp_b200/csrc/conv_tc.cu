@@ -195,13 +195,6 @@ __device__ __forceinline__ void release_tmem(uint64_t* bar, int lane) {
     if (lane == 0) mbar_arrive(bar);
 }
 
-// rna(S / 8192) from V = 8 HH + (X >> 5) and U = LL + 256 (X & 31) + 4096
-// (recombine32 split in two halves).
-__device__ __forceinline__ int32_t finish_rna(int32_t V, int32_t U) {
-    const int32_t T = V + (U >> 13);
-    return T - static_cast<int32_t>(((U & 8191) == 0) & (T <= 0));
-}
-
 // TMA load of one epilogue warp's box (residual rows), completing on bar.
 template <bool SPATIAL>
 __device__ __forceinline__ void tma_load_quarter(const CUtensorMap* map, void* dst, uint64_t* bar, const ConvTcArgs& a,
@@ -454,8 +447,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
             const bool even = (ti & 1) == 0;
             const uint32_t a_ll = acc + (even ? 2 : 1) * kBN, a_x = acc + (even ? 1 : 2) * kBN,
                            a_hh = acc + (even ? 0 : 3) * kBN;
-            // Drain LL and X 32 columns at a time, then hand the shared slots back
-            // to the MMA warp.  NARROW: D = P = LL + 256 X (P + 4096 fits 32 bits
+            // Drain LL and X, then hand the shared slots back to the MMA warp.  NARROW: D = P = LL + 256 X (P + 4096 fits 32 bits
             // for this layer's weights), so S = 65536 HH + P.  Otherwise
             // D = (X >> 5) + (U >> 13) with U = LL + 256 (X & 31) + 4096 and a
             // tie bit U % 8192 == 0, so S + 4096 = 8192 (8 HH + D) + (U & 8191).
@@ -509,10 +501,10 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         const int j = 16 * h + 4 * q + t;
                         const int32_t H8 = static_cast<int32_t>(hh[4 * q + t]) * c8;
                         if (NARROW) {
-                            // q = floor(S / 8192) is negative exactly when S is, and
+                            // fl = floor(S / 8192) is negative exactly when S is, and
                             // rna(S / 8192) = 8 HH + floor((P + 4096 - [S < 0]) / 8192)
-                            const int32_t q = H8 + (D[j] >> 13);
-                            r[t] = H8 + ((D[j] + 4096 + (q >> 31)) >> 13) + bb[t];
+                            const int32_t fl = H8 + (D[j] >> 13);
+                            r[t] = H8 + ((D[j] + 4096 + (fl >> 31)) >> 13) + bb[t];
                         } else {
                             const int32_t T = H8 + D[j];
                             const bool tie = (ties[j / 32] >> (j % 32)) & 1u;
