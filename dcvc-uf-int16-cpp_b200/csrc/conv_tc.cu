@@ -431,8 +431,10 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
             const int cbase = tc.co0 + cgroup * kCols;
             if (MODE == kEpiRes && lane == 0) {
                 // this warp's 32 x 64 residual tile (both planes): in flight while the
-                // MMAs finish and the accumulators are recombined; the stage is free
-                // (the last TMA store out of it has been read)
+                // MMAs finish and the accumulators are recombined, once the previous
+                // tile's TMA store has read the stage (that store was left in flight
+                // so the previous tile did not wait for it)
+                bulk_wait_read();
                 mbar_arrive_expect_tx(&res_bar[ew], 2 * kPlaneStage);
                 tma_load_quarter<SPATIAL>(&mapRes1, stage, &res_bar[ew], args, tc, quarter, cbase, 0);
                 tma_load_quarter<SPATIAL>(&mapRes1, stage + kPlaneStage, &res_bar[ew], args, tc, quarter, cbase, 1);
@@ -616,10 +618,8 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                 if (lane == 0) {
                     tma_store_quarter<SPATIAL>(&mapOut, stage, args, tc, quarter, cbase, 0);
                     tma_store_quarter<SPATIAL>(&mapOut, stage + kPlaneStage, args, tc, quarter, cbase, 1);
-                    bulk_commit();
-                    bulk_wait_read();
+                    bulk_commit();  // read by the next tile's residual load (bulk_wait_read there)
                 }
-                __syncwarp();
             } else if (STORE == kStoreTma) {
                 // each warp stores its own 32 pixels x 64 channels, one byte plane
                 // at a time, through its 2 KB stage in the 64-byte swizzle
@@ -627,6 +627,10 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                 // the eight lanes of a shared-memory phase hit distinct banks
 #pragma unroll
                 for (int plane = 0; plane < 2; ++plane) {
+                    // the stage is free once the previous store out of it (the other
+                    // plane, or the previous tile's second plane, left in flight) is read
+                    if (lane == 0) bulk_wait_read();
+                    __syncwarp();
 #pragma unroll
                     for (int h = 0; h < kCols / 16; ++h) {
                         uint32_t p8[8];
@@ -641,9 +645,7 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     if (lane == 0) {
                         tma_store_quarter<SPATIAL>(&mapOut, stage, args, tc, quarter, cbase, plane);
                         bulk_commit();
-                        bulk_wait_read();  // the stage is reused by the next plane
                     }
-                    __syncwarp();
                 }
             } else {
                 // wsilu4: each thread holds kCols / 4 = 16 output channels of its
