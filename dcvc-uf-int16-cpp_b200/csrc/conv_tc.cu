@@ -373,24 +373,28 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                     const uint32_t a_lo = base, a_hi = base + kABytes, b_first = base + 2 * kABytes,
                                    b_second = b_first + kBN * kBK;
                     const uint32_t b_lo = even ? b_second : b_first, b_hi = even ? b_first : b_second;
+                    // descriptors are linear in the start address (its >> 4 in the low
+                    // bits), so each K step adds 32 >> 4 = 2 to the block's base ones
+                    const uint64_t q_alo = sw128_desc(a_lo), q_ahi = sw128_desc(a_hi), q_bf = sw128_desc(b_first),
+                                   q_blo = sw128_desc(b_lo), q_bhi = sw128_desc(b_hi);
 #pragma unroll
                     for (int kk = 0; kk < kBK / 32; ++kk) {
-                        const uint32_t o = kk * 32;
+                        const uint64_t o = 2 * kk;
                         const bool first = k == 0 && kk == 0;
                         if (SIGNED) {
-                            mma_i8(d_lo2, sw128_desc(a_lo + o), sw128_desc(b_first + o), i_us2, first ? 0u : 1u);
+                            mma_i8(d_lo2, q_alo + o, q_bf + o, i_us2, first ? 0u : 1u);
                             if (first) {
-                                mma_i8(d_x, sw128_desc(a_hi + o), sw128_desc(b_lo + o), i_ss, 1u);
-                                mma_i8(d_hh, sw128_desc(a_hi + o), sw128_desc(b_hi + o), i_ss, 0u);
+                                mma_i8(d_x, q_ahi + o, q_blo + o, i_ss, 1u);
+                                mma_i8(d_hh, q_ahi + o, q_bhi + o, i_ss, 0u);
                             } else {
-                                mma_i8(d_hi2, sw128_desc(a_hi + o), sw128_desc(b_first + o), i_ss2, 1u);
+                                mma_i8(d_hi2, q_ahi + o, q_bf + o, i_ss2, 1u);
                             }
                         } else {
                             const uint32_t acc = first ? 0u : 1u;
-                            mma_i8(d_ll, sw128_desc(a_lo + o), sw128_desc(b_lo + o), i_uu, acc);
-                            mma_i8(d_x, sw128_desc(a_hi + o), sw128_desc(b_lo + o), i_su, acc);
-                            mma_i8(d_x, sw128_desc(a_lo + o), sw128_desc(b_hi + o), i_us, 1u);
-                            mma_i8(d_hh, sw128_desc(a_hi + o), sw128_desc(b_hi + o), i_ss, acc);
+                            mma_i8(d_ll, q_alo + o, q_blo + o, i_uu, acc);
+                            mma_i8(d_x, q_ahi + o, q_blo + o, i_su, acc);
+                            mma_i8(d_x, q_alo + o, q_bhi + o, i_us, 1u);
+                            mma_i8(d_hh, q_ahi + o, q_bhi + o, i_ss, acc);
                         }
                     }
                     mma_commit(&empty_bar[s]);
