@@ -145,20 +145,61 @@ def reduce_over_ranks(value, world, device, op):
     return float(t.item())
 
 
-def print_shapes(codecs, frames):
-    """Per launch shape convolution time of the timed steps, to stderr."""
+def merged_shapes(codecs):
+    """The profiled launches of several codecs by shape and epilogue:
+    {shape: [launches, int16 MACs, ms, algorithmic DRAM bytes]}."""
     table = {}
     for c in codecs:
-        for k, (n, macs, ms) in c.shape_table().items():
-            t = table.setdefault(k, [0, 0.0, 0.0])
-            t[0] += n
-            t[1] += macs
-            t[2] += ms
+        for k, v in c.shape_table().items():
+            t = table.setdefault(k, [0, 0.0, 0.0, 0.0])
+            for i in range(4):
+                t[i] += v[i]
+    return table
+
+
+def print_shapes(table, frames):
+    """Per launch shape convolution time of the profiled step, to stderr."""
     total = sum(t[2] for t in table.values())
-    print(f"# shape  launches  ms  share  int8-TOPS  ({frames} frames)", file=sys.stderr)
-    for k, (n, macs, ms) in sorted(table.items(), key=lambda kv: -kv[1][2]):
+    print(f"# shape  launches  ms  share  int8-TOPS  GB/s  ({frames} frames)", file=sys.stderr)
+    for k, (n, macs, ms, hbm) in sorted(table.items(), key=lambda kv: -kv[1][2]):
         tops = 8 * macs / (ms * 1e-3) / 1e12 if ms else 0.0
-        print(f"{k:40s} {n:6d} {ms:9.2f} {ms / total * 100:5.1f}% {tops:7.0f}", file=sys.stderr)
+        gbs = hbm / (ms * 1e-3) / 1e9 if ms else 0.0
+        print(f"{k:52s} {n:6d} {ms:9.2f} {ms / total * 100:5.1f}% {tops:7.0f} {gbs:7.0f}", file=sys.stderr)
+
+
+def launch_rooflines(table, peak_tops, hbm_gbs, step_ms):
+    """Roofline of every profiled launch: the slower of its int8 MMA time at
+    peak_tops and its algorithmic DRAM bytes at hbm_gbs.  Returns the
+    tensor-core convolutions' summed floor against their summed event time
+    and the depthwise launches' DRAM throughput."""
+    floor = meas = hbm_ms = 0.0
+    for k, (n, macs, ms, hbm) in table.items():
+        if not k.startswith("conv") or not ms:
+            continue
+        t_tensor = 8 * macs / (peak_tops * 1e12) * 1e3
+        t_hbm = hbm / (hbm_gbs * 1e9) * 1e3
+        floor += max(t_tensor, t_hbm)
+        meas += ms
+        if t_hbm > t_tensor:
+            hbm_ms += ms
+    dw = [v for k, v in table.items() if k.startswith("depthwise")]
+    dw_ms = sum(v[2] for v in dw)
+    dw_bytes = sum(v[3] for v in dw)
+    conv = {"frac": floor / meas if meas else None, "floor_ms": floor, "measured_ms": meas,
+            "hbm_bound_time_share": hbm_ms / meas if meas else None,
+            "peak_tops": peak_tops, "hbm_gbs": hbm_gbs,
+            "rule": "per launch the slower of its int8 MMA time at the sustained probe peak and its algorithmic "
+                    "DRAM bytes (input and residuals read once, output written once, weights) at the measured "
+                    "copy bandwidth; summed over the step's tensor-core convolutions and divided by their "
+                    "summed event time"}
+    depth = None
+    if dw_ms:
+        depth = {"launches": int(sum(v[0] for v in dw)), "ms": dw_ms,
+                 "share_of_serial_step": dw_ms / step_ms if step_ms else None,
+                 "achieved_gbs": dw_bytes / (dw_ms * 1e-3) / 1e9,
+                 "frac": dw_bytes / (dw_ms * 1e-3) / 1e9 / hbm_gbs, "bound": "hbm", "peak_gbs": hbm_gbs,
+                 "algorithmic": "input read once, output written once (both byte planes), weights"}
+    return conv, depth
 
 
 def load_traffic(key):
@@ -334,13 +375,15 @@ def bench_decode_ours(args, rank, world, local):
         torch.cuda.nvtx.range_pop()
         barrier(world)
         st = {"launches": 0, "conv_launches": 0, "conv_int16_macs": 0.0, "conv_ms": 0.0}
-        if args.shapes and profile:
-            print_shapes([c for pair in decoders for c in pair], frames)
+        if profile:
+            st["shapes"] = merged_shapes([c for pair in decoders for c in pair])
+            if args.shapes:
+                print_shapes(st["shapes"], frames)
         for pair in decoders:
             for c in pair:
                 s = c.stats()
                 c.profile(False)
-                for k in st:
+                for k in s:
                     st[k] += s[k]
         return frames, e0.elapsed_time(e1), st
 
@@ -383,6 +426,8 @@ def bench_decode_ours(args, rank, world, local):
 
     per_step_ms = ms / args.steps
     achieved = 8 * pst["conv_int16_macs"] / (pst["conv_ms"] * 1e-3) / 1e12 if pst["conv_ms"] else None
+    hbm, hbm_src = hbm_peak()
+    per_launch, depthwise = launch_rooflines(pst["shapes"], peak, hbm, prof_ms)
     secondary = None
     if world == 1 and not args.no_secondary:
         del decoders, sinks
@@ -427,7 +472,10 @@ def bench_decode_ours(args, rank, world, local):
                                     "bracketed by CUDA events on its stream",
                      "conv_share_of_serial_step": pst["conv_ms"] / prof_ms if prof_ms else None,
                      "conv_launches_per_step": pst["conv_launches"],
-                     "conv_int16_macs_per_step": pst["conv_int16_macs"]},
+                     "conv_int16_macs_per_step": pst["conv_int16_macs"],
+                     # the same launches against each one's own bound (tensor or DRAM)
+                     "per_launch_roofline": dict(per_launch, hbm_source=hbm_src)},
+        "depthwise": depthwise,
         "e2e": {"value": e2e_total / (e2e_ms * 1e-3), "unit": "frames/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
         "secondary": secondary,
@@ -483,30 +531,37 @@ def bench_626(ufb, syn, mi, mv, dev, stream, peak):
         e1.record(stream)
         torch.cuda.synchronize()
         st = {"conv_int16_macs": 0.0, "conv_ms": 0.0}
+        if profile:
+            st["shapes"] = merged_shapes([c for pair in decoders for c in pair])
         for pair in decoders:
             for c in pair:
                 x = c.stats()
                 c.profile(False)
-                for k in st:
+                for k in ("conv_int16_macs", "conv_ms"):
                     st[k] += x[k]
         return n, e0.elapsed_time(e1), st
 
     run(2)
     frames, ms, _ = run(3)
-    _, _, pst = run(1, profile=True)
+    _, prof_ms, pst = run(1, profile=True)
     for g, (_, dv) in enumerate(decoders):
         for k, want in groups[g][5].items():
             if dv.state_hash(k) != want:
                 raise RuntimeError(f"626x352 group {g}: decoder {k} state differs from the encoder's")
     achieved = 8 * pst["conv_int16_macs"] / (pst["conv_ms"] * 1e-3) / 1e12 if pst["conv_ms"] else None
+    hbm, _ = hbm_peak()
+    per_launch, depthwise = launch_rooflines(pst["shapes"], peak, hbm, prof_ms)
     out["multi_stream"] = {
         "value": frames / (ms * 1e-3), "unit": "frames/s", "ms_per_step": ms / 3, "steps": 3,
         "workload": f"{SEQS} seqs x {FRAMES} frames 626x352 (seeds 3..{2 + SEQS}), I + 4 P packets each, "
                     "qp_i 0 qp_p 20, reset 8, skip 0.2, two concurrent codec groups",
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS(int8)",
                      "frac": achieved / peak if achieved else None,
+                     "per_launch_roofline_frac": per_launch["frac"],
+                     "hbm_bound_time_share": per_launch["hbm_bound_time_share"],
                      "measured_on": "one extra step, groups in turn, every tensor-core convolution bracketed "
-                                    "by CUDA events"}}
+                                    "by CUDA events"},
+        "depthwise": depthwise}
     del decoders, groups
 
     # single stream: the config-4 GOP (120 frames: I + 15 P packets), batch 1

@@ -73,7 +73,8 @@ def _cuda(t: torch.Tensor, dtype, what: str) -> torch.Tensor:
 
 
 def set_conv_max_ctas(n: int) -> None:
-    """Testing aid: cap the persistent convolution grid at n CTAs (0: one per SM)."""
+    """Testing aid: cap the persistent tensor-core and depthwise convolution
+    grids at n CTAs (0: no cap)."""
     _check(library().ufb_set_conv_max_ctas(int(n)))
 
 
@@ -423,16 +424,17 @@ class Codec:
         return {"launches": a.value, "conv_launches": b.value, "conv_int16_macs": m.value, "conv_ms": t.value}
 
     def shape_table(self):
-        """Profiled convolution time per launch shape since the last stats reset:
-        {shape: (launches, int16 MACs, ms)} (profiling must be on)."""
+        """Profiled convolution time per launch shape and epilogue since the last
+        stats reset: {shape: (launches, int16 MACs, ms, algorithmic DRAM bytes)}
+        (profiling must be on)."""
         n = C.c_int64()
         _check(self.L.ufb_codec_shape_table(self.h, None, 0, C.byref(n)))
         buf = C.create_string_buffer(n.value + 1)
         _check(self.L.ufb_codec_shape_table(self.h, buf, n.value + 1, C.byref(n)))
         table = {}
         for line in buf.value.decode().splitlines():
-            shape, launches, macs, ms = line.split("\t")
-            table[shape] = (int(launches), float(macs), float(ms))
+            shape, launches, macs, ms, hbm = line.split("\t")
+            table[shape] = (int(launches), float(macs), float(ms), float(hbm))
         return table
 
 

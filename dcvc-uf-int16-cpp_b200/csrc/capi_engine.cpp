@@ -233,10 +233,10 @@ int ufb_codec_shape_table(ufb_codec* c, char* text, int64_t capacity, int64_t* l
         if (!c || !length) throw std::invalid_argument("codec or length is null");
         EngineStats& st = c->c->stats();
         std::string out;
-        char line[192];
+        char line[256];
         for (const auto& kv : st.shapes) {
-            snprintf(line, sizeof(line), "%s\t%lld\t%.6g\t%.6f\n", kv.first.c_str(), kv.second.launches,
-                     kv.second.int16_macs, kv.second.ms);
+            snprintf(line, sizeof(line), "%s\t%lld\t%.9g\t%.6f\t%.9g\n", kv.first.c_str(), kv.second.launches,
+                     kv.second.int16_macs, kv.second.ms, kv.second.hbm_bytes);
             out += line;
         }
         *length = static_cast<int64_t>(out.size());

@@ -156,14 +156,25 @@ __device__ __forceinline__ void store_shuffle2(const Act& out, const uint32_t (&
     }
 }
 
-// v = sat(v + res) for 16 packed outputs of one pixel at a ragged channel tail
-// (n_valid < 16 channels are real; src/layers.cpp:98-104).
+// v = sat(v + res) for 16 packed outputs of one pixel, the second residual of
+// the fused epilogue (n_valid < 16 at a ragged channel tail; src/layers.cpp:98-104).
 __device__ __forceinline__ void add_one_residual(const Act& res, uint32_t (&p)[8], int cbase, int n_valid,
                                                  long long rp) {
     uint32_t wl[4] = {0, 0, 0, 0}, wh[4] = {0, 0, 0, 0};
-    for (int j = 0; j < n_valid; ++j) {
-        wl[j >> 2] |= static_cast<uint32_t>(res.lo(rp)[cbase + j]) << (8 * (j & 3));
-        wh[j >> 2] |= static_cast<uint32_t>(res.hi(rp)[cbase + j]) << (8 * (j & 3));
+    const uint8_t* lo = res.lo(rp) + cbase;
+    const uint8_t* hi = lo + res.pitch;
+    if (n_valid == 16 && ((reinterpret_cast<uintptr_t>(lo) | reinterpret_cast<uintptr_t>(hi)) & 15) == 0) {
+        // 16 channels of both planes in two 16-byte loads
+        const uint4 l = *reinterpret_cast<const uint4*>(lo);
+        const uint4 h = *reinterpret_cast<const uint4*>(hi);
+        wl[0] = l.x, wl[1] = l.y, wl[2] = l.z, wl[3] = l.w;
+        wh[0] = h.x, wh[1] = h.y, wh[2] = h.z, wh[3] = h.w;
+    } else {
+        // channel tails and views that are not 16-byte aligned: byte by byte
+        for (int j = 0; j < n_valid; ++j) {
+            wl[j >> 2] |= static_cast<uint32_t>(lo[j]) << (8 * (j & 3));
+            wh[j >> 2] |= static_cast<uint32_t>(hi[j]) << (8 * (j & 3));
+        }
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -861,6 +872,7 @@ bool act_map(CUtensorMap* map, const Act& v, bool flat, int tw, int th, cuuint32
 }  // namespace
 
 void tc_set_max_ctas(int n) { g_max_ctas.store(n > 0 ? n : 0, std::memory_order_relaxed); }
+int tc_max_ctas() { return g_max_ctas.load(std::memory_order_relaxed); }
 
 void tc_set_narrow(bool enable) { g_narrow.store(enable, std::memory_order_relaxed); }
 

@@ -67,9 +67,12 @@ bool tc_encode_map(CUtensorMap* map, void* base, int rank, const cuuint64_t* dim
                    const cuuint32_t* box, std::string& err,
                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
-// Caps the persistent grid at n CTAs (0: one per SM).  A testing aid: with few
-// CTAs every CTA walks many tiles, which exercises both TMEM accumulator sets.
+// Caps the persistent grids of the tensor-core and depthwise convolutions at n
+// CTAs (0: no cap).  A testing aid: with few CTAs every CTA walks many tiles,
+// which exercises both TMEM accumulator sets and every reuse of the depthwise
+// window buffers.
 void tc_set_max_ctas(int n);
+int tc_max_ctas();
 
 // True when, for every output channel o of these int16 [co, ci, kh, kw] weights
 // (host data) in the given byte split, sum_k 32768 |wl| + 65280 |wh| + 4096 fits

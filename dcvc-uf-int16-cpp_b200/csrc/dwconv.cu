@@ -130,11 +130,13 @@ __device__ __forceinline__ void dw_add(DwAcc& a, const DwRow& lo, const DwRow& h
 // U = l + 256 (h & 31) and T = (h >> 5) + (U >> 13) = floor((S + 4096) / 8192)
 // + bias, and an exact tie (U % 8192 == 0) with S < 0, i.e. T <= bias, rounds
 // away from zero to T - 1 (the recombination of conv_epi.cuh, recombine32).
-__device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], const Act& out, int img, int oy,
-                                         int ox, int c0) {
+// The output pixel of column j sits at lo + j * px_bytes (low plane) and
+// pitch bytes further (high plane); columns from ncols on are outside the image.
+__device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], uint8_t* lo, long long px_bytes,
+                                         int pitch, int ncols) {
 #pragma unroll
     for (int j = 0; j < kCols; ++j) {
-        if (ox + j >= out.w) break;
+        if (j >= ncols) break;
         int32_t r[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -143,9 +145,9 @@ __device__ __forceinline__ void dw_store(const DwAcc& a, const int32_t (&b)[4], 
             r[c] = T - static_cast<int32_t>(((U & 8191) == 0) & (T <= b[c]));
         }
         const uint32_t p0 = pack2_sat(r[0], r[1]), p1 = pack2_sat(r[2], r[3]);
-        const long long px = out.pixel(img, oy, ox + j);
-        *reinterpret_cast<uint32_t*>(out.lo(px) + c0) = __byte_perm(p0, p1, 0x6420);
-        *reinterpret_cast<uint32_t*>(out.hi(px) + c0) = __byte_perm(p0, p1, 0x7531);
+        uint8_t* dst = lo + j * px_bytes;
+        *reinterpret_cast<uint32_t*>(dst) = __byte_perm(p0, p1, 0x6420);
+        *reinterpret_cast<uint32_t*>(dst + pitch) = __byte_perm(p0, p1, 0x7531);
     }
 }
 
@@ -203,18 +205,19 @@ __device__ __forceinline__ void dw_add_n(DwAccN& a, const DwRowN& row, const int
 
 // sat(rna(S / 8192) + bias) from s = S + 4096 + 8192 bias: rna(S / 8192) =
 // floor((S + 4096 - [S < 0]) / 8192), and S < 0 exactly when s < s0.
-__device__ __forceinline__ void dw_store_n(const DwAccN& a, const int32_t (&s0)[4], const Act& out, int img, int oy,
-                                           int ox, int c0) {
+// (stored as dw_store does).
+__device__ __forceinline__ void dw_store_n(const DwAccN& a, const int32_t (&s0)[4], uint8_t* lo, long long px_bytes,
+                                           int pitch, int ncols) {
 #pragma unroll
     for (int j = 0; j < kCols; ++j) {
-        if (ox + j >= out.w) break;
+        if (j >= ncols) break;
         int32_t r[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) r[c] = (a.s[j][c] - static_cast<int32_t>(a.s[j][c] < s0[c])) >> 13;
         const uint32_t p0 = pack2_sat(r[0], r[1]), p1 = pack2_sat(r[2], r[3]);
-        const long long px = out.pixel(img, oy, ox + j);
-        *reinterpret_cast<uint32_t*>(out.lo(px) + c0) = __byte_perm(p0, p1, 0x6420);
-        *reinterpret_cast<uint32_t*>(out.hi(px) + c0) = __byte_perm(p0, p1, 0x7531);
+        uint8_t* dst = lo + j * px_bytes;
+        *reinterpret_cast<uint32_t*>(dst) = __byte_perm(p0, p1, 0x6420);
+        *reinterpret_cast<uint32_t*>(dst + pitch) = __byte_perm(p0, p1, 0x7531);
     }
 }
 
@@ -238,8 +241,10 @@ dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t
                      int total_tiles, int* status) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-    __shared__ __align__(8) uint64_t full[2];
-    const int q = threadIdx.x % kQuads, t = threadIdx.x / kQuads;
+    // full[b]: the window load into buffer b landed; empty[b]: every warp is
+    // done reading buffer b (one arrival per warp)
+    __shared__ __align__(8) uint64_t full[2], empty[2];
+    const int q = threadIdx.x % kQuads, t = threadIdx.x / kQuads;  // t is also the warp index
     const int per_block = tiles_x * tiles_y * images;  // tiles of one channel block
 
     auto issue = [&](int tile, int b) {
@@ -258,6 +263,8 @@ dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t
     if (threadIdx.x == 0) {
         mbar_init(&full[0], 1);
         mbar_init(&full[1], 1);
+        mbar_init(&empty[0], kThreads / 32);
+        mbar_init(&empty[1], kThreads / 32);
         fence_mbar_init();
         prefetch_tmap(&map);
     }
@@ -272,9 +279,21 @@ dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t
     bool next_issued = false;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++i) {
         const int b = i & 1;
-        // the other buffer was released by the barrier that ended the previous tile
         next_issued = tile + static_cast<int>(gridDim.x) < total_tiles;
-        if (threadIdx.x == 0 && next_issued) issue(tile + gridDim.x, b ^ 1);
+        if (t == 0) {
+            // warp 0 refills the other buffer once every warp has released its
+            // previous use (tile i - 1); the other warps run on meanwhile
+            int ok = 1;
+            if (q == 0 && next_issued) {
+                ok = i == 0 || mbar_wait(&empty[b ^ 1], ((i - 1) >> 1) & 1, status, 11);
+                if (ok) issue(tile + gridDim.x, b ^ 1);
+            }
+            if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                // abort: the load into this tile's buffer must land before the CTA exits
+                if (q == 0) mbar_wait(&full[b], (i >> 1) & 1, status, 10);
+                break;
+            }
+        }
         const int cb = tile / per_block;
         int r = tile - cb * per_block;
         const int tx = r % tiles_x;
@@ -304,14 +323,19 @@ dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t
             loaded_cb = cb;
         }
         const bool ready = mbar_wait(&full[b], (i >> 1) & 1, status, 9);
-        if (!__syncthreads_and(ready)) {
-            // abort: the window load of the next tile must land before the CTA exits
+        if (!__all_sync(0xffffffffu, ready)) {
+            // abort (every wait is bounded, so the other warps give up too): the
+            // window load of the next tile must land before the CTA exits
             if (threadIdx.x == 0 && next_issued) mbar_wait(&full[b ^ 1], ((i + 1) >> 1) & 1, status, 10);
             break;
         }
         const uint8_t* buf = smem + b * kBuffer;
         const int oy0 = ty * kTileH, ox = tx * kTileW + kCols * t;
         const bool active = c0 < channels && ox < out.w;
+        // low-plane address of this thread's first output of the next row to store
+        const long long px_bytes = 2ll * out.pitch, row_bytes = px_bytes * out.row_px;
+        const int ncols = min(kCols, out.w - ox);
+        uint8_t* dst = active ? out.lo(out.pixel(img, oy0, ox)) + c0 : nullptr;
         if (active && NARROW) {
             // the general path's row schedule with whole-value sums
             const int32_t s0[4] = {4096 + 8192 * bv[0], 4096 + 8192 * bv[1], 4096 + 8192 * bv[2],
@@ -324,7 +348,8 @@ dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t
                 if (wr >= 1) dw_add_n<false>(mid, row, wn[1], s0);
                 if (wr >= 2) {
                     dw_add_n<false>(done, row, wn[2], s0);
-                    if (oy0 + wr - 2 < out.h) dw_store_n(done, s0, out, img, oy0 + wr - 2, ox, c0);
+                    if (oy0 + wr - 2 < out.h) dw_store_n(done, s0, dst, px_bytes, out.pitch, ncols);
+                    dst += row_bytes;
                 }
             };
 #pragma unroll 1
@@ -349,7 +374,10 @@ dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t
                 dw_add<true>(next, lo, hi, wp[0], ws[0], h0);
                 dw_add<false>(mid, lo, hi, wp[1], ws[1], h0);
                 dw_add<false>(done, lo, hi, wp[2], ws[2], h0);
-                if (wr >= 2 && oy0 + wr - 2 < out.h) dw_store(done, bv, out, img, oy0 + wr - 2, ox, c0);
+                if (wr >= 2) {
+                    if (oy0 + wr - 2 < out.h) dw_store(done, bv, dst, px_bytes, out.pitch, ncols);
+                    dst += row_bytes;
+                }
             };
 #pragma unroll 1
             for (int wr = 0; wr < kInH; wr += 3) {
@@ -360,7 +388,8 @@ dwconv3x3_kernel(const __grid_constant__ CUtensorMap map, Act out, const int16_t
                 step(a1, a2, a0, wr + 2);
             }
         }
-        __syncthreads();  // every thread is done with this buffer before it is refilled
+        __syncwarp();
+        if (q == 0) mbar_arrive(&empty[b]);  // this warp is done with the buffer
     }
 }
 
@@ -405,7 +434,9 @@ cudaError_t dwconv3x3(const Act& in, const Act& out, const int16_t* weight, cons
     if (attr != cudaSuccess) return attr;
     int device = 0, sms = 148;
     if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    const long long grid = total < 2ll * sms ? total : 2ll * sms;
+    long long grid = total < 2ll * sms ? total : 2ll * sms;
+    const int cap = tc_max_ctas();
+    if (cap > 0 && grid > cap) grid = cap;
     kernel<<<static_cast<unsigned>(grid), kThreads, kSmem, s>>>(map, out, weight, bias, in.c, tiles_x, tiles_y, in.n,
                                                                  static_cast<int>(total), status);
     return cudaGetLastError();

@@ -297,11 +297,14 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
             cudaEvent_t ev1 = stats_->take_event();
             ck(cudaEventRecord(ev1, s_), "event");
             char key[96];
-            snprintf(key, sizeof(key), "depthwise %d 3x3 @ %lld", L->co, static_cast<long long>(in.a.n) * oh * ow);
+            const long long px = static_cast<long long>(in.a.n) * oh * ow;
+            snprintf(key, sizeof(key), "depthwise %d 3x3 @ %lld", L->co, px);
             stats_->pending.push_back({ev0, ev1, key, false});
             auto& sh = stats_->shapes[key];
             ++sh.launches;
-            sh.int16_macs += static_cast<double>(in.a.n) * oh * ow * L->co * 9;
+            sh.int16_macs += static_cast<double>(px) * L->co * 9;
+            sh.hbm_bytes += 2.0 * (static_cast<double>(in.a.pixels()) * in.a.c + static_cast<double>(px) * L->co +
+                                   9.0 * L->co);
         }
         count();
         return out;
@@ -340,13 +343,19 @@ Tensor Runner::conv(const std::string& name, const Tensor& in, const Fuse& f, co
         if (ev0) {
             cudaEvent_t ev1 = stats_->take_event();
             ck(cudaEventRecord(ev1, s_), "event");
-            char key[96];
-            snprintf(key, sizeof(key), "conv %d>%d %dx%d%s @ %lld", L->ci, L->co, L->kh, L->kw,
-                     stride == 2 ? "/2" : "", static_cast<long long>(in.a.n) * oh * ow);
+            char key[128];
+            const char* epi = f.wsilu4 ? " +wsilu4" : f.lut ? " +lut" : f.shuffle2 ? " +shuffle2" : "";
+            snprintf(key, sizeof(key), "conv %d>%d %dx%d%s%s%s%s%s @ %lld", L->ci, L->co, L->kh, L->kw,
+                     stride == 2 ? "/2" : "", epi, f.res1 ? " +res" : "", f.res2 ? " +res" : "",
+                     f.mulq ? " +mulq" : "", static_cast<long long>(in.a.n) * oh * ow);
             stats_->pending.push_back({ev0, ev1, key, true});
             auto& sh = stats_->shapes[key];
             ++sh.launches;
             sh.int16_macs += macs;
+            const double out_values = static_cast<double>(out.a.pixels()) * out.a.c;
+            sh.hbm_bytes += 2.0 * (static_cast<double>(in.a.pixels()) * in.a.c + out_values *
+                                   (1 + (f.res1 ? 1 : 0) + (f.res2 ? 1 : 0)) +
+                                   static_cast<double>(L->co) * L->ci * L->kh * L->kw);
         }
         if (stats_) {
             ++stats_->launches;

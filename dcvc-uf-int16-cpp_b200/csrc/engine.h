@@ -145,12 +145,15 @@ struct EngineStats {
     double conv_int16_macs = 0;    // algorithmic int16 MACs of those launches
     double conv_ms = 0;            // summed event time of those launches (profiling on)
     bool profile = false;
-    // per launch shape ("conv ci>co kh x kw @ pixels", "depthwise c @ pixels"),
-    // filled while profiling is on
+    // per launch shape and epilogue ("conv ci>co kh x kw +epilogue @ pixels",
+    // "depthwise c 3x3 @ pixels"), filled while profiling is on; hbm_bytes is
+    // the launch's algorithmic DRAM traffic (input and residuals read once,
+    // output written once, weights)
     struct Shape {
         long long launches = 0;
         double int16_macs = 0;
         double ms = 0;
+        double hbm_bytes = 0;
     };
     std::map<std::string, Shape> shapes;
     struct Pending {

@@ -42,9 +42,10 @@ int ufb_version(void);
 /* Message of the last failing call on this thread ("" if none). */
 const char* ufb_last_error(void);
 
-/* Testing aid (no reference counterpart): caps the persistent tensor-core
- * convolution grid at n CTAs per launch (0 restores one CTA per SM), so small
- * problems still run many tiles per CTA.  Process-wide; not for production. */
+/* Testing aid (no reference counterpart): caps the persistent tensor-core and
+ * depthwise convolution grids at n CTAs per launch (0 removes the cap), so
+ * small problems still run many tiles per CTA.  Process-wide; not for
+ * production. */
 int ufb_set_conv_max_ctas(int n);
 
 /* Testing aid (no reference counterpart): enable (1, the default) or disable
@@ -275,7 +276,8 @@ int ufb_codec_stats(ufb_codec* c, int reset, int64_t* launches, int64_t* conv_la
                     double* conv_ms);
 /* Per launch shape breakdown of the profiled convolutions (tensor-core and
  * depthwise) since the last reset, one tab-separated line per shape:
- * "<shape>\t<launches>\t<int16 MACs>\t<ms>".  Writes at most capacity - 1 bytes
+ * "<shape>\t<launches>\t<int16 MACs>\t<ms>\t<algorithmic DRAM bytes>" (the launches'
+ * inputs and residuals read once, outputs written once, weights).  Writes at most capacity - 1 bytes
  * plus a terminating zero and sets *length to the full text length. */
 int ufb_codec_shape_table(ufb_codec* c, char* text, int64_t capacity, int64_t* length);
 

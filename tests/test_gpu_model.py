@@ -367,6 +367,22 @@ def test_narrow_bound_edges(ufb, ref, syn, margin):
     assert np.array_equal(mine.run("feature_extractor", x), theirs.run("feature_extractor", x))
 
 
+def test_depthwise_narrow_many_tiles_per_cta(ufb, models):
+    """The narrow depthwise instance (every dc.2 of the seeded model) with the
+    grids capped at two CTAs: each depthwise CTA walks 12 of the 24 tiles
+    (4 channel blocks x 3 x 2), refilling both window buffers behind the
+    warps' release barriers."""
+    mine, theirs = models["htl"]
+    x = rnd(np.random.default_rng(43), (1, 512, 12, 36))
+    want = theirs.run("feature_extractor", x)
+    ufb.set_conv_max_ctas(2)
+    try:
+        got = mine.run("feature_extractor", x)
+    finally:
+        ufb.set_conv_max_ctas(0)
+    assert np.array_equal(got, want)
+
+
 @pytest.mark.parametrize("margin", ["inside", "outside"])
 def test_depthwise_narrow_bound_edges(ufb, ref, syn, margin):
     """The depthwise dc.2 sums run in one int32 when, per channel,

@@ -209,6 +209,25 @@ def test_depthwise_split_kernel(ufb, ora, dev, n, c, h, w):
     _status_clean(ufb)
 
 
+@pytest.mark.parametrize("ctas", [1, 5])
+def test_depthwise_many_tiles_per_cta(ufb, ora, dev, ctas):
+    """With the grid capped every depthwise CTA walks many tiles, so both
+    window buffers are refilled many times behind the warps' release
+    barriers (60 tiles: 2 channel blocks x 3 x 5 per image, 2 images)."""
+    rng = np.random.default_rng(41 + ctas)
+    n, c, h, w = 2, 256, 37, 45
+    x = rng.integers(-32768, 32768, (n, c, h, w)).astype(np.int16)
+    wd = rng.integers(-32768, 32768, (c, 1, 3, 3)).astype(np.int16)
+    b = rng.integers(-32768, 32768, (c,)).astype(np.int16)
+    ufb.set_conv_max_ctas(ctas)
+    try:
+        got = ufb.conv2d(T(x, dev), T(wd, dev), T(b, dev), 1, 1, 1, 1, c)
+    finally:
+        ufb.set_conv_max_ctas(0)
+    assert np.array_equal(N(got), ora.conv2d(x, wd, b, 1, 1, c))
+    _status_clean(ufb)
+
+
 @pytest.mark.parametrize("xv,wv", [(-32768, -32768), (32767, -32768), (-32768, 32767), (-1, 4096), (3, 4096),
                                    (-3, 4096), (255, 32767), (-256, -32768)])
 def test_depthwise_extremes_and_ties(ufb, ora, dev, xv, wv):
