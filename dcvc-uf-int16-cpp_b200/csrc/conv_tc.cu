@@ -171,9 +171,13 @@ __device__ __forceinline__ void add_one_residual(const Act& res, uint32_t (&p)[8
         wh[0] = h.x, wh[1] = h.y, wh[2] = h.z, wh[3] = h.w;
     } else {
         // channel tails and views that are not 16-byte aligned: byte by byte
-        for (int j = 0; j < n_valid; ++j) {
-            wl[j >> 2] |= static_cast<uint32_t>(lo[j]) << (8 * (j & 3));
-            wh[j >> 2] |= static_cast<uint32_t>(hi[j]) << (8 * (j & 3));
+        // (unrolled, so the words stay in registers)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (j < n_valid) {
+                wl[j >> 2] |= static_cast<uint32_t>(lo[j]) << (8 * (j & 3));
+                wh[j >> 2] |= static_cast<uint32_t>(hi[j]) << (8 * (j & 3));
+            }
         }
     }
 #pragma unroll
@@ -682,9 +686,13 @@ conv_i16_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_consta
                         *reinterpret_cast<uint4*>(out.lo(opx) + oc) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
                         *reinterpret_cast<uint4*>(out.hi(opx) + oc) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
                     } else {
-                        for (int j = 0; j < n_out; ++j) {
-                            out.lo(opx)[oc + j] = static_cast<uint8_t>(lw[j >> 2] >> (8 * (j & 3)));
-                            out.hi(opx)[oc + j] = static_cast<uint8_t>(hw[j >> 2] >> (8 * (j & 3)));
+                        // channel tail (unrolled, so the words stay in registers)
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            if (j < n_out) {
+                                out.lo(opx)[oc + j] = static_cast<uint8_t>(lw[j >> 2] >> (8 * (j & 3)));
+                                out.hi(opx)[oc + j] = static_cast<uint8_t>(hw[j >> 2] >> (8 * (j & 3)));
+                            }
                         }
                     }
                 }
