@@ -1,6 +1,7 @@
 """CPU: the benchmark's multi-rank host logic on world-size-2 gloo ranks --
 stream sharding (independent streams, no data-path collective), the start
-barrier and the max / sum reductions of the per-rank timings."""
+barrier and the max / sum reductions of the per-rank timings -- and its
+per-launch roofline arithmetic."""
 import os
 import sys
 
@@ -59,3 +60,30 @@ def test_two_gloo_ranks():
     assert [g[1] for g in got] == [2.5, 2.5]   # max over ranks
     assert [g[2] for g in got] == [4.0, 4.0]   # sum over ranks
     assert got[0][3] == list(range(32)) and got[1][3] == list(range(32, 64))
+
+
+def test_launch_rooflines_take_each_launchs_slower_bound():
+    """The per-launch roofline: every convolution launch is bounded by the
+    slower of its int8 MMA time at the peak and its DRAM bytes at the copy
+    bandwidth; depthwise launches are reported against the copy bandwidth."""
+    bench = _bench()
+    peak_tops, hbm_gbs = 4000.0, 5000.0
+    table = {
+        # 1e12 int16 MACs: 8e12 int8 ops -> 2 ms at 4000 TOPS; 1 GB -> 0.2 ms: tensor-bound
+        "conv 512>512 1x1 +res @ 100": [10, 1e12, 4.0, 1e9],
+        # 1e10 MACs -> 0.02 ms; 10 GB -> 2 ms: DRAM-bound
+        "conv 256>256 1x1 +lut @ 100": [10, 1e10, 4.0, 1e10],
+        "depthwise 256 3x3 @ 100": [5, 1e9, 2.0, 5e9],
+    }
+    conv, depth = bench.launch_rooflines(table, peak_tops, hbm_gbs, step_ms=20.0)
+    assert conv["floor_ms"] == pytest.approx(4.0)
+    assert conv["measured_ms"] == pytest.approx(8.0)
+    assert conv["frac"] == pytest.approx(0.5)
+    assert conv["hbm_bound_time_share"] == pytest.approx(0.5)
+    assert depth["launches"] == 5
+    assert depth["share_of_serial_step"] == pytest.approx(0.1)
+    assert depth["achieved_gbs"] == pytest.approx(2500.0)
+    assert depth["frac"] == pytest.approx(0.5)
+    conv, depth = bench.launch_rooflines({k: v for k, v in table.items() if k.startswith("conv")},
+                                         peak_tops, hbm_gbs, step_ms=20.0)
+    assert depth is None
