@@ -817,15 +817,11 @@ void Codec::emit_frames(const std::vector<Tensor>& frames, uint32_t width, uint3
         const size_t bytes = yuv_frame * F * batch_;
         uint8_t* d = static_cast<uint8_t*>(pool_.get(bytes));
         for (int f = 0; f < F; ++f) {
-            for (int b = 0; b < batch_; ++b) {
-                Act one = frames[f].a;
-                one.base = frames[f].a.base + static_cast<long long>(b) * frames[f].a.img_px * 2 * frames[f].a.pitch;
-                one.n = 1;
-                ck(raw_frame(one, static_cast<int>(height), static_cast<int>(width),
-                             d + (static_cast<size_t>(b) * F + f) * yuv_frame, static_cast<long long>(yuv_frame), s_),
-                   "raw frame");
-                stats_.launches += 1;
-            }
+            // every stream's frame f in one launch: stream b lands at (b * F + f) * yuv_frame
+            ck(raw_frame(frames[f].a, static_cast<int>(height), static_cast<int>(width), d + f * yuv_frame,
+                         static_cast<long long>(F) * yuv_frame, s_),
+               "raw frame");
+            stats_.launches += 1;
         }
         ck(cudaMemcpyAsync(yuv_out, d, bytes, cudaMemcpyDeviceToHost, s_), "yuv download");
         sync_and_check();

@@ -4,6 +4,8 @@
 #include "engine_kernels.h"
 #include "uf_common.cuh"
 
+#include <climits>
+
 namespace ufb {
 
 namespace {
@@ -89,31 +91,116 @@ __global__ void split_to_symbols_kernel(Act in, int8_t* __restrict__ s) {
 
 // out = pixel_unshuffle(multiply(in, q), 2): out channel 4c + 2i + j of
 // pixel (y, x) = sat(rna(in[(2y + i, 2x + j), c] * q[c] / 512)); q may be null.
+// One thread per output pixel and 16 output channels (input channels c0 ..
+// c0 + 3 of the four input pixels), stored as one 16-byte word per plane
+// where the views allow; the multiplier product is the 32-bit one of
+// mul_channels_kernel (defined below).
+__device__ __forceinline__ int16_t mul_q9(int32_t v, int32_t q);
+
 __global__ void mul_unshuffle2_kernel(Act in, const int16_t* __restrict__ q, Act out) {
-    GRID_LOOP(i, in.pixels() * in.c) {
-        const int c = static_cast<int>(i % in.c);
-        int b, y, x;
-        px_of(in, i / in.c, b, y, x);
-        const long long p = in.pixel(b, y, x);
-        int16_t v = join16(in.lo(p)[c], in.hi(p)[c]);
-        if (q) v = sat16(rna_shift(static_cast<int64_t>(v) * q[c], 9));
-        const long long op = out.pixel(b, y >> 1, x >> 1);
-        const int oc = c * 4 + (y & 1) * 2 + (x & 1);
-        out.lo(op)[oc] = static_cast<uint8_t>(v & 0xff);
-        out.hi(op)[oc] = static_cast<uint8_t>((v >> 8) & 0xff);
+    const int groups = (in.c + 3) / 4;
+    GRID_LOOP(i, out.pixels() * groups) {
+        const int g = static_cast<int>(i % groups);
+        int b, oy, ox;
+        px_of(out, i / groups, b, oy, ox);
+        const int c0 = 4 * g;
+        const long long op = out.pixel(b, oy, ox);
+        uint8_t* ol = out.lo(op) + 4 * c0;
+        uint8_t* oh = out.hi(op) + 4 * c0;
+        long long ip[4];  // input pixel of sub-position ij = 2 i + j
+#pragma unroll
+        for (int ij = 0; ij < 4; ++ij) ip[ij] = in.pixel(b, 2 * oy + (ij >> 1), 2 * ox + (ij & 1));
+        uintptr_t align = reinterpret_cast<uintptr_t>(ol) | reinterpret_cast<uintptr_t>(oh);
+#pragma unroll
+        for (int ij = 0; ij < 4; ++ij)
+            align |= (reinterpret_cast<uintptr_t>(in.lo(ip[ij]) + c0) | reinterpret_cast<uintptr_t>(in.hi(ip[ij]) + c0)) &
+                     3;
+        if (c0 + 4 <= in.c && 2 * oy + 1 < in.h && 2 * ox + 1 < in.w && (align & 15) == 0) {
+            uint32_t lw[4], hw[4];
+#pragma unroll
+            for (int ij = 0; ij < 4; ++ij) {
+                lw[ij] = *reinterpret_cast<const uint32_t*>(in.lo(ip[ij]) + c0);
+                hw[ij] = *reinterpret_cast<const uint32_t*>(in.hi(ip[ij]) + c0);
+            }
+            uint32_t rl[4], rh[4];  // output word cc holds channels 4 (c0 + cc) + ij
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                rl[cc] = rh[cc] = 0;
+#pragma unroll
+                for (int ij = 0; ij < 4; ++ij) {
+                    int16_t v = static_cast<int16_t>(((lw[ij] >> (8 * cc)) & 0xffu) |
+                                                     (((hw[ij] >> (8 * cc)) & 0xffu) << 8));
+                    if (q) v = mul_q9(v, q[c0 + cc]);
+                    const uint16_t u = static_cast<uint16_t>(v);
+                    rl[cc] |= static_cast<uint32_t>(u & 0xffu) << (8 * ij);
+                    rh[cc] |= static_cast<uint32_t>(u >> 8) << (8 * ij);
+                }
+            }
+            *reinterpret_cast<uint4*>(ol) = make_uint4(rl[0], rl[1], rl[2], rl[3]);
+            *reinterpret_cast<uint4*>(oh) = make_uint4(rh[0], rh[1], rh[2], rh[3]);
+        } else {
+            for (int k = 0; k < 16; ++k) {
+                const int c = c0 + (k >> 2), ij = k & 3;
+                const int iy = 2 * oy + (ij >> 1), ix = 2 * ox + (ij & 1);
+                if (c >= in.c || iy >= in.h || ix >= in.w) continue;
+                int16_t v = join16(in.lo(ip[ij])[c], in.hi(ip[ij])[c]);
+                if (q) v = mul_q9(v, q[c]);
+                ol[k] = static_cast<uint8_t>(v & 0xff);
+                oh[k] = static_cast<uint8_t>((v >> 8) & 0xff);
+            }
+        }
     }
 }
 
-// out = sat(rna(in * q / 512)); q per channel (q_img_stride == 0) or a view.
+// sat(rna(v * q / 512)) in 32 bits (|v * q| <= 2^30).
+__device__ __forceinline__ int16_t mul_q9(int32_t v, int32_t q) {
+    const int32_t pr = v * q;
+    const int32_t sg = pr >> 31;
+    const int32_t r = (((pr ^ sg) - sg) + 256) >> 9;
+    return sat16i((r ^ sg) - sg);
+}
+
+// out = sat(rna(in * q / 512)) with one multiplier per channel; 16 channels
+// of one pixel per thread, in 16-byte words where the views allow.
 __global__ void mul_channels_kernel(Act in, const int16_t* __restrict__ q, Act out) {
-    GRID_LOOP(i, in.pixels() * in.c) {
-        const int c = static_cast<int>(i % in.c);
+    const int groups = (in.c + 15) / 16;
+    GRID_LOOP(i, in.pixels() * groups) {
+        const int g = static_cast<int>(i % groups);
         int b, y, x;
-        px_of(in, i / in.c, b, y, x);
+        px_of(in, i / groups, b, y, x);
         const long long p = in.pixel(b, y, x), op = out.pixel(b, y, x);
-        const int16_t v = sat16(rna_shift(static_cast<int64_t>(join16(in.lo(p)[c], in.hi(p)[c])) * q[c], 9));
-        out.lo(op)[c] = static_cast<uint8_t>(v & 0xff);
-        out.hi(op)[c] = static_cast<uint8_t>((v >> 8) & 0xff);
+        const int c0 = g * 16;
+        const uint8_t* il = in.lo(p) + c0;
+        const uint8_t* ih = in.hi(p) + c0;
+        uint8_t* ol = out.lo(op) + c0;
+        uint8_t* oh = out.hi(op) + c0;
+        const uintptr_t align = reinterpret_cast<uintptr_t>(il) | reinterpret_cast<uintptr_t>(ih) |
+                                reinterpret_cast<uintptr_t>(ol) | reinterpret_cast<uintptr_t>(oh);
+        if (c0 + 16 <= in.c && (align & 15) == 0) {
+            const uint4 l4 = *reinterpret_cast<const uint4*>(il), h4 = *reinterpret_cast<const uint4*>(ih);
+            const uint32_t lw[4] = {l4.x, l4.y, l4.z, l4.w}, hw[4] = {h4.x, h4.y, h4.z, h4.w};
+            uint32_t rl[4], rh[4];
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                rl[w] = rh[w] = 0;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int32_t v = static_cast<int16_t>(((lw[w] >> (8 * k)) & 0xffu) | (((hw[w] >> (8 * k)) & 0xffu) << 8));
+                    const uint16_t r = static_cast<uint16_t>(mul_q9(v, q[c0 + 4 * w + k]));
+                    rl[w] |= static_cast<uint32_t>(r & 0xffu) << (8 * k);
+                    rh[w] |= static_cast<uint32_t>(r >> 8) << (8 * k);
+                }
+            }
+            *reinterpret_cast<uint4*>(ol) = make_uint4(rl[0], rl[1], rl[2], rl[3]);
+            *reinterpret_cast<uint4*>(oh) = make_uint4(rh[0], rh[1], rh[2], rh[3]);
+        } else {
+            const int n = in.c - c0 < 16 ? in.c - c0 : 16;
+            for (int k = 0; k < n; ++k) {
+                const int16_t v = mul_q9(join16(il[k], ih[k]), q[c0 + k]);
+                ol[k] = static_cast<uint8_t>(v & 0xff);
+                oh[k] = static_cast<uint8_t>((v >> 8) & 0xff);
+            }
+        }
     }
 }
 
@@ -176,17 +263,32 @@ __device__ __forceinline__ int part_of(int c, int channels, int y, int x) {
 
 struct PriorGeom {
     int channels, h, w;   // per stream NCHW extents
-    long long elems;      // channels * h * w
+    long long elems;      // channels * h * w (below 2^31, checked by the launchers)
 };
 
-__device__ __forceinline__ bool prior_flag(const PriorGeom& g, int b, long long e, int part, const Act& scales,
-                                           int thr, int16_t& scale_out, int& c_out, int& y_out, int& x_out) {
-    const int x = static_cast<int>(e % g.w);
-    const int y = static_cast<int>((e / g.w) % g.h);
-    const int c = static_cast<int>(e / (static_cast<long long>(g.w) * g.h));
-    c_out = c;
-    y_out = y;
-    x_out = x;
+// (c, y, x) of NCHW position e of one stream (32-bit divisions), and the
+// position after (c, y, x).
+__device__ __forceinline__ void prior_pos(const PriorGeom& g, long long e, int& c, int& y, int& x) {
+    const uint32_t u = static_cast<uint32_t>(e);
+    const uint32_t t = u / static_cast<uint32_t>(g.w);
+    x = static_cast<int>(u - t * static_cast<uint32_t>(g.w));
+    const uint32_t cc = t / static_cast<uint32_t>(g.h);
+    y = static_cast<int>(t - cc * static_cast<uint32_t>(g.h));
+    c = static_cast<int>(cc);
+}
+
+__device__ __forceinline__ void prior_next(const PriorGeom& g, int& c, int& y, int& x) {
+    if (++x == g.w) {
+        x = 0;
+        if (++y == g.h) {
+            y = 0;
+            ++c;
+        }
+    }
+}
+
+__device__ __forceinline__ bool prior_flag(const PriorGeom& g, int b, int c, int y, int x, int part,
+                                           const Act& scales, int thr, int16_t& scale_out) {
     if (part_of(c, g.channels, y, x) != part) return false;
     const long long p = scales.pixel(b, y, x);
     const int16_t s = join16(scales.lo(p)[c], scales.hi(p)[c]);
@@ -234,7 +336,8 @@ __global__ void prior_count_kernel(PriorGeom g, int part, Act scales, int thr, i
         if (e >= g.elems) break;
         int16_t s;
         int c, y, x;
-        count += prior_flag(g, b, e, part, scales, thr, s, c, y, x) ? 1 : 0;
+        prior_pos(g, e, c, y, x);
+        count += prior_flag(g, b, c, y, x, part, scales, thr, s) ? 1 : 0;
     }
     __shared__ int total;
     // reduce via the scan helper
@@ -269,28 +372,35 @@ __device__ __forceinline__ void prior_visit(const PriorGeom& g, int part, const 
     // each thread takes 16 consecutive positions so per-thread ranks are local
     constexpr int kPer = kChunk / kPriorThreads;
     const long long first = base + static_cast<long long>(threadIdx.x) * kPer;
-    uint32_t mask = 0;
+    int c0 = 0, y0 = 0, x0 = 0;
+    if (first < g.elems) prior_pos(g, first, c0, y0, x0);
+    uint32_t mask = 0, parts = 0;  // active positions; positions of this part
     int16_t sc[kPer];
+    int c = c0, y = y0, x = x0;
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
         const long long e = first + k;
-        int c, y, x;
         sc[k] = 0;
-        if (e < g.elems && prior_flag(g, b, e, part, scales, thr, sc[k], c, y, x)) mask |= 1u << k;
+        if (e < g.elems && part_of(c, g.channels, y, x) == part) {
+            parts |= 1u << k;
+            const long long p = scales.pixel(b, y, x);
+            sc[k] = join16(scales.lo(p)[c], scales.hi(p)[c]);
+            if (thr == 0 || sc[k] > thr) mask |= 1u << k;
+        }
+        prior_next(g, c, y, x);
     }
     __shared__ int total;
     int rank = block_offset + block_scan(__popc(mask), &total);
+    c = c0, y = y0, x = x0;
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
         const long long e = first + k;
         if (e >= g.elems) break;
-        const int x = static_cast<int>(e % g.w);
-        const int y = static_cast<int>((e / g.w) % g.h);
-        const int c = static_cast<int>(e / (static_cast<long long>(g.w) * g.h));
-        const bool in_part = part_of(c, g.channels, y, x) == part;
+        const bool in_part = (parts >> k) & 1u;
         const bool active = (mask >> k) & 1u;
         fn(in_part, active, active ? rank : -1, c, y, x, sc[k]);
         if (active) ++rank;
+        prior_next(g, c, y, x);
     }
 }
 
@@ -361,36 +471,39 @@ __global__ void prior_encode_kernel(PriorGeom g, int part, Act scales, Act means
 
 // IntegerCodec::raw_frame (src/integer_codec.cpp:294-323) on the shuffle(8)
 // layout of a recon head output: full-resolution pixel (Y, X) of component k
-// is channel k * 64 + (Y % 8) * 8 + X % 8 of head pixel (Y / 8, X / 8).
+// is channel k * 64 + (Y % 8) * 8 + X % 8 of head pixel (Y / 8, X / 8).  The
+// grid is x over columns, y over the rows of one output image (height luma
+// rows, then height / 2 rows of U and as many of V), z over images, so no
+// thread divides; every sum fits int32 and the divisions by powers of two are
+// shifts: luma rna((v + 256) * 255 / 512), chroma floor((s + 1024) * 255 / 2048)
+// over the four samples s of a 2 x 2 block.
+static_assert(kFeatureScale == 512, "raw_frame's shifts are written for a feature scale of 512");
 __global__ void raw_frame_kernel(Act head, int height, int width, uint8_t* __restrict__ out, long long frame_bytes) {
-    const long long luma = static_cast<long long>(height) * width;
-    const int ch = height / 2, cw = width / 2;
-    const long long chroma = static_cast<long long>(ch) * cw;
-    const long long per_img = luma + 2 * chroma;
-    GRID_LOOP(i, head.n * per_img) {
-        const int b = static_cast<int>(i / per_img);
-        long long r = i - static_cast<long long>(b) * per_img;
-        uint8_t* o = out + b * frame_bytes;
-        auto sample = [&](int comp, int Y, int X) -> int32_t {
-            const long long p = head.pixel(b, Y >> 3, X >> 3);
-            const int c = comp * 64 + (Y & 7) * 8 + (X & 7);
-            return join16(head.lo(p)[c], head.hi(p)[c]);
-        };
-        if (r < luma) {
-            const int Y = static_cast<int>(r / width), X = static_cast<int>(r % width);
-            int64_t v = rna_div((static_cast<int64_t>(sample(0, Y, X)) + kFeatureScale / 2) * 255, kFeatureScale);
-            o[r] = static_cast<uint8_t>(v < 0 ? 0 : (v > 255 ? 255 : v));
-        } else {
-            r -= luma;
-            const int comp = 1 + static_cast<int>(r / chroma);
-            const long long q = r % chroma;
-            const int y = static_cast<int>(q / cw), x = static_cast<int>(q % cw);
-            const int64_t s = sample(comp, 2 * y, 2 * x) + sample(comp, 2 * y + 1, 2 * x) +
-                              sample(comp, 2 * y, 2 * x + 1) + sample(comp, 2 * y + 1, 2 * x + 1);
-            const int64_t num = (s + 2 * kFeatureScale) * 255;
-            int64_t v = num >= 0 ? num / (4 * kFeatureScale) : -((-num + 4 * kFeatureScale - 1) / (4 * kFeatureScale));
-            o[luma + r] = static_cast<uint8_t>(v < 0 ? 0 : (v > 255 ? 255 : v));
-        }
+    const int b = blockIdx.z, row = blockIdx.y;
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    uint8_t* o = out + b * frame_bytes;
+    auto sample = [&](int comp, int Y, int X) -> int32_t {
+        const long long p = head.pixel(b, Y >> 3, X >> 3);
+        const int c = comp * 64 + (Y & 7) * 8 + (X & 7);
+        return join16(head.lo(p)[c], head.hi(p)[c]);
+    };
+    if (row < height) {
+        if (x >= width) return;
+        const int32_t t = (sample(0, row, x) + 256) * 255;
+        const int32_t v = t < 0 ? -((256 - t) >> 9) : (t + 256) >> 9;
+        o[static_cast<long long>(row) * width + x] = static_cast<uint8_t>(min(max(v, 0), 255));
+    } else {
+        const int ch = height / 2, cw = width / 2;
+        if (x >= cw) return;
+        const int r = row - height;
+        const int comp = r < ch ? 1 : 2;
+        const int y = r - (comp - 1) * ch;
+        const int32_t sum = sample(comp, 2 * y, 2 * x) + sample(comp, 2 * y + 1, 2 * x) +
+                            sample(comp, 2 * y, 2 * x + 1) + sample(comp, 2 * y + 1, 2 * x + 1);
+        const int32_t v = ((sum + 1024) * 255) >> 11;
+        const long long at = static_cast<long long>(height) * width + static_cast<long long>(comp - 1) * ch * cw +
+                             static_cast<long long>(y) * cw + x;
+        o[at] = static_cast<uint8_t>(min(max(v, 0), 255));
     }
 }
 
@@ -509,12 +622,12 @@ cudaError_t split_to_symbols(const Act& in, int8_t* sym, cudaStream_t s) {
 }
 
 cudaError_t mul_unshuffle2(const Act& in, const int16_t* q, const Act& out, cudaStream_t s) {
-    mul_unshuffle2_kernel<<<grid_for(in.pixels() * in.c), kBlock, 0, s>>>(in, q, out);
+    mul_unshuffle2_kernel<<<grid_for(out.pixels() * ((in.c + 3) / 4)), kBlock, 0, s>>>(in, q, out);
     return cudaGetLastError();
 }
 
 cudaError_t mul_channels(const Act& in, const int16_t* q, const Act& out, cudaStream_t s) {
-    mul_channels_kernel<<<grid_for(in.pixels() * in.c), kBlock, 0, s>>>(in, q, out);
+    mul_channels_kernel<<<grid_for(in.pixels() * ((in.c + 15) / 16)), kBlock, 0, s>>>(in, q, out);
     return cudaGetLastError();
 }
 
@@ -536,6 +649,7 @@ int prior_blocks_per_stream(int channels, int h, int w) {
 cudaError_t prior_scan(int channels, int h, int w, int n, int part, const Act& scales, int thr, int* block_counts,
                        int* totals, cudaStream_t s) {
     PriorGeom g{channels, h, w, static_cast<long long>(channels) * h * w};
+    if (g.elems > INT_MAX) return cudaErrorInvalidValue;
     const int bps = prior_blocks_per_stream(channels, h, w);
     prior_count_kernel<<<dim3(bps, n), kPriorThreads, 0, s>>>(g, part, scales, thr, block_counts, bps);
     prior_scan_kernel<<<n, kPriorThreads, 0, s>>>(block_counts, bps, totals);
@@ -546,6 +660,7 @@ cudaError_t prior_indexes(int channels, int h, int w, int n, int part, const Act
                           const int* offsets, const uint8_t* scale_index, uint8_t* indexes, long long cap,
                           cudaStream_t s) {
     PriorGeom g{channels, h, w, static_cast<long long>(channels) * h * w};
+    if (g.elems > INT_MAX) return cudaErrorInvalidValue;
     const int bps = prior_blocks_per_stream(channels, h, w);
     prior_indexes_kernel<<<dim3(bps, n), kPriorThreads, 0, s>>>(g, part, scales, thr, offsets, bps, scale_index,
                                                                   indexes, cap);
@@ -556,6 +671,7 @@ cudaError_t prior_restore(int channels, int h, int w, int n, int part, const Act
                           const int* offsets, const int8_t* symbols, long long cap, const Act& restored,
                           cudaStream_t s) {
     PriorGeom g{channels, h, w, static_cast<long long>(channels) * h * w};
+    if (g.elems > INT_MAX) return cudaErrorInvalidValue;
     const int bps = prior_blocks_per_stream(channels, h, w);
     prior_restore_kernel<<<dim3(bps, n), kPriorThreads, 0, s>>>(g, part, scales, means, thr, offsets, bps, symbols,
                                                                   cap, restored);
@@ -566,6 +682,7 @@ cudaError_t prior_encode(int channels, int h, int w, int n, int part, const Act&
                          const Act& yenc, int thr, const int* offsets, const uint8_t* scale_index, int16_t* packed,
                          long long cap, const Act& restored, cudaStream_t s) {
     PriorGeom g{channels, h, w, static_cast<long long>(channels) * h * w};
+    if (g.elems > INT_MAX) return cudaErrorInvalidValue;
     const int bps = prior_blocks_per_stream(channels, h, w);
     prior_encode_kernel<<<dim3(bps, n), kPriorThreads, 0, s>>>(g, part, scales, means, yenc, thr, offsets, bps,
                                                                  scale_index, packed, cap, restored);
@@ -573,8 +690,11 @@ cudaError_t prior_encode(int channels, int h, int w, int n, int part, const Act&
 }
 
 cudaError_t raw_frame(const Act& head, int height, int width, uint8_t* out, long long frame_bytes, cudaStream_t s) {
-    const long long per = static_cast<long long>(height) * width * 3 / 2;
-    raw_frame_kernel<<<grid_for(head.n * per), kBlock, 0, s>>>(head, height, width, out, frame_bytes);
+    if (head.n <= 0 || height <= 0 || width <= 0) return cudaSuccess;
+    const int rows = height + 2 * (height / 2);
+    if (head.n > 65535 || rows > 65535) return cudaErrorInvalidValue;
+    const dim3 grid((width + 255) / 256, rows, head.n);
+    raw_frame_kernel<<<grid, 256, 0, s>>>(head, height, width, out, frame_bytes);
     return cudaGetLastError();
 }
 

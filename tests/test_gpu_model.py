@@ -161,7 +161,8 @@ def test_video_p_packet_parity(ufb, ora, ref, syn, models, reset, size):
 
 
 def test_batched_streams_match_single(ufb, ora, ref, syn, models):
-    """Two independent streams decoded as one batch equal two single decodes."""
+    """Two independent streams decoded as one batch equal two single decodes
+    (frames and YUV420 output)."""
     mine, _ = models["htl"]
     vid_t = syn.prepared("htl", 2)
     payloads, refs = [], []
@@ -177,13 +178,14 @@ def test_batched_streams_match_single(ufb, ora, ref, syn, models):
     batch = ufb.Codec(mine, 2)
     batch.set_skip_threshold(0.2)
     batch.add_ref_frames(np.concatenate(refs, 0))
-    got, _ = batch.decompress(payloads, W, H, 20, True)
+    got, got_yuv = batch.decompress(payloads, W, H, 20, True, yuv=True)
     for s in range(2):
         one = ufb.Codec(mine, 1)
         one.set_skip_threshold(0.2)
         one.add_ref_frames(refs[s])
-        single, _ = one.decompress([payloads[s]], W, H, 20, True)
+        single, single_yuv = one.decompress([payloads[s]], W, H, 20, True, yuv=True)
         assert np.array_equal(got[s], single[0])
+        assert np.array_equal(got_yuv[s], single_yuv[0])  # stream s's frames land at its own offsets
 
 
 def test_concurrent_codecs_match(ufb, syn, models):
