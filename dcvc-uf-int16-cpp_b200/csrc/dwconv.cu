@@ -6,7 +6,10 @@
 // Each tile's input window (18 x 10 pixels with the halo, both byte planes,
 // 45 KB) arrives by TMA into one of two shared-memory buffers while the
 // previous tile is computed from the other; the halo outside the image is the
-// TMA's zero fill, which is exactly the convolution's padding.  A thread owns
+// TMA's zero fill, which is exactly the convolution's padding.  Each warp
+// releases a buffer with one arrival on its `empty` mbarrier, and only warp 0,
+// which issues the next window load into it, waits for all eight, so the other
+// warps run on into the next tile without a CTA-wide barrier.  A thread owns
 // four channels (one 32-bit word of each plane) of two adjacent output columns
 // and slides down the tile's rows, reading each input row once from shared
 // memory (a warp reads one 128-byte pixel line).  The arithmetic stays on the

@@ -14,8 +14,9 @@ cudaError_t conv_direct(int16_t* out, const int16_t* x, const int16_t* weight, c
                         int ci, int co, int h, int w, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw,
                         int groups, cudaStream_t s);
 // Depthwise 3x3, stride 1, padding 1 on split views (dwconv.cu); a bounded
-// wait that gives up records code 9 in *status.  narrow: the layer passed
-// dw_narrow_ok, so every sum runs in one int32.
+// wait that gives up records a code in *status (9: a window load, 11: a
+// buffer release, 10: the drain of a load in flight on the way out).
+// narrow: the layer passed dw_narrow_ok, so every sum runs in one int32.
 cudaError_t dwconv3x3(const Act& in, const Act& out, const int16_t* weight, const int16_t* bias, int* status,
                       cudaStream_t s, bool narrow = false);
 // True when, for every channel c of the int16 [channels, 1, 3, 3] weights and
