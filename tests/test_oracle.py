@@ -135,3 +135,49 @@ def test_reference_codec_stream_roundtrip(ref, syn):
     digest, yuv, p = ref.codec(img_t, ii, vid_t, vi, "htl", 0.2).decode(data, 9, 2, 64, 64)
     assert p == 2 and len(yuv) == 9
     assert hashlib.sha256(b"".join(y.tobytes() for y in yuv)).hexdigest() == digest
+
+
+def _raw_frame_int32(frame, h, w):
+    """The 32-bit forms the GPU's raw_frame kernel evaluates (engine_kernels.cu):
+    luma rna((v + 256) * 255 / 512) with the divide as shifts, chroma
+    floor((s + 1024) * 255 / 2048) = ((s + 1024) * 255) >> 11 over each 2 x 2 block."""
+    f = frame.reshape(3, frame.shape[-2], frame.shape[-1]).astype(np.int32)
+    t = (f[0, :h, :w] + 256) * 255
+    planes = [np.where(t < 0, -((256 - t) >> 9), (t + 256) >> 9)]
+    ch, cw = h // 2, w // 2
+    for comp in (1, 2):
+        c = f[comp, :2 * ch, :2 * cw]
+        s = c[0::2, 0::2] + c[1::2, 0::2] + c[0::2, 1::2] + c[1::2, 1::2]
+        planes.append(((s + 1024) * 255) >> 11)
+    return np.concatenate([np.clip(p, 0, 255).astype(np.uint8).reshape(-1) for p in planes])
+
+
+@pytest.mark.parametrize("size", [(64, 64), (72, 80), (352, 626)])
+def test_raw_frame_int32_forms_vs_reference(ref, size):
+    """The GPU kernel's shift forms give the reference's IntegerCodec::raw_frame
+    bytes: every int16 value in luma, chroma blocks at both saturation ends
+    and at every rounding boundary region."""
+    h, w = size
+    rng = np.random.default_rng(h + 7 * w)
+    fh, fw = (h + 15) // 16 * 16, (w + 15) // 16 * 16
+    frame = rng.integers(-32768, 32768, (1, 3, fh, fw)).astype(np.int16)
+    n = min(65536, h * w)
+    frame[0, 0].reshape(-1)[:n] = np.arange(-32768, 32768, dtype=np.int64).astype(np.int16)[:n]
+    frame[0, 1, : fh // 2] = 32767
+    frame[0, 2, : fh // 2] = -32768
+    frame[0, 1:, fh // 2:] = rng.integers(-1300, 1300, (2, fh - fh // 2, fw))
+    assert np.array_equal(_raw_frame_int32(frame, h, w), ref.raw_frame(frame, h, w))
+
+
+def test_q9_multiply_int32_form_vs_reference(ref):
+    """sat(rna(v * q / 512)) as the GPU's multiply kernels evaluate it in 32
+    bits (|v * q| <= 2^30) equals the reference's int16::multiply over every
+    int16 v and multipliers at the extremes and around the rounding unit."""
+    q = np.array([-32768, -32767, -513, -512, -511, -1, 0, 1, 255, 256, 511, 512, 513, 1024, 32766, 32767],
+                 np.int16)
+    x = np.arange(-32768, 32768, dtype=np.int64).astype(np.int16).reshape(1, 16, 64, 64)
+    p = x.astype(np.int32) * q.astype(np.int32)[None, :, None, None]
+    sg = p >> 31
+    r = ((((p ^ sg) - sg) + 256) >> 9 ^ sg) - sg
+    mine = np.clip(r, -32768, 32767).astype(np.int16)
+    assert np.array_equal(mine, ref.multiply(x, q.reshape(1, 16, 1, 1)))
