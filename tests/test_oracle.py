@@ -181,3 +181,32 @@ def test_q9_multiply_int32_form_vs_reference(ref):
     r = ((((p ^ sg) - sg) + 256) >> 9 ^ sg) - sg
     mine = np.clip(r, -32768, 32767).astype(np.int16)
     assert np.array_equal(mine, ref.multiply(x, q.reshape(1, 16, 1, 1)))
+
+
+def test_depthwise_narrow_form_vs_reference(ref):
+    """The narrow depthwise instance's arithmetic (dwconv.cu): per channel
+    s = S + 4096 + 8192 bias in one int32 (every channel inside
+    32768 sum|w| + 4096 + 8192 |bias| <= 2^31 - 1), output
+    sat((s - [s < 4096 + 8192 bias]) >> 13), equals the reference's depthwise
+    conv; the weights sit at the bound's edge and the inputs at the extremes."""
+    rng = np.random.default_rng(5)
+    c, h, w = 24, 9, 11
+    bias = rng.integers(-32768, 32768, c).astype(np.int16)
+    room = (2**31 - 1 - 4096 - 8192 * np.abs(bias.astype(np.int64))) // 32768  # largest sum|w| per channel
+    wt = np.zeros((c, 1, 3, 3), np.int16)
+    for ch in range(c):
+        taps = rng.integers(0, 1 << 12, 9).astype(np.float64)
+        taps = np.floor(taps / taps.sum() * min(room[ch], 9 * 32767)).astype(np.int64)
+        wt[ch, 0] = (taps * rng.choice([-1, 1], 9)).reshape(3, 3).astype(np.int16)
+    wsum = np.abs(wt.astype(np.int64)).reshape(c, 9).sum(1)
+    assert (32768 * wsum + 4096 + 8192 * np.abs(bias.astype(np.int64)) <= 2**31 - 1).all()
+    x = rng.choice(np.array([-32768, 32767, -1, 0, 1, 4096, -4096], np.int16), (2, c, h, w))
+    xp = np.pad(x.astype(np.int64), ((0, 0), (0, 0), (1, 1), (1, 1)))
+    S = sum(xp[:, :, ky:ky + h, kx:kx + w] * wt[None, :, 0, ky, kx, None, None].astype(np.int64)
+            for ky in range(3) for kx in range(3))
+    s0 = (4096 + 8192 * bias.astype(np.int64))[None, :, None, None]
+    s = S + s0
+    assert (np.abs(s) <= 2**31 - 1).all()
+    s = s.astype(np.int32)
+    mine = np.clip((s - (s < s0).astype(np.int32)) >> 13, -32768, 32767).astype(np.int16)
+    assert np.array_equal(mine, ref.conv2d(x, wt, bias, 1, 1, c))
