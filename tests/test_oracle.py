@@ -210,3 +210,38 @@ def test_depthwise_narrow_form_vs_reference(ref):
     s = s.astype(np.int32)
     mine = np.clip((s - (s < s0).astype(np.int32)) >> 13, -32768, 32767).astype(np.int16)
     assert np.array_equal(mine, ref.conv2d(x, wt, bias, 1, 1, c))
+
+
+def test_narrow_recombination_form_vs_reference(ref):
+    """The tensor-core epilogue's narrow recombination (conv_tc.cu): with
+    x = xl + 256 xh (xl unsigned, xh signed bytes) and w = wl + 256 wh (signed
+    split), LL = sum xl wl, X = sum xl wh + xh wl, HH = sum xh wh and
+    P = LL + 256 X inside int32 (4096 + sum 32768 |wl| + 65280 |wh| <= 2^31 - 1),
+    rna(S / 8192) = 8 HH + ((P + 4096 + (fl >> 31)) >> 13) with
+    fl = 8 HH + (P >> 13); plus the bias and saturation this equals the
+    reference's 1x1 convolution at the bound's edge with inputs at the extremes."""
+    rng = np.random.default_rng(9)
+    ci, co, n = 512, 8, 64
+    sign = rng.choice(np.array([-1, 1]), (co, ci))
+    w = sign * 127
+    w[:, :256] += sign[:, :256] * 256  # 4096 + 512 * 127 * 32768 + 256 * 65280 just below 2^31
+    x = np.where(rng.random((n, ci)) < 0.5, 32767, -32768)
+    x[: n // 2] = np.where(sign[0] > 0, 32767, -32768)  # rows that drive channel 0 to the bound
+    x[n - 4:] = rng.integers(-32768, 32768, (4, ci))
+    b = rng.integers(-32768, 32768, co)
+    wl = ((w + 128) & 255) - 128
+    wh = (w - wl) >> 8
+    xl, xh = x & 255, x >> 8
+    LL, HH = xl @ wl.T, xh @ wh.T
+    X = xl @ wh.T + xh @ wl.T
+    assert (4096 + (32768 * np.abs(wl) + 65280 * np.abs(wh)).sum(1) <= 2**31 - 1).all()
+    P = LL + 256 * X
+    assert (np.abs(P + 4096) <= 2**31 - 1).all()
+    P = P.astype(np.int32)
+    H8 = (8 * HH).astype(np.int32)
+    fl = H8 + (P >> 13)
+    r = H8 + ((P + 4096 + (fl >> 31)) >> 13) + b[None, :]
+    mine = np.clip(r, -32768, 32767).astype(np.int16)
+    want = ref.conv2d(x.astype(np.int16).reshape(n, ci, 1, 1), w.astype(np.int16).reshape(co, ci, 1, 1),
+                      b.astype(np.int16), 1, 0)
+    assert np.array_equal(mine, want.reshape(n, co))
